@@ -1,0 +1,367 @@
+"""Benchmark of the quantized-weight hot path on B200.
+
+Default workload (one JSON line): the decode Q-GEMV sweep -- Q5_0 [4864 x 896],
+Q6_K [896 x 4864] and Q4_K [896 x 4864] at batch 1, 4 and 16 with fp32
+activations ~ N(0,1).  One step runs every (type, batch) case once over each
+of `copies` device copies of its weight, so each step streams more than three
+times the 126 MB L2 from HBM (inputs larger than L2; no flush needed).
+
+  python bench.py [--gpus N] [--steps K] [--warmup W] [--impl ours|reference]
+
+N > 1 (torchrun, one rank per GPU): every rank runs the same sweep on its own
+GPU (weak scaling, no collective in the data path); the time is the max over
+ranks and `value` sums all ranks' bytes.
+
+Metric: algorithmic GB/s = (packed weight bytes + fp32 x bytes + fp32 y bytes)
+/ time.  `e2e` runs the same sweep through the reference-facing host-buffer
+call (hd_qgemv_host: x copied in, y copied out, per call).
+"""
+from __future__ import annotations
+
+import argparse
+import json
+import os
+import subprocess
+import sys
+import threading
+import time
+
+import numpy as np
+
+ROOT = os.path.dirname(os.path.abspath(__file__))
+sys.path[:0] = [ROOT, os.path.join(ROOT, "hace-fem-hacedle_b200", "python")]
+
+from hacedle_cuda import synth as S  # noqa: E402
+
+METRIC = "Q-GEMV GB/s vs 8 TB/s HBM; prefill TFLOP/s; decode tokens/s (0.5B-shape)"
+CASES = [(S.GGML_Q5_0, 4864, 896), (S.GGML_Q6_K, 896, 4864), (S.GGML_Q4_K, 896, 4864)]
+BATCHES = [1, 4, 16]
+FALLBACK_HBM_GBS = 6650.0
+
+
+def peaks():
+    p = os.path.join(ROOT, "MEASURED_PEAKS.json")
+    if os.path.exists(p):
+        d = json.load(open(p))
+        return float(d["hbm_gbs"]), float(d["bf16_tflops"]), "measured"
+    return FALLBACK_HBM_GBS, 1590.0, "fallback"
+
+
+def case_bytes(t, N, K, B):
+    return S.nbytes(t, N, K) + 4 * B * K + 4 * B * N
+
+
+class Clocks:
+    """nvidia-smi samples during the timed region."""
+
+    def __init__(self, index: int):
+        self.index, self.proc, self.lines = index, None, []
+
+    def __enter__(self):
+        q = ("index,clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.active,"
+             "clocks_event_reasons.hw_slowdown,clocks_event_reasons.hw_thermal_slowdown,"
+             "clocks_event_reasons.sw_thermal_slowdown,clocks_event_reasons.sw_power_cap")
+        try:
+            self.proc = subprocess.Popen(["nvidia-smi", "-i", str(self.index), f"--query-gpu={q}",
+                                          "--format=csv,noheader,nounits", "-lms", "200"],
+                                         stdout=subprocess.PIPE, stderr=subprocess.DEVNULL, text=True)
+            self.t = threading.Thread(target=self._read, daemon=True)
+            self.t.start()
+        except FileNotFoundError:
+            self.proc = None
+        return self
+
+    def _read(self):
+        for line in self.proc.stdout:
+            self.lines.append(line.strip())
+
+    def __exit__(self, *a):
+        if self.proc:
+            self.proc.terminate()
+            try:
+                self.proc.wait(timeout=5)
+            except subprocess.TimeoutExpired:
+                self.proc.kill()
+
+    def summary(self):
+        sm, mx, reasons = [], None, set()
+        names = ["hw_slowdown", "hw_thermal_slowdown", "sw_thermal_slowdown", "sw_power_cap"]
+        for ln in self.lines:
+            f = [x.strip() for x in ln.split(",")]
+            if len(f) < 9:
+                continue
+            try:
+                sm.append(float(f[1]))
+                mx = float(f[2])
+            except ValueError:
+                continue
+            for n, v in zip(names, f[5:9]):
+                if v.lower() == "active":
+                    reasons.add(n)
+        return {"sm_mhz": float(np.median(sm)) if sm else None, "sm_max_mhz": mx, "reasons": sorted(reasons),
+                "samples": len(sm)}
+
+
+def dist_init():
+    if int(os.environ.get("WORLD_SIZE", "1")) > 1:
+        import datetime
+
+        import torch
+        import torch.distributed as dist
+
+        lr = int(os.environ.get("LOCAL_RANK", "0"))
+        torch.cuda.set_device(lr)
+        dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=120))
+        return dist.get_rank(), dist.get_world_size(), lr
+    return 0, 1, 0
+
+
+def max_over_ranks(v: float, world: int) -> float:
+    if world == 1:
+        return v
+    import torch
+    import torch.distributed as dist
+
+    t = torch.tensor([v], dtype=torch.float64, device="cuda")
+    dist.all_reduce(t, op=dist.ReduceOp.MAX)
+    return float(t.item())
+
+
+def barrier(world: int):
+    if world > 1:
+        import torch.distributed as dist
+
+        dist.barrier()
+
+
+# ------------------------------------------------------------------ our arm
+def run_ours(args, rank, world, local):
+    import torch
+
+    import hacedle_cuda as hc
+
+    torch.cuda.set_device(local)
+    ctx = hc.Context(local)
+    hbm, _, peak_kind = peaks()
+    l2 = torch.cuda.get_device_properties(local).L2_cache_size
+    # Weights: `copies` device copies per type, together > 3x L2 per case.
+    weights, raws = {}, {}
+    for (t, N, K) in CASES:
+        raw = S.gen_weight(t, N, K, seed=2 + t)
+        raws[t] = raw
+        nb = S.nbytes(t, N, K)
+        copies = max(args.copies, int(np.ceil(3 * l2 / nb)))
+        weights[t] = [ctx.weight(t, raw, N, K) for _ in range(copies)]
+    xs = {(t, B): torch.from_numpy(S.gen_activations(B, K, 100 + B)).cuda() for (t, N, K) in CASES for B in BATCHES}
+    ys = {(t, B): torch.empty(B, N, device="cuda") for (t, N, K) in CASES for B in BATCHES}
+
+    def segment(t, B):
+        for w in weights[t]:
+            ctx.qgemv(w, xs[(t, B)], ys[(t, B)])
+
+    # One warm pass allocates the split-K workspace; then capture each
+    # (type, batch) segment as a CUDA graph (PDL edges between launches).
+    for (t, N, K) in CASES:
+        for B in BATCHES:
+            segment(t, B)
+    torch.cuda.synchronize()
+    graphs, launches_per_step = {}, 0
+    cap_stream = torch.cuda.Stream()
+    for (t, N, K) in CASES:
+        for B in BATCHES:
+            g = torch.cuda.CUDAGraph()
+            n0 = ctx.launches
+            with torch.cuda.graph(g, stream=cap_stream):
+                ctx.set_stream(torch.cuda.current_stream().cuda_stream)
+                segment(t, B)
+            launches_per_step += ctx.launches - n0
+            graphs[(t, B)] = g
+    ctx.set_stream(torch.cuda.current_stream().cuda_stream)
+    torch.cuda.synchronize()
+
+    step_bytes = sum(case_bytes(t, N, K, B) * len(weights[t]) for (t, N, K) in CASES for B in BATCHES)
+    ev = {k: (torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)) for k in graphs}
+    case_ms = {k: 0.0 for k in graphs}
+
+    for _ in range(args.warmup):
+        for g in graphs.values():
+            g.replay()
+    torch.cuda.synchronize()
+    barrier(world)
+    with Clocks(local) as clk:
+        torch.cuda.synchronize()
+        barrier(world)
+        start, end = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        start.record()
+        for _ in range(args.steps):
+            for k, g in graphs.items():
+                ev[k][0].record()
+                g.replay()
+                ev[k][1].record()
+            torch.cuda.synchronize()
+            for k in graphs:
+                case_ms[k] += ev[k][0].elapsed_time(ev[k][1])
+        end.record()
+        torch.cuda.synchronize()
+        barrier(world)
+    total_ms = start.elapsed_time(end)
+    kernel_ms = sum(case_ms.values())
+    ms_all = max_over_ranks(kernel_ms, world)
+    value = step_bytes * args.steps * world / (ms_all * 1e-3) / 1e9
+
+    # Per-case breakdown (rank-local), and the dominant kernel's roofline:
+    # every launch in the timed region is the Q-GEMV kernel.
+    breakdown = {}
+    for (t, N, K) in CASES:
+        for B in BATCHES:
+            n = len(weights[t]) * args.steps
+            per = case_ms[(t, B)] / n
+            breakdown[f"{S.TYPE_NAME[t]}_B{B}"] = {
+                "gbs": round(case_bytes(t, N, K, B) / (per * 1e-3) / 1e9, 1), "us_per_launch": round(per * 1e3, 3)}
+    launches = launches_per_step * args.steps
+    achieved = step_bytes * args.steps / (kernel_ms * 1e-3) / 1e9
+    roofline = {"bound": "hbm", "achieved": round(achieved, 1), "peak": hbm, "unit": "GB/s",
+                "frac": round(achieved / hbm, 4), "traffic": None, "peak_kind": peak_kind,
+                "kernel": "k_qgemv", "algorithmic_bytes_per_step": step_bytes}
+    trf = os.path.join(ROOT, "profiles", "gemv_traffic.json")
+    if os.path.exists(trf):
+        roofline["traffic"] = json.load(open(trf)).get("bytes_per_launch_avg")
+
+    # End to end through the host-buffer C-ABI call.
+    e2e = None
+    if not args.no_e2e:
+        e2e = e2e_host(ctx, weights, args)
+
+    cpu = None
+    if rank == 0 and world == 1 and not args.no_cpu:
+        cpu = cpu_baseline_sample(raws, budget_s=args.cpu_seconds)
+
+    res = {
+        "metric": METRIC, "value": round(value, 1), "unit": "GB/s", "n_gpus": world, "steps": args.steps,
+        "warmup": args.warmup, "ms_per_step": round(ms_all / args.steps, 4), "higher_is_better": True,
+        "scaling": "weak", "vs_baseline": None, "dtype": "fp32-accumulate (Q5_0/Q6_K/Q4_K weights)",
+        "data": "synthetic (seeded PCG64, BASELINE generators)",
+        "config": {"workload": "decode Q-GEMV sweep: Q5_0 4864x896, Q6_K 896x4864, Q4_K 896x4864 at B=1,4,16",
+                   "copies_per_type": {S.TYPE_NAME[t]: len(weights[t]) for t in weights},
+                   "l2_policy": "inputs larger than L2 (rotating weight copies, > 3x L2 per case)",
+                   "graph": "CUDA graph per case, programmatic dependent launch"},
+        "roofline": roofline, "breakdown": breakdown, "gpu_launches": launches,
+        "e2e": e2e, "cpu_baseline": cpu, "clocks": clk.summary(),
+        "wall_ms_timed_region": round(total_ms, 3),
+    }
+    if rank == 0:
+        print(json.dumps(res), flush=True)
+    ctx.close()
+
+
+def e2e_host(ctx, weights, args):
+    """Same sweep through hd_qgemv_host with host buffers (one weight copy per
+    case is enough: x and y cross PCIe every call, weights are device-resident)."""
+    import torch
+
+    reps = 8
+    xs = {(t, B): np.ascontiguousarray(S.gen_activations(B, K, 100 + B)) for (t, N, K) in CASES for B in BATCHES}
+    for (t, N, K) in CASES:
+        for B in BATCHES:
+            ctx.qgemv_host(weights[t][0], xs[(t, B)])
+    torch.cuda.synchronize()
+    t0 = time.perf_counter()
+    byts = h2d = d2h = 0
+    for _ in range(reps):
+        for (t, N, K) in CASES:
+            for i, B in enumerate(BATCHES):
+                w = weights[t][(_ * 3 + i) % len(weights[t])]
+                ctx.qgemv_host(w, xs[(t, B)])
+                byts += case_bytes(t, N, K, B)
+                h2d += 4 * B * K
+                d2h += 4 * B * N
+    dt = time.perf_counter() - t0
+    return {"value": round(byts / dt / 1e9, 2), "unit": "GB/s", "h2d_bytes_per_step": h2d // reps,
+            "d2h_bytes_per_step": d2h // reps, "calls_per_step": len(CASES) * len(BATCHES),
+            "api": "hd_qgemv_host (host slices in/out, sync per call)"}
+
+
+def cpu_baseline_sample(raws, budget_s=10.0, threads=1):
+    """The reference's CPU path (oracle port: whole-tensor dequant + sequential
+    GEMV, as NativeBackend / block.rs do) on a bounded sample of the sweep."""
+    from oracle import oracle as O
+
+    t0 = time.perf_counter()
+    byts, n = 0, 0
+    while True:
+        for (t, N, K) in CASES:
+            for B in BATCHES:
+                X = S.gen_activations(B, K, 100 + B)
+                O.qgemv(t, raws[t], N, K, X, threads=threads)
+                byts += case_bytes(t, N, K, B)
+                n += 1
+        if time.perf_counter() - t0 > budget_s:
+            break
+    dt = time.perf_counter() - t0
+    return {"value": round(byts / dt / 1e9, 4), "unit": "GB/s", "cores": threads, "kind": "port",
+            "sample": f"{n} GEMVs ({n // 9} passes of the 9-case sweep), whole-tensor dequant per call",
+            "seconds": round(dt, 2)}
+
+
+# ------------------------------------------------------------ reference arm
+def run_reference(args, rank, world):
+    """The reference's CPU implementation of the path (the oracle port; the
+    Rust crate has no toolchain here and does not build), all host threads."""
+    if rank != 0:
+        return
+    threads = os.cpu_count() or 1
+    raws = {t: S.gen_weight(t, N, K, seed=2 + t) for (t, N, K) in CASES}
+    from oracle import oracle as O
+
+    O.lib()
+    for _ in range(max(1, args.warmup)):
+        for (t, N, K) in CASES:
+            O.qgemv(t, raws[t], N, K, S.gen_activations(1, K, 101), threads=threads)
+    byts, t_total = 0, 0.0
+    for _ in range(args.steps):
+        t0 = time.perf_counter()
+        for (t, N, K) in CASES:
+            for B in BATCHES:
+                O.qgemv(t, raws[t], N, K, S.gen_activations(B, K, 100 + B), threads=threads)
+                byts += case_bytes(t, N, K, B)
+        t_total += time.perf_counter() - t0
+    value = byts / t_total / 1e9
+    res = {"metric": METRIC, "value": round(value, 4), "unit": "GB/s", "n_gpus": world, "steps": args.steps,
+           "warmup": args.warmup, "ms_per_step": round(t_total / args.steps * 1e3, 3), "higher_is_better": True,
+           "scaling": "weak", "vs_baseline": None, "dtype": "fp32", "data": "synthetic (seeded PCG64)",
+           "config": {"workload": "decode Q-GEMV sweep: Q5_0 4864x896, Q6_K 896x4864, Q4_K 896x4864 at B=1,4,16"},
+           "impl": "reference",
+           "cpu_baseline": {"value": round(value, 4), "unit": "GB/s", "cores": threads, "kind": "port",
+                            "sample": "one pass of the 9-case sweep per step (whole-tensor dequant per call)"},
+           "e2e": {"value": round(value, 4), "unit": "GB/s", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0}}
+    print(json.dumps(res), flush=True)
+
+
+def main():
+    ap = argparse.ArgumentParser()
+    ap.add_argument("--gpus", type=int, default=1)
+    ap.add_argument("--steps", type=int, default=20)
+    ap.add_argument("--warmup", type=int, default=3)
+    ap.add_argument("--impl", default="ours", choices=["ours", "reference"])
+    ap.add_argument("--copies", type=int, default=8)
+    ap.add_argument("--cpu-seconds", type=float, default=10.0)
+    ap.add_argument("--no-cpu", action="store_true")
+    ap.add_argument("--no-e2e", action="store_true")
+    args = ap.parse_args()
+    args.warmup = max(args.warmup, 3) if args.impl == "ours" else args.warmup
+    if args.impl == "reference":
+        rank = int(os.environ.get("RANK", "0"))
+        run_reference(args, rank, int(os.environ.get("WORLD_SIZE", "1")))
+        return
+    rank, world, local = dist_init()
+    try:
+        run_ours(args, rank, world, local)
+    finally:
+        if world > 1:
+            import torch.distributed as dist
+
+            dist.destroy_process_group()
+
+
+if __name__ == "__main__":
+    main()

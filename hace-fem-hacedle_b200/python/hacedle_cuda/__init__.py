@@ -1,0 +1,254 @@
+"""Python binding of libhacedle_cuda.so (ctypes over the C ABI in include/hacedle_cuda.h).
+
+Device buffers are torch tensors; their data pointers cross the C ABI as
+plain addresses.  There is no CPU fallback: every call goes to the CUDA
+library, and loading fails loudly when the library is missing.
+"""
+from __future__ import annotations
+
+import ctypes as C
+import os
+
+import numpy as np
+
+from . import synth  # noqa: F401
+
+_PKG = os.path.dirname(os.path.abspath(__file__))
+ROOT = os.path.abspath(os.path.join(_PKG, "..", ".."))
+LIB_PATH = os.path.join(ROOT, "lib", "libhacedle_cuda.so")
+
+HD_OK, HD_E_ARG, HD_E_SHAPE, HD_E_TYPE, HD_E_CUDA, HD_E_TIMEOUT, HD_E_NCCL, HD_E_OOM, HD_E_UNSUPPORTED = range(9)
+TYPE_Q5_0, TYPE_Q8_0, TYPE_Q4_K, TYPE_Q6_K = 6, 8, 12, 14
+PREC_FP32, PREC_BF16_TC = 0, 1
+
+# Every symbol include/hacedle_cuda.h declares.
+EXPORTS = [
+    "hd_ctx_create", "hd_ctx_destroy", "hd_ctx_set_stream", "hd_ctx_synchronize", "hd_ctx_reserve_workspace",
+    "hd_last_error", "hd_ctx_launch_count", "hd_version",
+    "hd_weight_upload", "hd_weight_upload_device", "hd_weight_free", "hd_weight_info", "hd_weight_download",
+    "hd_dequantize", "hd_qgemv", "hd_qgemv_swiglu", "hd_qgemv_host", "hd_qgemm", "hd_qgemm_host", "hd_matmul_f32",
+    "hd_rmsnorm", "hd_rmsnorm_graph", "hd_rope_neox", "hd_rope_interleaved", "hd_softmax_rows", "hd_swiglu",
+    "hd_add", "hd_argmax_rows", "hd_embed", "hd_kv_append", "hd_attention_decode", "hd_attention_prefill",
+    "hd_dot_i8", "hd_fused_qdot_qadd_qacc_i8", "hd_decoder_create", "hd_decoder_free", "hd_decoder_generate",
+]
+
+
+class HdError(RuntimeError):
+    def __init__(self, code: int, msg: str):
+        super().__init__(f"hacedle_cuda error {code}: {msg}")
+        self.code = code
+
+
+_lib = None
+V, I, I64, SZ, F = C.c_void_p, C.c_int, C.c_int64, C.c_size_t, C.c_float
+
+
+def lib() -> C.CDLL:
+    """Load the in-tree library (built by `make -C hace-fem-hacedle_b200`)."""
+    global _lib
+    if _lib is not None:
+        return _lib
+    if not os.path.exists(LIB_PATH):
+        raise RuntimeError(f"libhacedle_cuda.so is missing at {LIB_PATH}; run __graft_entry__.build()")
+    L = C.CDLL(LIB_PATH)
+    sig = {
+        "hd_ctx_create": [I, C.POINTER(V)], "hd_ctx_destroy": [V], "hd_ctx_set_stream": [V, V],
+        "hd_ctx_synchronize": [V], "hd_ctx_reserve_workspace": [V, SZ], "hd_last_error": [V],
+        "hd_ctx_launch_count": [V], "hd_version": [],
+        "hd_weight_upload": [V, V, SZ, I, I64, I64, C.POINTER(V)],
+        "hd_weight_upload_device": [V, V, SZ, I, I64, I64, C.POINTER(V)],
+        "hd_weight_free": [V, V],
+        "hd_weight_info": [V, C.POINTER(I), C.POINTER(I64), C.POINTER(I64), C.POINTER(SZ)],
+        "hd_weight_download": [V, V, V, SZ], "hd_dequantize": [V, V, V, SZ],
+        "hd_qgemv": [V, V, V, V, I, V, V], "hd_qgemv_swiglu": [V, V, V, V, V, I], "hd_qgemv_host": [V, V, V, V, I],
+        "hd_qgemm": [V, V, V, V, I, I], "hd_qgemm_host": [V, V, V, V, I, I], "hd_matmul_f32": [V, V, V, V, I64, I64, I64],
+        "hd_rmsnorm": [V, V, V, V, V, I64, I, F], "hd_rmsnorm_graph": [V, V, V, V, I64, I, F],
+        "hd_rope_neox": [V, V, V, I, I, I, F], "hd_rope_interleaved": [V, V, V, V, V, I64, I],
+        "hd_softmax_rows": [V, V, I64, I], "hd_swiglu": [V, V, V, V, I64], "hd_add": [V, V, V, V, I64],
+        "hd_argmax_rows": [V, V, I64, I64, V], "hd_embed": [V, V, V, I, V],
+        "hd_kv_append": [V, V, V, V, V, V, I, I, I, I, I],
+        "hd_attention_decode": [V, V, V, V, V, I, I, I, I, I, V],
+        "hd_attention_prefill": [V, V, V, V, I, I, I, I, I, I, V],
+        "hd_dot_i8": [V, V, V, I64, I, V], "hd_fused_qdot_qadd_qacc_i8": [V, V, V, I64, I, V, V, V],
+        "hd_decoder_create": [V, V, V, V, V, C.POINTER(V)], "hd_decoder_free": [V],
+        "hd_decoder_generate": [V, V, I, I, I, I, V, V, V],
+    }
+    for name, args in sig.items():
+        fn = getattr(L, name)
+        fn.argtypes = args
+        fn.restype = I
+    L.hd_last_error.restype = C.c_char_p
+    L.hd_version.restype = C.c_char_p
+    L.hd_ctx_launch_count.restype = C.c_uint64
+    _lib = L
+    return L
+
+
+def _ptr(t) -> int | None:
+    if t is None:
+        return None
+    if isinstance(t, np.ndarray):
+        return t.ctypes.data
+    return t.data_ptr()
+
+
+class Weight:
+    """Device weight handle (hd_weight): GGUF bytes uploaded once."""
+
+    def __init__(self, ctx: "Context", ggml_type: int, raw: np.ndarray, rows: int, cols: int):
+        raw = np.ascontiguousarray(raw, dtype=np.uint8).reshape(-1)
+        self.ctx, self.type, self.rows, self.cols, self.nbytes = ctx, ggml_type, rows, cols, raw.size
+        h = V()
+        ctx._check(lib().hd_weight_upload(ctx.h, raw.ctypes.data, raw.size, ggml_type, rows, cols, C.byref(h)))
+        self.h = h
+
+    def download(self) -> np.ndarray:
+        out = np.zeros(self.nbytes, np.uint8)
+        self.ctx._check(lib().hd_weight_download(self.ctx.h, self.h, out.ctypes.data, out.size))
+        return out
+
+    def free(self):
+        if self.h:
+            lib().hd_weight_free(self.ctx.h, self.h)
+            self.h = None
+
+    def __del__(self):
+        try:
+            self.free()
+        except Exception:
+            pass
+
+
+class Context:
+    """One hd_ctx on `device`; work goes on torch's current stream."""
+
+    def __init__(self, device: int = 0, use_torch_stream: bool = True):
+        import torch
+
+        h = V()
+        rc = lib().hd_ctx_create(device, C.byref(h))
+        if rc != HD_OK:
+            raise HdError(rc, f"hd_ctx_create({device}) failed")
+        self.h = h
+        self.device = device
+        if use_torch_stream:
+            self.set_stream(torch.cuda.current_stream(device).cuda_stream)
+
+    def set_stream(self, stream: int | None):
+        self._check(lib().hd_ctx_set_stream(self.h, stream))
+
+    def _check(self, rc: int):
+        if rc != HD_OK:
+            raise HdError(rc, lib().hd_last_error(self.h).decode())
+
+    def last_error(self) -> str:
+        return lib().hd_last_error(self.h).decode()
+
+    @property
+    def launches(self) -> int:
+        return int(lib().hd_ctx_launch_count(self.h))
+
+    def synchronize(self):
+        self._check(lib().hd_ctx_synchronize(self.h))
+
+    def reserve_workspace(self, nbytes: int):
+        self._check(lib().hd_ctx_reserve_workspace(self.h, nbytes))
+
+    def weight(self, ggml_type: int, raw, rows: int, cols: int) -> Weight:
+        return Weight(self, ggml_type, raw, rows, cols)
+
+    # ---- kernels (device tensors) ----
+    def dequantize(self, w: Weight, out):
+        self._check(lib().hd_dequantize(self.h, w.h, _ptr(out), out.numel()))
+
+    def qgemv(self, w: Weight, x, y, bias=None, residual=None):
+        B = x.shape[0] if x.dim() == 2 else 1
+        self._check(lib().hd_qgemv(self.h, w.h, _ptr(x), _ptr(y), B, _ptr(bias), _ptr(residual)))
+
+    def qgemv_swiglu(self, wg: Weight, wu: Weight, x, y):
+        B = x.shape[0] if x.dim() == 2 else 1
+        self._check(lib().hd_qgemv_swiglu(self.h, wg.h, wu.h, _ptr(x), _ptr(y), B))
+
+    def qgemv_host(self, w: Weight, x: np.ndarray) -> np.ndarray:
+        x = np.ascontiguousarray(x, np.float32).reshape(-1, w.cols)
+        y = np.zeros((x.shape[0], w.rows), np.float32)
+        self._check(lib().hd_qgemv_host(self.h, w.h, x.ctypes.data, y.ctypes.data, x.shape[0]))
+        return y
+
+    def qgemm(self, w: Weight, X, Y, precision: int = PREC_FP32):
+        self._check(lib().hd_qgemm(self.h, w.h, _ptr(X), _ptr(Y), X.shape[0], precision))
+
+    def qgemm_host(self, w: Weight, X: np.ndarray, precision: int = PREC_FP32) -> np.ndarray:
+        X = np.ascontiguousarray(X, np.float32).reshape(-1, w.cols)
+        Y = np.zeros((X.shape[0], w.rows), np.float32)
+        self._check(lib().hd_qgemm_host(self.h, w.h, X.ctypes.data, Y.ctypes.data, X.shape[0], precision))
+        return Y
+
+    def matmul_f32(self, a, b, out):
+        self._check(lib().hd_matmul_f32(self.h, _ptr(a), _ptr(b), _ptr(out), a.shape[0], b.shape[1], a.shape[1]))
+
+    def rmsnorm(self, x, w, y, eps: float = 1e-6, residual=None):
+        dim = w.numel()
+        self._check(lib().hd_rmsnorm(self.h, _ptr(x), _ptr(w), _ptr(residual), _ptr(y), x.numel() // dim, dim, eps))
+
+    def rmsnorm_graph(self, x, w, y, eps: float = 1e-5):
+        dim = w.numel()
+        self._check(lib().hd_rmsnorm_graph(self.h, _ptr(x), _ptr(w), _ptr(y), x.numel() // dim, dim, eps))
+
+    def rope_neox(self, x, pos, heads: int, head_dim: int, theta: float = 1e6):
+        self._check(lib().hd_rope_neox(self.h, _ptr(x), _ptr(pos), pos.numel(), heads, head_dim, theta))
+
+    def rope_interleaved(self, x, cos, sin, out):
+        last = x.shape[-1]
+        self._check(lib().hd_rope_interleaved(self.h, _ptr(x), _ptr(cos), _ptr(sin), _ptr(out), x.numel() // last,
+                                              last))
+
+    def softmax_rows(self, x):
+        n = x.shape[-1]
+        self._check(lib().hd_softmax_rows(self.h, _ptr(x), x.numel() // n, n))
+
+    def swiglu(self, g, u, y):
+        self._check(lib().hd_swiglu(self.h, _ptr(g), _ptr(u), _ptr(y), g.numel()))
+
+    def add(self, a, b, y):
+        self._check(lib().hd_add(self.h, _ptr(a), _ptr(b), _ptr(y), a.numel()))
+
+    def argmax_rows(self, x, idx):
+        n = x.shape[-1]
+        rows = x.numel() // n if n else idx.numel()
+        self._check(lib().hd_argmax_rows(self.h, _ptr(x), rows, n, _ptr(idx)))
+
+    def embed(self, table: Weight, ids, out):
+        self._check(lib().hd_embed(self.h, table.h, _ptr(ids), ids.numel(), _ptr(out)))
+
+    def kv_append(self, k, v, kc, vc, pos0, seqs, tokens, n_kv, head_dim, max_ctx):
+        self._check(lib().hd_kv_append(self.h, _ptr(k), _ptr(v), _ptr(kc), _ptr(vc), _ptr(pos0), seqs, tokens, n_kv,
+                                       head_dim, max_ctx))
+
+    def attention_decode(self, q, kc, vc, lens, n_heads, n_kv, head_dim, max_ctx, out):
+        self._check(lib().hd_attention_decode(self.h, _ptr(q), _ptr(kc), _ptr(vc), _ptr(lens), lens.numel(), n_heads,
+                                              n_kv, head_dim, max_ctx, _ptr(out)))
+
+    def attention_prefill(self, q, kc, vc, T, pos0, n_heads, n_kv, head_dim, max_ctx, out):
+        self._check(lib().hd_attention_prefill(self.h, _ptr(q), _ptr(kc), _ptr(vc), T, pos0, n_heads, n_kv, head_dim,
+                                               max_ctx, _ptr(out)))
+
+    def dot_i8(self, a, b, out):
+        n = a.shape[-1]
+        self._check(lib().hd_dot_i8(self.h, _ptr(a), _ptr(b), n, a.numel() // n if n else out.numel(), _ptr(out)))
+
+    def fused_qdot_qadd_qacc_i8(self, a, b, bias, carry, out):
+        n = a.shape[-1]
+        self._check(lib().hd_fused_qdot_qadd_qacc_i8(self.h, _ptr(a), _ptr(b), n, out.numel(), _ptr(bias),
+                                                     _ptr(carry), _ptr(out)))
+
+    def close(self):
+        if getattr(self, "h", None):
+            lib().hd_ctx_destroy(self.h)
+            self.h = None
+
+    def __del__(self):
+        try:
+            self.close()
+        except Exception:
+            pass

@@ -1,0 +1,225 @@
+/*
+ * hacedle_cuda.h -- C ABI of libhacedle_cuda.so, the B200 (sm_100a) kernels for
+ * the quantized-weight hot path of the hacedle crate: GGUF block dequantization
+ * (Q8_0, Q5_0, Q4_K, Q6_K) fused into GEMV / GEMM, plus the RMSNorm, RoPE,
+ * GQA attention, SwiGLU and argmax kernels of a Qwen2-shaped decoder.
+ *
+ * Conventions
+ *  - Every function returns an hd_status (0 = HD_OK).  hd_last_error() gives
+ *    the message of the last failure on that context.  No C++ exception
+ *    crosses this boundary.
+ *  - Pointers named *_dev are device memory; *_host are host memory.  Sizes are
+ *    element counts unless named *bytes.
+ *  - A weight [rows x cols] is `rows` output rows of `cols` inputs, row-major
+ *    with cols contiguous, exactly as a GGUF tensor stores it
+ *    (QuantTensorView{data, shape=[rows, cols]}, src/quant_view/q4k_tensor_view.rs:46-61).
+ *  - Work is enqueued on the context's stream (hd_ctx_set_stream; default: a
+ *    stream the context creates).  Functions taking only device pointers are
+ *    asynchronous; *_host functions synchronize before returning.
+ *  - One context per host thread; a context is not safe for concurrent use.
+ *  - Type ids are ggml's (gguf 0.19.0 GGMLQuantizationType).  The reference's
+ *    QuantType discriminants (q4k_tensor_view.rs:9-19) are not ggml ids; a Rust
+ *    binding maps enum variants, not their integer values (HD_TYPE_*).
+ */
+#ifndef HACEDLE_CUDA_H
+#define HACEDLE_CUDA_H
+
+#include <stddef.h>
+#include <stdint.h>
+
+#ifdef __cplusplus
+extern "C" {
+#endif
+
+typedef enum {
+    HD_OK = 0,
+    HD_E_ARG = 1,          /* null pointer or bad argument value          */
+    HD_E_SHAPE = 2,        /* MatMulError::ShapeMismatch and kin           */
+    HD_E_TYPE = 3,         /* quant type not carried by this library       */
+    HD_E_CUDA = 4,         /* a CUDA runtime call failed                   */
+    HD_E_TIMEOUT = 5,      /* a bounded device-side wait ran out           */
+    HD_E_NCCL = 6,         /* a collective failed                          */
+    HD_E_OOM = 7,          /* device allocation failed                     */
+    HD_E_UNSUPPORTED = 8   /* valid request this build does not implement */
+} hd_status;
+
+enum {
+    HD_TYPE_F32 = 0, HD_TYPE_F16 = 1, HD_TYPE_Q5_0 = 6, HD_TYPE_Q8_0 = 8,
+    HD_TYPE_Q4_K = 12, HD_TYPE_Q6_K = 14
+};
+
+/* GEMM arithmetic: fp32 CUDA-core accumulate (1e-5 relative contract) or
+ * bf16 operands on the tcgen05 tensor cores with fp32 accumulation in TMEM
+ * (2e-2 relative contract). */
+enum { HD_PREC_FP32 = 0, HD_PREC_BF16_TC = 1 };
+
+typedef struct hd_ctx hd_ctx;
+typedef struct hd_weight hd_weight;
+typedef struct hd_decoder hd_decoder;
+
+/* ---------------------------------------------------------------- context */
+/* New context on CUDA device `device`. */
+int hd_ctx_create(int device, hd_ctx **out);
+int hd_ctx_destroy(hd_ctx *ctx);
+/* Enqueue subsequent work on `stream` (a cudaStream_t); NULL restores the
+ * context's own stream. */
+int hd_ctx_set_stream(hd_ctx *ctx, void *stream);
+int hd_ctx_synchronize(hd_ctx *ctx);
+/* Make sure the context's split-K workspace holds at least `bytes`, so that
+ * later calls allocate nothing (needed before stream capture). */
+int hd_ctx_reserve_workspace(hd_ctx *ctx, size_t bytes);
+/* Message of the last failure on this context ("" if none). */
+const char *hd_last_error(const hd_ctx *ctx);
+/* Number of kernels this context has launched (for launch accounting). */
+uint64_t hd_ctx_launch_count(const hd_ctx *ctx);
+const char *hd_version(void);
+
+/* ---------------------------------------------------------------- weights */
+/* Replaces QuantTensorView::new + its per-call clone (q4k_tensor_view.rs:46-56,
+ * core/ops/block.rs:75-89): copies `nbytes` of GGUF blocks once to the device
+ * and re-lays them out for the kernels (a lossless permutation of the same
+ * bytes).  `cols` must be a multiple of the type's block (32 or 256) and
+ * nbytes must equal QuantTensorView::size_bytes (:58-62). */
+int hd_weight_upload(hd_ctx *ctx, const uint8_t *gguf_host, size_t nbytes, int ggml_type,
+                     int64_t rows, int64_t cols, hd_weight **out);
+/* Same, from GGUF bytes already in device memory. */
+int hd_weight_upload_device(hd_ctx *ctx, const uint8_t *gguf_dev, size_t nbytes, int ggml_type,
+                            int64_t rows, int64_t cols, hd_weight **out);
+int hd_weight_free(hd_ctx *ctx, hd_weight *w);
+int hd_weight_info(const hd_weight *w, int *ggml_type, int64_t *rows, int64_t *cols,
+                   size_t *gguf_bytes);
+/* Writes the weight back in GGUF block layout (round trip of the upload). */
+int hd_weight_download(hd_ctx *ctx, const hd_weight *w, uint8_t *gguf_host, size_t nbytes);
+
+/* -------------------------------------------------------------- dequant */
+/* QuantTensorView::dequantize (q4k_tensor_view.rs:63-114): the full f32
+ * tensor, bit-exact with IEEE f16 scales.  out_dev holds rows*cols floats. */
+int hd_dequantize(hd_ctx *ctx, const hd_weight *w, float *out_dev, size_t n);
+
+/* ----------------------------------------------------------------- GEMV */
+/* Decode Q-GEMV, y[b][i] = sum_k W[i][k] x[b][k] (+ bias[i]) (+ residual[b][i])
+ * for b < B <= 16.  Replaces matmul_vec_matrix (core/tensor_ops/matmul.rs:4-21),
+ * the projection loops of BrainBlock::forward (core/ops/block.rs:104-128,
+ * 210-231) and LMHead::forward (src/x/provider/candle/lmhead.rs:22-38).
+ * x_dev [B][cols], y_dev [B][rows]; bias_dev [rows] or NULL; residual_dev
+ * [B][rows] or NULL (may alias y_dev).  fp32 accumulate. */
+int hd_qgemv(hd_ctx *ctx, const hd_weight *w, const float *x_dev, float *y_dev, int B,
+             const float *bias_dev, const float *residual_dev);
+/* Gate/up pair with the SwiGLU epilogue: y[b][i] = silu(G x)_i * (U x)_i
+ * (src/ops/silu.rs:5-13 applied as Qwen2's silu(gate)*up). */
+int hd_qgemv_swiglu(hd_ctx *ctx, const hd_weight *w_gate, const hd_weight *w_up,
+                    const float *x_dev, float *y_dev, int B);
+/* The reference operator with host slices in and out (matmul_vec_matrix's
+ * &[f32] -> Vec<f32> contract): copies x in, runs hd_qgemv, copies y out. */
+int hd_qgemv_host(hd_ctx *ctx, const hd_weight *w, const float *x_host, float *y_host, int B);
+
+/* ----------------------------------------------------------------- GEMM */
+/* Prefill Q-GEMM, Y[t][i] = sum_k W[i][k] X[t][k] for t < T.  Replaces
+ * ComputeBackend::matmul_q4k/q6k (src/quant_view/dequant_dispatcher.rs:10-48,
+ * routed by DequantDispatcher::dispatch_matmul :148-154) and matmul_f32 of a
+ * quantized operand.  precision: HD_PREC_FP32 or HD_PREC_BF16_TC. */
+int hd_qgemm(hd_ctx *ctx, const hd_weight *w, const float *X_dev, float *Y_dev, int T,
+             int precision);
+int hd_qgemm_host(hd_ctx *ctx, const hd_weight *w, const float *X_host, float *Y_host, int T,
+                  int precision);
+/* Dense f32 GEMM, out[m][n] = sum_k a[m][k] b[k][n] (core/ops/matmul.rs:16-51,
+ * ComputeBackend::matmul_f32 dequant_dispatcher.rs:72-83). */
+int hd_matmul_f32(hd_ctx *ctx, const float *a_dev, const float *b_dev, float *out_dev, int64_t m,
+                  int64_t n, int64_t k);
+
+/* ------------------------------------------------ elementwise / reduction */
+/* RMSNorm per row (dequant_dispatcher.rs:85-93, core/tensor_ops/rms_norm.rs:4-13):
+ * y = x * w * (1/sqrt(mean(x^2) + eps)).  If residual_dev is not NULL it is
+ * added to x first and the sum is written back to residual_dev (fused
+ * residual add).  x_dev/y_dev [rows][dim]. */
+int hd_rmsnorm(hd_ctx *ctx, const float *x_dev, const float *w_dev, float *residual_dev,
+               float *y_dev, int64_t rows, int dim, float eps);
+/* rmsnorm_f32 of the graph executor (core/ops/rmsnorm.rs:16-61): v*inv*w. */
+int hd_rmsnorm_graph(hd_ctx *ctx, const float *x_dev, const float *w_dev, float *y_dev,
+                     int64_t rows, int dim, float eps);
+/* Per-head NEOX RoPE in place (apply_rope_pairwise, src/ops/rope.rs:5-31):
+ * x_dev [tokens][heads][head_dim]; pos_dev [tokens]. */
+int hd_rope_neox(hd_ctx *ctx, float *x_dev, const int32_t *pos_dev, int tokens, int heads,
+                 int head_dim, float theta);
+/* Interleaved-pair RoPE from cos/sin tables (rope_f32, core/ops/rope.rs:16-64). */
+int hd_rope_interleaved(hd_ctx *ctx, const float *x_dev, const float *cos_dev,
+                        const float *sin_dev, float *out_dev, int64_t rows, int last_dim);
+/* Row softmax in place (NativeBackend::softmax, dequant_dispatcher.rs:117-128). */
+int hd_softmax_rows(hd_ctx *ctx, float *x_dev, int64_t rows, int n);
+/* out = silu(g) * u (n elements). */
+int hd_swiglu(hd_ctx *ctx, const float *g_dev, const float *u_dev, float *out_dev, int64_t n);
+/* out = a + b (add_f32, core/ops/add.rs:16-43). */
+int hd_add(hd_ctx *ctx, const float *a_dev, const float *b_dev, float *out_dev, int64_t n);
+/* First index of each row's maximum, strict > (ArgMaxSampler::sample,
+ * runtime/sampler/argmax.rs:8-24); 0 for n == 0. */
+int hd_argmax_rows(hd_ctx *ctx, const float *x_dev, int64_t rows, int64_t n, int32_t *idx_dev);
+/* Embedding rows dequantized from a quantized table (embedding_lookup,
+ * core/tensor_ops/embedding.rs:4-17): ids outside [0, rows) give zeros.
+ * out_dev [n][cols]. */
+int hd_embed(hd_ctx *ctx, const hd_weight *table, const int32_t *ids_dev, int n, float *out_dev);
+
+/* ------------------------------------------------------- KV and attention */
+/* Device KV cache (KvCache::append, core/ops/block.rs:268-282, KvArena
+ * runtime/kv_cache.rs:8-34): caches are [seq][max_ctx][n_kv][head_dim] f32;
+ * k/v_dev [seq][tokens][n_kv][head_dim] written at positions pos0[s] + t. */
+int hd_kv_append(hd_ctx *ctx, const float *k_dev, const float *v_dev, float *kcache_dev,
+                 float *vcache_dev, const int32_t *pos0_dev, int seqs, int tokens, int n_kv,
+                 int head_dim, int max_ctx);
+/* GQA decode attention, one query token per sequence (block.rs:138-173 with
+ * kv head = h / (n_heads/n_kv)): q_dev [seq][n_heads][hd], attends to cache
+ * positions [0, len[s]); out_dev [seq][n_heads][hd]. */
+int hd_attention_decode(hd_ctx *ctx, const float *q_dev, const float *kcache_dev,
+                        const float *vcache_dev, const int32_t *len_dev, int seqs, int n_heads,
+                        int n_kv, int head_dim, int max_ctx, float *out_dev);
+/* Causal prefill attention for one sequence: q_dev [T][n_heads][hd] at
+ * positions pos0..pos0+T-1 attends to cache positions [0, pos0+t]. */
+int hd_attention_prefill(hd_ctx *ctx, const float *q_dev, const float *kcache_dev,
+                         const float *vcache_dev, int T, int pos0, int n_heads, int n_kv,
+                         int head_dim, int max_ctx, float *out_dev);
+
+/* ------------------------------------------------------------ integer ops */
+/* exec_q_dot / dot_batch (ops/q_ops.rs:11-13, ops/batch.rs:3-29): wrapping
+ * i32 dot of two i8 vectors, for `count` independent pairs of length n
+ * (a_dev, b_dev [count][n]); out_dev [count]. */
+int hd_dot_i8(hd_ctx *ctx, const int8_t *a_dev, const int8_t *b_dev, int64_t n, int count,
+              int32_t *out_dev);
+/* fused_qdot_qadd_qacc_i8 (ops/fused.rs:52-57) for `count` independent
+ * streams: out = dot + bias + carry (wrapping), carry = out. */
+int hd_fused_qdot_qadd_qacc_i8(hd_ctx *ctx, const int8_t *a_dev, const int8_t *b_dev, int64_t n,
+                               int count, const int32_t *bias_dev, int32_t *carry_dev,
+                               int32_t *out_dev);
+
+/* ---------------------------------------------------------------- decoder */
+/* Qwen2-shaped decoder run natively on the device: BrainBlock::forward
+ * (core/ops/block.rs:51-238, corrected: RoPE on all heads, GQA h/(nh/nkv),
+ * o_proj applied, silu(gate)*up, q/k/v biases) for every layer, then the
+ * final RMSNorm, the tied LM head and greedy argmax (runtime/sampler/argmax.rs). */
+typedef struct {
+    int hidden, n_layers, n_heads, n_kv, head_dim, ffn, vocab;
+    int max_ctx;    /* positions per sequence in the KV cache */
+    int max_seqs;   /* sequences decoded together (1..256)     */
+    float eps, theta;
+} hd_decoder_config;
+
+typedef struct {
+    const hd_weight *wq, *wk, *wv, *wo, *wg, *wu, *wd;
+    /* host f32 vectors, copied at create time */
+    const float *bq, *bk, *bv, *attn_norm, *ffn_norm;
+} hd_layer_weights;
+
+int hd_decoder_create(hd_ctx *ctx, const hd_decoder_config *cfg, const hd_layer_weights *layers,
+                      const float *out_norm_host, const hd_weight *embed, hd_decoder **out);
+int hd_decoder_free(hd_decoder *dec);
+/* Prefill `n_prompt` ids of each of `seqs` sequences (prompts_host
+ * [seqs][n_prompt]) and greedy-decode n_gen ids each (out_host [seqs][n_gen]).
+ * prefill_precision: HD_PREC_FP32 or HD_PREC_BF16_TC.  Decode steps replay a
+ * captured CUDA graph.  If step_ms_out is not NULL it receives the device time
+ * of the decode loop in milliseconds. */
+int hd_decoder_generate(hd_decoder *dec, const int32_t *prompts_host, int seqs, int n_prompt,
+                        int n_gen, int prefill_precision, int32_t *out_host, float *decode_ms_out,
+                        float *prefill_ms_out);
+
+#ifdef __cplusplus
+}
+#endif
+#endif /* HACEDLE_CUDA_H */

@@ -1,0 +1,184 @@
+"""CUDA dequant and decode Q-GEMV against the oracle (B200).
+
+Dequantized weights must be bit-exact.  GEMV outputs must be within 1e-5
+relative of the oracle's sequential-sum GEMV, norm-wise:
+||y - y_ref||_inf <= 1e-5 * ||y_ref||_inf (the fp32-accumulate contract).
+"""
+import os
+
+import numpy as np
+import pytest
+
+from oracle import oracle as O
+from hacedle_cuda import synth as S
+
+pytestmark = pytest.mark.gpu
+TYPES = [S.GGML_Q8_0, S.GGML_Q5_0, S.GGML_Q4_K, S.GGML_Q6_K]
+NAMES = {S.GGML_Q8_0: "q8_0", S.GGML_Q5_0: "q5_0", S.GGML_Q4_K: "q4_k", S.GGML_Q6_K: "q6_k"}
+REL_TOL = 1e-5
+
+
+def _torch():
+    import torch
+    return torch
+
+
+def _dequant_gpu(ctx, w, rows, cols):
+    torch = _torch()
+    out = torch.empty(rows * cols, dtype=torch.float32, device="cuda")
+    ctx.dequantize(w, out)
+    torch.cuda.synchronize()
+    return out.cpu().numpy()
+
+
+def _rel_err(y, ref):
+    return float(np.abs(y - ref).max() / max(np.abs(ref).max(), 1e-30))
+
+
+@pytest.mark.parametrize("t", TYPES)
+def test_golden_blocks_bit_exact(ctx, golden_dir, t):
+    nm = NAMES[t]
+    for kind in ("ref_{}_block", "gguf_{}_rand", "gguf_{}_edge"):
+        base = kind.format(nm)
+        if kind.startswith("ref"):
+            raw = np.fromfile(os.path.join(golden_dir, base + ".raw"), np.uint8)
+            exp = np.fromfile(os.path.join(golden_dir, base + ".f32"), np.float32)
+        else:
+            raw = np.fromfile(os.path.join(golden_dir, base + ".raw"), np.uint8)
+            exp = np.fromfile(os.path.join(golden_dir, base + ".f32"), np.float32)
+        be, bb = S.BLOCK[t]
+        nblk = raw.size // bb
+        cols = be if kind.startswith("ref") or kind.endswith("edge") else 512
+        rows = nblk * be // cols
+        w = ctx.weight(t, raw, rows, cols)
+        y = _dequant_gpu(ctx, w, rows, cols)
+        same = (y.view(np.uint32) == exp.view(np.uint32)) | (np.isnan(y) & np.isnan(exp))
+        assert same.all(), base
+        assert np.array_equal(w.download(), raw), base
+
+
+@pytest.mark.parametrize("t,N,K", [(S.GGML_Q8_0, 896, 896), (S.GGML_Q5_0, 4864, 896), (S.GGML_Q6_K, 896, 4864),
+                                   (S.GGML_Q4_K, 896, 4864), (S.GGML_Q5_0, 37, 96), (S.GGML_Q4_K, 3, 512)])
+def test_dequant_full_tensor_bit_exact_and_round_trip(ctx, t, N, K):
+    raw = S.gen_weight(t, N, K, 1234 + t)
+    w = ctx.weight(t, raw, N, K)
+    y = _dequant_gpu(ctx, w, N, K)
+    ref = O.dequantize(t, raw, N * K)
+    assert np.array_equal(y.view(np.uint32), ref.view(np.uint32))
+    assert np.array_equal(w.download(), raw.reshape(-1))
+
+
+def test_dequant_random_bytes_bit_exact(ctx):
+    # Any byte pattern is a block (subnormal, inf and NaN scales included).
+    g = np.random.default_rng(5)
+    for t in TYPES:
+        be, bb = S.BLOCK[t]
+        raw = g.integers(0, 256, (16, (512 // be) * bb), dtype=np.uint8)
+        w = ctx.weight(t, raw, 16, 512)
+        y = _dequant_gpu(ctx, w, 16, 512)
+        ref = O.dequantize(t, raw, 16 * 512)
+        same = (y.view(np.uint32) == ref.view(np.uint32)) | (np.isnan(y) & np.isnan(ref))
+        assert same.all()
+        assert np.array_equal(w.download(), raw.reshape(-1))
+
+
+def test_upload_rejects_bad_shapes(ctx):
+    import hacedle_cuda as hc
+    raw = S.gen_weight(S.GGML_Q8_0, 4, 64, 1)
+    with pytest.raises(hc.HdError) as e:
+        ctx.weight(S.GGML_Q8_0, raw, 4, 48)
+    assert e.value.code == hc.HD_E_SHAPE
+    with pytest.raises(hc.HdError) as e:
+        ctx.weight(S.GGML_Q8_0, raw[:, :-1], 4, 64)
+    assert e.value.code == hc.HD_E_SHAPE
+    with pytest.raises(hc.HdError) as e:
+        ctx.weight(2, raw, 4, 64)  # Q4_0: not on this path
+    assert e.value.code == hc.HD_E_TYPE
+
+
+def _gemv_case(ctx, t, N, K, B, seed, bias=False, residual=False):
+    torch = _torch()
+    raw = S.gen_weight(t, N, K, seed)
+    X = S.gen_activations(B, K, seed + 1)
+    w = ctx.weight(t, raw, N, K)
+    x = torch.from_numpy(X).cuda()
+    y = torch.empty(B, N, dtype=torch.float32, device="cuda")
+    ref = O.qgemv(t, raw, N, K, X, threads=8)
+    b = r = None
+    if bias:
+        bh = S.rng(seed + 2).standard_normal(N, dtype=np.float32) * np.float32(0.02)
+        b = torch.from_numpy(bh).cuda()
+        ref = ref + bh[None, :]
+    if residual:
+        rh = S.rng(seed + 3).standard_normal((B, N), dtype=np.float32)
+        r = torch.from_numpy(rh).cuda()
+        y = r  # in place: y = residual + W x
+        ref = rh + ref
+    ctx.qgemv(w, x, y, bias=b, residual=r)
+    torch.cuda.synchronize()
+    return y.cpu().numpy(), ref
+
+
+@pytest.mark.parametrize("t,N,K", [(S.GGML_Q8_0, 896, 896), (S.GGML_Q5_0, 4864, 896), (S.GGML_Q6_K, 896, 4864),
+                                   (S.GGML_Q4_K, 896, 4864)])
+@pytest.mark.parametrize("B", [1, 4, 16])
+def test_gemv_config_shapes(ctx, t, N, K, B):
+    y, ref = _gemv_case(ctx, t, N, K, B, 10 + t)
+    assert _rel_err(y, ref) <= REL_TOL
+
+
+@pytest.mark.parametrize("t", TYPES)
+@pytest.mark.parametrize("N,K,B", [(1, 256, 1), (100, 512, 3), (129, 256, 2), (300, 768, 5), (257, 2304, 7),
+                                   (64, 256, 16), (1000, 256, 9)])
+def test_gemv_ragged_shapes(ctx, t, N, K, B):
+    y, ref = _gemv_case(ctx, t, N, K, B, 77 + N + K + B)
+    assert _rel_err(y, ref) <= REL_TOL
+
+
+@pytest.mark.parametrize("t", [S.GGML_Q5_0, S.GGML_Q6_K])
+def test_gemv_bias_and_residual_epilogues(ctx, t):
+    K = 896 if t == S.GGML_Q5_0 else 4864
+    y, ref = _gemv_case(ctx, t, 1152, K, 1, 5, bias=True)
+    assert _rel_err(y, ref) <= REL_TOL
+    y, ref = _gemv_case(ctx, t, 896, K, 4, 6, residual=True)
+    assert _rel_err(y, ref) <= REL_TOL
+
+
+@pytest.mark.parametrize("B", [1, 2, 4, 8, 16])
+def test_gemv_swiglu_pair(ctx, B):
+    torch = _torch()
+    N, K = 4864, 896
+    rg, ru = S.gen_weight(S.GGML_Q5_0, N, K, 21), S.gen_weight(S.GGML_Q5_0, N, K, 22)
+    X = S.gen_activations(B, K, 23)
+    wg, wu = ctx.weight(S.GGML_Q5_0, rg, N, K), ctx.weight(S.GGML_Q5_0, ru, N, K)
+    x = torch.from_numpy(X).cuda()
+    y = torch.empty(B, N, dtype=torch.float32, device="cuda")
+    ctx.qgemv_swiglu(wg, wu, x, y)
+    torch.cuda.synchronize()
+    g = O.qgemv(S.GGML_Q5_0, rg, N, K, X, threads=8)
+    u = O.qgemv(S.GGML_Q5_0, ru, N, K, X, threads=8)
+    ref = O.swiglu(g, u).reshape(B, N)
+    assert _rel_err(y.cpu().numpy(), ref) <= 2 * REL_TOL
+
+
+def test_gemv_deterministic_and_host_entry(ctx):
+    torch = _torch()
+    t, N, K = S.GGML_Q4_K, 896, 4864
+    raw = S.gen_weight(t, N, K, 99)
+    X = S.gen_activations(4, K, 98)
+    w = ctx.weight(t, raw, N, K)
+    x = torch.from_numpy(X).cuda()
+    ys = []
+    for _ in range(3):
+        y = torch.empty(4, N, dtype=torch.float32, device="cuda")
+        ctx.qgemv(w, x, y)
+        ys.append(y.cpu().numpy())
+    assert all(np.array_equal(ys[0].view(np.uint32), a.view(np.uint32)) for a in ys[1:])
+    yh = ctx.qgemv_host(w, X)
+    assert np.array_equal(yh.view(np.uint32), ys[0].view(np.uint32))
+
+
+def test_gemv_lm_head_q8_0(ctx):
+    # The tied LM head shape: 151936 x 896 Q8_0 (144.6 MB), batch 1.
+    y, ref = _gemv_case(ctx, S.GGML_Q8_0, 151936, 896, 1, 314)
+    assert _rel_err(y, ref) <= REL_TOL
