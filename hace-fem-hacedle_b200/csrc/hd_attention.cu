@@ -31,19 +31,20 @@ __global__ void k_kv_append(const float *__restrict__ k, const float *__restrict
 
 // rows: query rows; row r reads cache sequence cseq(r) with length len(r):
 //   decode  (lens != null): cseq = r, len = lens[r]
-//   prefill (lens == null): cseq = 0, len = pos0 + r + 1
+//   prefill (lens == null): rows are seqT consecutive tokens per sequence,
+//                           cseq = r / seqT, len = pos0 + r % seqT + 1
 template <int HD>
 __global__ void __launch_bounds__(128) k_attention(const float *__restrict__ q, const float *__restrict__ kc,
                                                    const float *__restrict__ vc, const int32_t *__restrict__ lens,
-                                                   int pos0, int n_heads, int n_kv, int max_ctx, float scale,
-                                                   float *__restrict__ out) {
+                                                   int pos0, int seqT, int n_heads, int n_kv, int max_ctx,
+                                                   float scale, float *__restrict__ out) {
     extern __shared__ float sm[];
     pdl_wait();
     pdl_trigger();
     const int r = blockIdx.x, kvh = blockIdx.y;
     const int rep = n_heads / n_kv, h0 = kvh * rep;
-    const int cseq = lens ? r : 0;
-    int L = lens ? lens[r] : pos0 + r + 1;
+    const int cseq = lens ? r : r / seqT;
+    int L = lens ? lens[r] : pos0 + r % seqT + 1;
     L = L < 0 ? 0 : L > max_ctx ? max_ctx : L;
     float *qs = sm;               // [rep][HD]
     float *sc = sm + rep * HD;    // [rep][L]
@@ -98,7 +99,7 @@ __global__ void __launch_bounds__(128) k_attention(const float *__restrict__ q, 
 
 template <int HD>
 cudaError_t launch_attn(hd_ctx *ctx, int rows, int n_heads, int n_kv, int maxlen, const float *q, const float *kc,
-                        const float *vc, const int32_t *lens, int pos0, int max_ctx, float *out) {
+                        const float *vc, const int32_t *lens, int pos0, int seqT, int max_ctx, float *out) {
     int rep = n_heads / n_kv;
     size_t smem = (size_t)rep * (HD + maxlen) * sizeof(float);
     if (smem > 48 * 1024) {
@@ -107,12 +108,15 @@ cudaError_t launch_attn(hd_ctx *ctx, int rows, int n_heads, int n_kv, int maxlen
         if (e != cudaSuccess) return e;
     }
     float scale = sqrtf((float)HD);
-    return hd_launch(ctx, k_attention<HD>, dim3(rows, n_kv), dim3(128), smem, q, kc, vc, lens, pos0, n_heads, n_kv,
-                     max_ctx, scale, out);
+    return hd_launch(ctx, k_attention<HD>, dim3(rows, n_kv), dim3(128), smem, q, kc, vc, lens, pos0, seqT, n_heads,
+                     n_kv, max_ctx, scale, out);
 }
 
-int run_attention(hd_ctx *ctx, const float *q, const float *kc, const float *vc, const int32_t *lens, int rows,
-                  int pos0, int n_heads, int n_kv, int hd, int max_ctx, int maxlen, float *out, const char *name) {
+}  // namespace
+
+int hd_attention_run(hd_ctx *ctx, const float *q, const float *kc, const float *vc, const int32_t *lens, int rows,
+                     int pos0, int seqT, int n_heads, int n_kv, int hd, int max_ctx, int maxlen, float *out,
+                     const char *name) {
     if (!ctx || !q || !kc || !vc || !out) return hd_fail(ctx, HD_E_ARG, "%s: null argument", name);
     HD_REQUIRE(ctx, n_heads > 0 && n_kv > 0 && n_heads % n_kv == 0, HD_E_SHAPE,
                "%s: n_heads %d is not a multiple of n_kv %d", name, n_heads, n_kv);
@@ -122,15 +126,13 @@ int run_attention(hd_ctx *ctx, const float *q, const float *kc, const float *vc,
                maxlen, n_heads / n_kv);
     if (rows == 0) return HD_OK;
     cudaError_t e;
-    if (hd == 64) e = launch_attn<64>(ctx, rows, n_heads, n_kv, maxlen, q, kc, vc, lens, pos0, max_ctx, out);
-    else if (hd == 128) e = launch_attn<128>(ctx, rows, n_heads, n_kv, maxlen, q, kc, vc, lens, pos0, max_ctx, out);
-    else if (hd == 32) e = launch_attn<32>(ctx, rows, n_heads, n_kv, maxlen, q, kc, vc, lens, pos0, max_ctx, out);
+    if (hd == 64) e = launch_attn<64>(ctx, rows, n_heads, n_kv, maxlen, q, kc, vc, lens, pos0, seqT, max_ctx, out);
+    else if (hd == 128) e = launch_attn<128>(ctx, rows, n_heads, n_kv, maxlen, q, kc, vc, lens, pos0, seqT, max_ctx, out);
+    else if (hd == 32) e = launch_attn<32>(ctx, rows, n_heads, n_kv, maxlen, q, kc, vc, lens, pos0, seqT, max_ctx, out);
     else return hd_fail(ctx, HD_E_UNSUPPORTED, "%s: head_dim %d (32, 64 or 128 supported)", name, hd);
     if (e != cudaSuccess) return hd_fail(ctx, HD_E_CUDA, "%s: %s", name, cudaGetErrorString(e));
     return HD_OK;
 }
-
-}  // namespace
 
 extern "C" int hd_kv_append(hd_ctx *ctx, const float *k, const float *v, float *kc, float *vc, const int32_t *pos0,
                             int seqs, int tokens, int n_kv, int head_dim, int max_ctx) {
@@ -148,13 +150,13 @@ extern "C" int hd_attention_decode(hd_ctx *ctx, const float *q, const float *kc,
                                    const int32_t *len, int seqs, int n_heads, int n_kv, int head_dim, int max_ctx,
                                    float *out) {
     if (!len) return hd_fail(ctx, HD_E_ARG, "hd_attention_decode: null lengths");
-    return run_attention(ctx, q, kc, vc, len, seqs, 0, n_heads, n_kv, head_dim, max_ctx, max_ctx, out,
-                         "hd_attention_decode");
+    return hd_attention_run(ctx, q, kc, vc, len, seqs, 0, 1, n_heads, n_kv, head_dim, max_ctx, max_ctx, out,
+                            "hd_attention_decode");
 }
 
 extern "C" int hd_attention_prefill(hd_ctx *ctx, const float *q, const float *kc, const float *vc, int T, int pos0,
                                     int n_heads, int n_kv, int head_dim, int max_ctx, float *out) {
     if (T < 0 || pos0 < 0) return hd_fail(ctx, HD_E_ARG, "hd_attention_prefill: negative size");
-    return run_attention(ctx, q, kc, vc, nullptr, T, pos0, n_heads, n_kv, head_dim, max_ctx, pos0 + T, out,
-                         "hd_attention_prefill");
+    return hd_attention_run(ctx, q, kc, vc, nullptr, T, pos0, T > 0 ? T : 1, n_heads, n_kv, head_dim, max_ctx,
+                            pos0 + T, out, "hd_attention_prefill");
 }

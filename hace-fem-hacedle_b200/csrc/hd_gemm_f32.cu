@@ -157,8 +157,7 @@ extern "C" int hd_qgemm_host(hd_ctx *ctx, const hd_weight *w, const float *X_hos
     rc = hd_qgemm(ctx, w, ctx->hbuf_x, ctx->hbuf_y, T, precision);
     if (rc) return rc;
     HD_CUDA_TRY(ctx, cudaMemcpyAsync(Y_host, ctx->hbuf_y, yb, cudaMemcpyDeviceToHost, ctx->stream));
-    HD_CUDA_TRY(ctx, cudaStreamSynchronize(ctx->stream));
-    return HD_OK;
+    return hd_ctx_check_device_errors(ctx);
 }
 
 extern "C" int hd_matmul_f32(hd_ctx *ctx, const float *a, const float *b, float *out, int64_t m, int64_t n,

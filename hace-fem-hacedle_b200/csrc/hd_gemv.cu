@@ -2,22 +2,29 @@
 // a gate/up pair) for b < B <= 16, fp32 accumulation, weights unpacked in
 // registers straight from the unit-major layout.
 //
-// Work split.  A CTA owns NT*RPT output rows (lane t of a warp owns row
-// tile*NT*RPT + i*NT + t) over a range of U units (32 inputs each) of K; the
-// grid is tiles x splits.  For every unit a warp reads 32 consecutive rows'
-// quants as one contiguous span; x[b][unit] comes from shared memory as a
-// warp-wide broadcast, so x traffic is one shared load per 4 inputs per batch
-// row, shared by all rows of the thread.
+// Work split.  A CTA owns RC consecutive output rows over the whole of K (or
+// over one of S slices of K when K is very long for few rows).  Its NT = RC*G
+// threads form G groups: thread t owns row t % RC and the units
+// t / RC, t / RC + G, ...; lanes on consecutive rows read one unit of
+// consecutive rows as one contiguous span of the unit-major layout.  RC is
+// about rows / SMs, so there is roughly one CTA per SM and every CTA streams
+// its whole slice of W with all of its loads in flight at once.
 //
-// Overlap.  The CTA issues the loads of its first chunk of weights before
+// Reduction.  Per-row partial sums meet in shared memory and are added in a
+// fixed order (group 0, 1, ..., G-1), so results are bitwise reproducible.
+// With S > 1 the CTAs of a row tile publish partials to the workspace and the
+// last to arrive (atomic ticket) adds them in split order and resets the
+// ticket.
+//
+// x.  Activations are read from global memory through L1 after the
+// dependency wait; lanes that share a unit read the same addresses (a
+// broadcast).  Q4_K's per-unit sums of x, needed for its min term, are
+// computed once per CTA into shared memory.
+//
+// Overlap.  The first chunk of each thread's weight loads is issued before
 // griddepcontrol.wait: under programmatic dependent launch those loads run
 // while the previous kernel in the stream is still finishing.  Nothing the
-// previous kernel writes is touched before the wait.
-//
-// Split-K.  With S > 1 splits each CTA writes its partial sums to the
-// workspace; the last CTA to arrive for a row tile (atomic ticket) adds the S
-// partials in split order 0..S-1 -- a fixed order, so results are bitwise
-// reproducible -- applies the epilogue and resets the ticket to zero.
+// previous kernel writes is read or written before the wait.
 //
 // Unpacking.  Bytes become floats exactly via byte_perm into 0x4B0000bb
 // (= 2^23 + byte) and one subtraction of 2^23 + offset; Q5_0's fifth bit and
@@ -27,7 +34,7 @@
 
 namespace {
 
-constexpr int UC = 4;  // units per register chunk
+constexpr int UC = 4;  // units per thread per register chunk
 
 struct GemvArgs {
     WView w0, w1;          // w1: the up weight of a SwiGLU pair
@@ -38,10 +45,10 @@ struct GemvArgs {
     float *ws;             // split-K partials [S][NB][Neff]
     int *tickets;          // [tiles]
     int B, N, ldy, K;
+    int RC, G;             // rows per CTA, unit groups per CTA
     int U, S;              // units per split, splits
     int pair;              // 1: SwiGLU of (w0, w1)
 };
-
 template <int TYPE>
 struct URegs;
 template <>
@@ -201,121 +208,130 @@ __device__ __forceinline__ void unit_fma(const URegs<TYPE> &g, int u, const floa
 
 __device__ __forceinline__ float silu_mul(float g, float u) { return g / (1.0f + expf(-g)) * u; }
 
-template <int TYPE, int NB, int RPT>
+template <int TYPE, int NB, int P>
 __global__ void __launch_bounds__(256) k_qgemv(GemvArgs a) {
-    extern __shared__ float4 smem4[];
+    extern __shared__ float sm[];
     const int t = threadIdx.x, NT = blockDim.x;
+    const int RC = a.RC, G = a.G;
     const int tile = blockIdx.x, split = blockIdx.y;
-    const int rows_cta = a.pair ? NT : NT * RPT;
+    const int r = t % RC, g = t / RC;
+    const int64_t row = (int64_t)tile * RC + r;
+    const bool ok = row < a.N && g < G;
     const int u0 = split * a.U;
-    const int ucta = min(a.U, a.w0.units - u0);
-
-    int64_t row[RPT];
-    bool ok[RPT];
-#pragma unroll
-    for (int i = 0; i < RPT; i++) {
-        row[i] = a.pair ? (int64_t)tile * rows_cta + t : (int64_t)tile * rows_cta + i * NT + t;
-        ok[i] = row[i] < a.N;
-    }
+    const int u1 = min(a.w0.units, u0 + a.U);
     const WView wa = a.w0, wb = a.w1;
-    auto wsel = [&](int i) -> WView { return (a.pair && i == 1) ? wb : wa; };
 
-    // Chunk 0 of the weights: independent of earlier kernels, so issued
-    // before the dependency wait.
-    URegs<TYPE> cur[UC][RPT];
+    URegs<TYPE> cur[UC][P + 1];
 #pragma unroll
-    for (int c = 0; c < UC; c++)
+    for (int c = 0; c < UC; c++) {
+        const int u = u0 + g + c * G;
 #pragma unroll
-        for (int i = 0; i < RPT; i++) {
-            if (ok[i] && c < ucta) load_unit<TYPE>(wsel(i), row[i], u0 + c, cur[c][i]);
-            else zero_unit<TYPE>(cur[c][i]);
+        for (int p = 0; p <= P; p++) {
+            if (ok && u < u1) load_unit<TYPE>(p ? wb : wa, row, u, cur[c][p]);
+            else zero_unit<TYPE>(cur[c][p]);
         }
+    }
     pdl_trigger();
     pdl_wait();
 
-    // Stage x[b][u0*32 .. (u0+ucta)*32) for b < NB (zeros for b >= B).
-    const int xs4 = a.U * 8;  // float4 per batch row in shared memory
-    float4 *xsm = smem4;
-    float *xsum = (float *)(smem4 + NB * xs4);
-    for (int i = t; i < NB * ucta * 8; i += NT) {
-        int b = i / (ucta * 8), j = i % (ucta * 8);
-        float4 v = make_float4(0.f, 0.f, 0.f, 0.f);
-        if (b < a.B) v = __ldg((const float4 *)(a.x + (int64_t)b * a.K + (int64_t)u0 * 32) + j);
-        xsm[b * xs4 + j] = v;
-    }
+    // Q4_K: sum of x over every unit of this CTA's K range, per batch row.
+    float *xsum = sm;                         // [NB][U]
+    float *red = sm + (TYPE == HD_TYPE_Q4_K ? NB * a.U : 0);  // [NT][P+1][NB]
     if constexpr (TYPE == HD_TYPE_Q4_K) {
-        __syncthreads();
-        for (int i = t; i < NB * ucta; i += NT) {
-            int b = i / ucta, ul = i % ucta;
-            const float *p = (const float *)(xsm + b * xs4 + ul * 8);
+        const int nu = u1 - u0;
+        for (int i = t; i < NB * nu; i += NT) {
+            const int b = i / nu, ul = i % nu;
             float s = 0.f;
+            if (b < a.B) {
+                const float4 *p = (const float4 *)(a.x + (int64_t)b * a.K + (int64_t)(u0 + ul) * 32);
 #pragma unroll
-            for (int j = 0; j < 32; j++) s += p[j];
+                for (int j = 0; j < 8; j++) {
+                    float4 v = p[j];
+                    s += (v.x + v.y) + (v.z + v.w);
+                }
+            }
             xsum[b * a.U + ul] = s;
         }
+        __syncthreads();
     }
-    __syncthreads();
 
-    float acc[RPT][NB];
+    float acc[P + 1][NB];
 #pragma unroll
-    for (int i = 0; i < RPT; i++)
+    for (int p = 0; p <= P; p++)
 #pragma unroll
-        for (int b = 0; b < NB; b++) acc[i][b] = 0.f;
+        for (int b = 0; b < NB; b++) acc[p][b] = 0.f;
 
-    for (int c0 = 0; c0 < ucta; c0 += UC) {
-        if (c0 > 0) {
+    const int xs4 = a.K / 4;  // float4 per batch row of x
+    for (int base = u0 + g; base < u1; base += UC * G) {
+        if (base != u0 + g) {
 #pragma unroll
-            for (int c = 0; c < UC; c++)
+            for (int c = 0; c < UC; c++) {
+                const int u = base + c * G;
 #pragma unroll
-                for (int i = 0; i < RPT; i++) {
-                    if (ok[i] && c0 + c < ucta) load_unit<TYPE>(wsel(i), row[i], u0 + c0 + c, cur[c][i]);
-                    else zero_unit<TYPE>(cur[c][i]);
+                for (int p = 0; p <= P; p++) {
+                    if (ok && u < u1) load_unit<TYPE>(p ? wb : wa, row, u, cur[c][p]);
+                    else zero_unit<TYPE>(cur[c][p]);
                 }
+            }
         }
 #pragma unroll
         for (int c = 0; c < UC; c++) {
-            if (c0 + c < ucta) {
+            const int u = base + c * G;
+            if (ok && u < u1) {
+                const float4 *xp = (const float4 *)(a.x + (int64_t)u * 32);
 #pragma unroll
-                for (int i = 0; i < RPT; i++)
-                    unit_fma<TYPE, NB>(cur[c][i], u0 + c0 + c, xsm + (c0 + c) * 8, xs4, xsum + (c0 + c), a.U,
-                                       acc[i]);
+                for (int p = 0; p <= P; p++)
+                    unit_fma<TYPE, NB>(cur[c][p], u, xp, xs4, xsum + (u - u0), a.U, acc[p]);
             }
         }
     }
 
-    auto epilogue = [&](int i, int b, float v, float v_up) {
-        int64_t r = row[i];
-        if (a.pair) {
-            a.y[(int64_t)b * a.ldy + r] = silu_mul(v, v_up);
+    // Per-row sums over the G groups, in group order.
+#pragma unroll
+    for (int p = 0; p <= P; p++)
+#pragma unroll
+        for (int b = 0; b < NB; b++) red[(t * (P + 1) + p) * NB + b] = acc[p][b];
+    __syncthreads();
+
+    const int64_t neff = P ? 2 * (int64_t)a.N : (int64_t)a.N;
+    auto epilogue = [&](int64_t rw, int b, float v, float vu) {
+        if (P) {
+            a.y[(int64_t)b * a.ldy + rw] = silu_mul(v, vu);
         } else {
-            if (a.bias) v = v + a.bias[r];
-            if (a.residual) v = a.residual[(int64_t)b * a.ldy + r] + v;
-            a.y[(int64_t)b * a.ldy + r] = v;
+            if (a.bias) v = v + a.bias[rw];
+            if (a.residual) v = a.residual[(int64_t)b * a.ldy + rw] + v;
+            a.y[(int64_t)b * a.ldy + rw] = v;
         }
     };
-
+    const int nout = RC * a.B;
     if (a.S == 1) {
-        if (a.pair) {
-            if (ok[0])
-                for (int b = 0; b < a.B; b++) epilogue(0, b, acc[0][b], acc[RPT - 1][b]);
-        } else {
+        for (int j = t; j < nout; j += NT) {
+            const int rr = j % RC, b = j / RC;
+            const int64_t rw = (int64_t)tile * RC + rr;
+            if (rw >= a.N) continue;
+            float v[P + 1];
 #pragma unroll
-            for (int i = 0; i < RPT; i++)
-                if (ok[i])
-                    for (int b = 0; b < a.B; b++) epilogue(i, b, acc[i][b], 0.f);
+            for (int p = 0; p <= P; p++) {
+                float s = 0.f;
+                for (int gg = 0; gg < G; gg++) s += red[((gg * RC + rr) * (P + 1) + p) * NB + b];
+                v[p] = s;
+            }
+            epilogue(rw, b, v[0], v[P]);
         }
         return;
     }
 
-    // Split-K: publish partials, last arriving CTA of the tile reduces.
-    const int64_t neff = a.pair ? 2 * (int64_t)a.N : (int64_t)a.N;
+    // Split-K: publish this CTA's row sums, the last CTA of the tile reduces.
+    for (int j = t; j < nout; j += NT) {
+        const int rr = j % RC, b = j / RC;
+        const int64_t rw = (int64_t)tile * RC + rr;
+        if (rw >= a.N) continue;
 #pragma unroll
-    for (int i = 0; i < RPT; i++) {
-        if (!ok[i]) continue;
-        int64_t re = (a.pair && i == 1) ? a.N + row[i] : row[i];
-#pragma unroll
-        for (int b = 0; b < NB; b++)
-            if (b < a.B) __stcg(a.ws + ((int64_t)split * NB + b) * neff + re, acc[i][b]);
+        for (int p = 0; p <= P; p++) {
+            float s = 0.f;
+            for (int gg = 0; gg < G; gg++) s += red[((gg * RC + rr) * (P + 1) + p) * NB + b];
+            __stcg(a.ws + ((int64_t)split * NB + b) * neff + (p ? a.N + rw : rw), s);
+        }
     }
     __threadfence();
     __syncthreads();
@@ -324,71 +340,75 @@ __global__ void __launch_bounds__(256) k_qgemv(GemvArgs a) {
     __syncthreads();
     if (!last) return;
     __threadfence();
-    float red[RPT][NB];
+    for (int j = t; j < nout; j += NT) {
+        const int rr = j % RC, b = j / RC;
+        const int64_t rw = (int64_t)tile * RC + rr;
+        if (rw >= a.N) continue;
+        float v[P + 1];
 #pragma unroll
-    for (int i = 0; i < RPT; i++) {
-        int64_t re = (a.pair && i == 1) ? a.N + row[i] : row[i];
-#pragma unroll
-        for (int b = 0; b < NB; b++) {
+        for (int p = 0; p <= P; p++) {
             float s = 0.f;
-            if (ok[i] && b < a.B)
-                for (int sp = 0; sp < a.S; sp++) s += __ldcg(a.ws + ((int64_t)sp * NB + b) * neff + re);
-            red[i][b] = s;
+            for (int sp = 0; sp < a.S; sp++) s += __ldcg(a.ws + ((int64_t)sp * NB + b) * neff + (p ? a.N + rw : rw));
+            v[p] = s;
         }
-    }
-    if (a.pair) {
-        if (ok[0])
-            for (int b = 0; b < a.B; b++) epilogue(0, b, red[0][b], red[RPT - 1][b]);
-    } else {
-#pragma unroll
-        for (int i = 0; i < RPT; i++)
-            if (ok[i])
-                for (int b = 0; b < a.B; b++) epilogue(i, b, red[i][b], 0.f);
+        epilogue(rw, b, v[0], v[P]);
     }
     if (t == 0) a.tickets[tile] = 0;
 }
 
 struct Plan {
-    int nt, rpt, nb, U, S, tiles;
+    int nb, RC, G, nt, U, S, tiles;
+    size_t smem;
 };
 
 int pad_batch(int B) { return B <= 1 ? 1 : B <= 2 ? 2 : B <= 4 ? 4 : B <= 8 ? 8 : 16; }
 
-// Rows per CTA and split count: aim for about two resident CTAs per SM with
-// as few splits as that allows; the x slice in shared memory stays <= 48 KB.
+// RC ~ rows / SMs (one CTA per SM), G groups of RC threads (NT <= 256, no more
+// groups than units).  Split K only when the row tiles alone leave most SMs
+// idle and every split still gives each group a unit or more.
 Plan plan_gemv(int N, int units, int B, bool pair, int sms) {
     Plan p;
     p.nb = pad_batch(B);
-    p.rpt = (pair || p.nb <= 2) ? 2 : 1;
-    p.nt = 128;
-    int rows_cta = pair ? p.nt : p.nt * p.rpt;
-    p.tiles = (N + rows_cta - 1) / rows_cta;
-    int target = 2 * sms;
-    int S = (target + p.tiles - 1) / p.tiles;
-    S = S < 1 ? 1 : S > units ? units : S;
-    int U = (units + S - 1) / S;
-    int umax = (48 * 1024) / (p.nb * 128 + (p.nb * 4));
-    if (U > umax) U = umax;
-    if (U < 1) U = 1;
-    p.U = U;
-    p.S = (units + U - 1) / U;
+    int RC = (N + sms - 1) / sms;
+    RC = RC < 1 ? 1 : RC > 32 ? 32 : RC;
+    int G = 256 / RC;
+    if (G > units) G = units;
+    p.RC = RC;
+    p.G = G;
+    p.nt = RC * G;
+    p.tiles = (N + RC - 1) / RC;
+    int S = 1;
+    if (p.tiles * 2 < sms && units >= 2 * G) {
+        S = (sms + p.tiles - 1) / p.tiles;
+        if (S > units / G) S = units / G;
+        if (S < 1) S = 1;
+    }
+    p.U = (units + S - 1) / S;
+    p.S = (units + p.U - 1) / p.U;
+    const int P1 = pair ? 2 : 1;
+    p.smem = (size_t)p.nt * P1 * p.nb * sizeof(float) + (size_t)p.nb * p.U * sizeof(float);
     return p;
 }
 
-template <int TYPE, int NB, int RPT>
+template <int TYPE, int NB, int P>
 cudaError_t launch_inst(hd_ctx *ctx, const Plan &p, const GemvArgs &a) {
-    size_t smem = (size_t)NB * p.U * 32 * sizeof(float) + (size_t)NB * p.U * sizeof(float);
-    return hd_launch(ctx, k_qgemv<TYPE, NB, RPT>, dim3(p.tiles, p.S), dim3(p.nt), smem, a);
+    if (p.smem > 48 * 1024) {
+        cudaError_t e = cudaFuncSetAttribute(k_qgemv<TYPE, NB, P>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                             (int)p.smem);
+        if (e != cudaSuccess) return e;
+    }
+    return hd_launch(ctx, k_qgemv<TYPE, NB, P>, dim3(p.tiles, p.S), dim3(p.nt), p.smem, a);
 }
 
 template <int TYPE>
 cudaError_t launch_type(hd_ctx *ctx, const Plan &p, const GemvArgs &a) {
+    const bool pr = a.pair != 0;
     switch (p.nb) {
-    case 1: return p.rpt == 2 ? launch_inst<TYPE, 1, 2>(ctx, p, a) : launch_inst<TYPE, 1, 1>(ctx, p, a);
-    case 2: return p.rpt == 2 ? launch_inst<TYPE, 2, 2>(ctx, p, a) : launch_inst<TYPE, 2, 1>(ctx, p, a);
-    case 4: return p.rpt == 2 ? launch_inst<TYPE, 4, 2>(ctx, p, a) : launch_inst<TYPE, 4, 1>(ctx, p, a);
-    case 8: return p.rpt == 2 ? launch_inst<TYPE, 8, 2>(ctx, p, a) : launch_inst<TYPE, 8, 1>(ctx, p, a);
-    default: return p.rpt == 2 ? launch_inst<TYPE, 16, 2>(ctx, p, a) : launch_inst<TYPE, 16, 1>(ctx, p, a);
+    case 1: return pr ? launch_inst<TYPE, 1, 1>(ctx, p, a) : launch_inst<TYPE, 1, 0>(ctx, p, a);
+    case 2: return pr ? launch_inst<TYPE, 2, 1>(ctx, p, a) : launch_inst<TYPE, 2, 0>(ctx, p, a);
+    case 4: return pr ? launch_inst<TYPE, 4, 1>(ctx, p, a) : launch_inst<TYPE, 4, 0>(ctx, p, a);
+    case 8: return launch_inst<TYPE, 8, 0>(ctx, p, a);
+    default: return launch_inst<TYPE, 16, 0>(ctx, p, a);
     }
 }
 
@@ -406,7 +426,7 @@ int run_gemv(hd_ctx *ctx, const hd_weight *w, const hd_weight *w_up, const float
                    "%s: gate and up weights differ in type or shape", name);
     if (w_up && pad_batch(B) >= 8) {
         // Two plain GEMVs into scratch, then the elementwise SwiGLU (the fused
-        // pair would need 2 x 16 accumulators per thread at this batch).
+        // pair would hold 2 x 16 accumulators per thread at this batch).
         size_t one = (size_t)B * w->rows;
         int rc = hd_ensure_hbuf(ctx, &ctx->scratch, &ctx->scratch_bytes, 2 * one * sizeof(float));
         if (!rc) rc = run_gemv(ctx, w, nullptr, x, ctx->scratch, B, nullptr, nullptr, name);
@@ -433,6 +453,8 @@ int run_gemv(hd_ctx *ctx, const hd_weight *w, const hd_weight *w_up, const float
     a.N = (int)w->rows;
     a.ldy = (int)w->rows;
     a.K = (int)w->cols;
+    a.RC = p.RC;
+    a.G = p.G;
     a.U = p.U;
     a.S = p.S;
     a.pair = w_up ? 1 : 0;
@@ -455,7 +477,7 @@ extern "C" int hd_qgemv_swiglu(hd_ctx *ctx, const hd_weight *w_gate, const hd_we
     return run_gemv(ctx, w_gate, w_up, x_dev, y_dev, B, nullptr, nullptr, "hd_qgemv_swiglu");
 }
 
-static int ensure_hbuf(hd_ctx *ctx, float **buf, size_t *have, size_t need) {
+int hd_ensure_hbuf(hd_ctx *ctx, float **buf, size_t *have, size_t need) {
     if (need <= *have) return HD_OK;
     HD_CUDA_TRY(ctx, cudaStreamSynchronize(ctx->stream));
     cudaFree(*buf);
@@ -470,8 +492,8 @@ extern "C" int hd_qgemv_host(hd_ctx *ctx, const hd_weight *w, const float *x_hos
     if (!ctx || !w || !x_host || !y_host) return hd_fail(ctx, HD_E_ARG, "hd_qgemv_host: null argument");
     HD_REQUIRE(ctx, B >= 1 && B <= 16, HD_E_ARG, "hd_qgemv_host: batch %d outside 1..16", B);
     size_t xb = (size_t)B * w->cols * sizeof(float), yb = (size_t)B * w->rows * sizeof(float);
-    int rc = ensure_hbuf(ctx, &ctx->hbuf_x, &ctx->hbuf_x_bytes, xb);
-    if (!rc) rc = ensure_hbuf(ctx, &ctx->hbuf_y, &ctx->hbuf_y_bytes, yb);
+    int rc = hd_ensure_hbuf(ctx, &ctx->hbuf_x, &ctx->hbuf_x_bytes, xb);
+    if (!rc) rc = hd_ensure_hbuf(ctx, &ctx->hbuf_y, &ctx->hbuf_y_bytes, yb);
     if (rc) return rc;
     HD_CUDA_TRY(ctx, cudaMemcpyAsync(ctx->hbuf_x, x_host, xb, cudaMemcpyHostToDevice, ctx->stream));
     rc = hd_qgemv(ctx, w, ctx->hbuf_x, ctx->hbuf_y, B, nullptr, nullptr);
@@ -480,6 +502,3 @@ extern "C" int hd_qgemv_host(hd_ctx *ctx, const hd_weight *w, const float *x_hos
     HD_CUDA_TRY(ctx, cudaStreamSynchronize(ctx->stream));
     return HD_OK;
 }
-
-// Exposed for the GEMM and decoder files.
-int hd_ensure_hbuf(hd_ctx *ctx, float **buf, size_t *have, size_t need) { return ensure_hbuf(ctx, buf, have, need); }

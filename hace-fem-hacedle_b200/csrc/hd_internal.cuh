@@ -96,6 +96,12 @@ int hd_ensure_workspace(hd_ctx *ctx, size_t bytes, size_t tickets);
 int hd_ensure_rope(hd_ctx *ctx, int head_dim, float theta);
 int hd_check_launch(hd_ctx *ctx, const char *what);
 bool hd_type_supported(int t);
+int hd_ensure_hbuf(hd_ctx *ctx, float **buf, size_t *have, size_t need);
+int hd_qgemm_f32(hd_ctx *ctx, const hd_weight *w, const float *X, float *Y, int T);
+// Attention over `rows` query rows (see k_attention in hd_attention.cu).
+int hd_attention_run(hd_ctx *ctx, const float *q, const float *kc, const float *vc, const int32_t *lens, int rows,
+                     int pos0, int seqT, int n_heads, int n_kv, int hd, int max_ctx, int maxlen, float *out,
+                     const char *name);
 
 // Launch with programmatic stream serialization, so the next kernel's
 // pre-dependency prologue (weight prefetch) overlaps this one's tail.

@@ -20,11 +20,12 @@ LIB_PATH = os.path.join(ROOT, "lib", "libhacedle_cuda.so")
 HD_OK, HD_E_ARG, HD_E_SHAPE, HD_E_TYPE, HD_E_CUDA, HD_E_TIMEOUT, HD_E_NCCL, HD_E_OOM, HD_E_UNSUPPORTED = range(9)
 TYPE_Q5_0, TYPE_Q8_0, TYPE_Q4_K, TYPE_Q6_K = 6, 8, 12, 14
 PREC_FP32, PREC_BF16_TC = 0, 1
+CUDA_STREAM_LEGACY = 1  # cudaStreamLegacy
 
 # Every symbol include/hacedle_cuda.h declares.
 EXPORTS = [
     "hd_ctx_create", "hd_ctx_destroy", "hd_ctx_set_stream", "hd_ctx_synchronize", "hd_ctx_reserve_workspace",
-    "hd_last_error", "hd_ctx_launch_count", "hd_version",
+    "hd_last_error", "hd_ctx_launch_count", "hd_version", "hd_ctx_check_device_errors",
     "hd_weight_upload", "hd_weight_upload_device", "hd_weight_free", "hd_weight_info", "hd_weight_download",
     "hd_dequantize", "hd_qgemv", "hd_qgemv_swiglu", "hd_qgemv_host", "hd_qgemm", "hd_qgemm_host", "hd_matmul_f32",
     "hd_rmsnorm", "hd_rmsnorm_graph", "hd_rope_neox", "hd_rope_interleaved", "hd_softmax_rows", "hd_swiglu",
@@ -54,7 +55,7 @@ def lib() -> C.CDLL:
     sig = {
         "hd_ctx_create": [I, C.POINTER(V)], "hd_ctx_destroy": [V], "hd_ctx_set_stream": [V, V],
         "hd_ctx_synchronize": [V], "hd_ctx_reserve_workspace": [V, SZ], "hd_last_error": [V],
-        "hd_ctx_launch_count": [V], "hd_version": [],
+        "hd_ctx_launch_count": [V], "hd_version": [], "hd_ctx_check_device_errors": [V],
         "hd_weight_upload": [V, V, SZ, I, I64, I64, C.POINTER(V)],
         "hd_weight_upload_device": [V, V, SZ, I, I64, I64, C.POINTER(V)],
         "hd_weight_free": [V, V],
@@ -135,7 +136,10 @@ class Context:
             self.set_stream(torch.cuda.current_stream(device).cuda_stream)
 
     def set_stream(self, stream: int | None):
-        self._check(lib().hd_ctx_set_stream(self.h, stream))
+        """Enqueue on `stream` (a cudaStream_t as int).  Handle 0, torch's
+        default stream, is the legacy default stream: it is passed as
+        cudaStreamLegacy (1), because NULL selects the context's own stream."""
+        self._check(lib().hd_ctx_set_stream(self.h, stream if stream else CUDA_STREAM_LEGACY))
 
     def _check(self, rc: int):
         if rc != HD_OK:
@@ -150,6 +154,9 @@ class Context:
 
     def synchronize(self):
         self._check(lib().hd_ctx_synchronize(self.h))
+
+    def check_device_errors(self):
+        self._check(lib().hd_ctx_check_device_errors(self.h))
 
     def reserve_workspace(self, nbytes: int):
         self._check(lib().hd_ctx_reserve_workspace(self.h, nbytes))
@@ -250,5 +257,76 @@ class Context:
     def __del__(self):
         try:
             self.close()
+        except Exception:
+            pass
+
+
+class _DecCfg(C.Structure):
+    _fields_ = [(n, C.c_int) for n in ("hidden", "n_layers", "n_heads", "n_kv", "head_dim", "ffn", "vocab", "max_ctx",
+                                        "max_seqs")] + [("eps", C.c_float), ("theta", C.c_float)]
+
+
+class _LayerW(C.Structure):
+    _fields_ = [(n, C.c_void_p) for n in ("wq", "wk", "wv", "wo", "wg", "wu", "wd", "bq", "bk", "bv", "attn_norm",
+                                           "ffn_norm")]
+
+
+class Decoder:
+    """hd_decoder: the Qwen2-shaped decoder on the device.
+
+    `model` is synth.gen_decoder()'s dict: cfg, layers (each weight a tuple
+    (ggml_type, raw bytes, rows, cols) plus f32 bias / norm vectors), out_norm,
+    embed.  Weights are uploaded once."""
+
+    def __init__(self, ctx: Context, model: dict, max_ctx: int, max_seqs: int = 1):
+        cfg = model["cfg"]
+        self.ctx, self.cfg = ctx, cfg
+        self.weights, self._keep = [], []
+        arr = (_LayerW * cfg["n_layers"])()
+        for i, L in enumerate(model["layers"]):
+            for name in ("wq", "wk", "wv", "wo", "wg", "wu", "wd"):
+                t, raw, n, k = L[name]
+                w = ctx.weight(t, raw, n, k)
+                self.weights.append(w)
+                setattr(arr[i], name, w.h)
+            for name in ("bq", "bk", "bv", "attn_norm", "ffn_norm"):
+                a = np.ascontiguousarray(L[name], np.float32)
+                self._keep.append(a)
+                setattr(arr[i], name, a.ctypes.data)
+        t, raw, n, k = model["embed"]
+        self.embed = ctx.weight(t, raw, n, k)
+        on = np.ascontiguousarray(model["out_norm"], np.float32)
+        c = _DecCfg(cfg["hidden"], cfg["n_layers"], cfg["n_heads"], cfg["n_kv"], cfg["head_dim"], cfg["ffn"],
+                    cfg["vocab"], max_ctx, max_seqs, cfg["eps"], cfg["theta"])
+        h = V()
+        ctx._check(lib().hd_decoder_create(ctx.h, C.byref(c), arr, on.ctypes.data, self.embed.h, C.byref(h)))
+        self.h = h
+        self._keep.clear()
+
+    def generate(self, prompts: np.ndarray, n_gen: int, precision: int = PREC_FP32):
+        """prompts [seqs, n_prompt] int32 -> (tokens [seqs, n_gen], decode_ms, prefill_ms)."""
+        p = np.ascontiguousarray(prompts, np.int32)
+        if p.ndim == 1:
+            p = p[None]
+        out = np.zeros((p.shape[0], n_gen), np.int32)
+        dm, pm = C.c_float(), C.c_float()
+        self.ctx._check(lib().hd_decoder_generate(self.h, p.ctypes.data, p.shape[0], p.shape[1], n_gen, precision,
+                                                  out.ctypes.data, C.byref(dm), C.byref(pm)))
+        return out, dm.value, pm.value
+
+    def free(self):
+        if getattr(self, "h", None):
+            lib().hd_decoder_free(self.h)
+            self.h = None
+        for w in self.weights:
+            w.free()
+        self.weights = []
+        if getattr(self, "embed", None):
+            self.embed.free()
+            self.embed = None
+
+    def __del__(self):
+        try:
+            self.free()
         except Exception:
             pass

@@ -62,7 +62,8 @@ typedef struct hd_decoder hd_decoder;
 int hd_ctx_create(int device, hd_ctx **out);
 int hd_ctx_destroy(hd_ctx *ctx);
 /* Enqueue subsequent work on `stream` (a cudaStream_t); NULL restores the
- * context's own stream. */
+ * context's own (non-blocking) stream.  Pass cudaStreamLegacy for the legacy
+ * default stream. */
 int hd_ctx_set_stream(hd_ctx *ctx, void *stream);
 int hd_ctx_synchronize(hd_ctx *ctx);
 /* Make sure the context's split-K workspace holds at least `bytes`, so that
@@ -70,6 +71,9 @@ int hd_ctx_synchronize(hd_ctx *ctx);
 int hd_ctx_reserve_workspace(hd_ctx *ctx, size_t bytes);
 /* Message of the last failure on this context ("" if none). */
 const char *hd_last_error(const hd_ctx *ctx);
+/* Synchronizes the stream, then reads and clears the device error word that
+ * bounded device-side waits set when they expire: HD_E_TIMEOUT if one did. */
+int hd_ctx_check_device_errors(hd_ctx *ctx);
 /* Number of kernels this context has launched (for launch accounting). */
 uint64_t hd_ctx_launch_count(const hd_ctx *ctx);
 const char *hd_version(void);

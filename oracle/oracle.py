@@ -277,3 +277,17 @@ def decoder_generate(cfg: dict, layers: list, out_norm, embed, prompt, n_gen: in
     if rc != 0:
         raise RuntimeError("oracle: decoder_generate failed")
     return (out, logits) if return_logits else out
+
+
+def dequant_model(model: dict):
+    """A synth.gen_decoder() model with every quantized weight dequantized
+    (f32 [rows, cols]); returns (layers, out_norm, embed) for decoder_generate."""
+    layers = []
+    for L in model["layers"]:
+        d = {k: L[k] for k in ("bq", "bk", "bv", "attn_norm", "ffn_norm")}
+        for k in ("wq", "wk", "wv", "wo", "wg", "wu", "wd"):
+            t, raw, n, kk = L[k]
+            d[k] = dequantize(t, raw, n * kk).reshape(n, kk)
+        layers.append(d)
+    t, raw, n, kk = model["embed"]
+    return layers, model["out_norm"], dequantize(t, raw, n * kk).reshape(n, kk)

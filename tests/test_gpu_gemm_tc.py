@@ -1,0 +1,65 @@
+"""tcgen05 prefill Q-GEMM (bf16 operands, fp32 accumulate in TMEM) against the
+oracle: ||Y - Y_ref||_inf <= 2e-2 * ||Y_ref||_inf (the bf16 tensor-core
+contract), no bounded device wait expired, and bitwise-stable reruns."""
+import numpy as np
+import pytest
+
+from oracle import oracle as O
+from hacedle_cuda import synth as S
+
+pytestmark = pytest.mark.gpu
+TOL = 2e-2
+
+
+@pytest.mark.parametrize("t,N,K", [(S.GGML_Q5_0, 4864, 896), (S.GGML_Q4_K, 896, 4864), (S.GGML_Q6_K, 896, 4864),
+                                   (S.GGML_Q8_0, 896, 896)])
+@pytest.mark.parametrize("T", [128, 512])
+def test_qgemm_tc_config_shapes(ctx, t, N, K, T):
+    import torch
+    raw = S.gen_weight(t, N, K, 60 + t)
+    X = S.gen_activations(T, K, 61)
+    w = ctx.weight(t, raw, N, K)
+    Y = torch.empty(T, N, device="cuda")
+    ctx.qgemm(w, torch.from_numpy(X).cuda(), Y, precision=1)
+    ctx.check_device_errors()
+    got = Y.cpu().numpy()
+    Wf = O.dequantize(t, raw, N * K).reshape(N, K)
+    ref = X @ Wf.T
+    err = np.abs(got - ref).max() / np.abs(ref).max()
+    assert err <= TOL, err
+    Y2 = torch.empty(T, N, device="cuda")
+    ctx.qgemm(w, torch.from_numpy(X).cuda(), Y2, precision=1)
+    torch.cuda.synchronize()
+    assert torch.equal(Y, Y2)
+
+
+@pytest.mark.parametrize("t,N,K,T", [(S.GGML_Q5_0, 100, 96, 1), (S.GGML_Q5_0, 200, 160, 70), (S.GGML_Q4_K, 130, 512, 33),
+                                     (S.GGML_Q6_K, 257, 256, 257), (S.GGML_Q8_0, 64, 64, 300)])
+def test_qgemm_tc_ragged(ctx, t, N, K, T):
+    import torch
+    raw = S.gen_weight(t, N, K, 70 + N)
+    X = S.gen_activations(T, K, 71)
+    w = ctx.weight(t, raw, N, K)
+    Y = torch.full((T, N), float("nan"), device="cuda")
+    ctx.qgemm(w, torch.from_numpy(X).cuda(), Y, precision=1)
+    ctx.check_device_errors()
+    ref = X @ O.dequantize(t, raw, N * K).reshape(N, K).T
+    got = Y.cpu().numpy()
+    assert np.isfinite(got).all()
+    assert np.abs(got - ref).max() / np.abs(ref).max() <= TOL
+
+
+def test_qgemm_tc_prefill_2048(ctx):
+    import torch
+    t, N, K, T = S.GGML_Q5_0, 4864, 896, 2048
+    raw = S.gen_weight(t, N, K, 5)
+    X = S.gen_activations(T, K, 6)
+    w = ctx.weight(t, raw, N, K)
+    Y = torch.empty(T, N, device="cuda")
+    ctx.qgemm(w, torch.from_numpy(X).cuda(), Y, precision=1)
+    ctx.check_device_errors()
+    Yf = torch.empty(T, N, device="cuda")
+    ctx.qgemm(w, torch.from_numpy(X).cuda(), Yf, precision=0)   # exact-weight fp32 path
+    torch.cuda.synchronize()
+    ref = Yf.cpu().numpy()
+    assert np.abs(Y.cpu().numpy() - ref).max() / np.abs(ref).max() <= TOL
