@@ -29,7 +29,7 @@ EXPORTS = [
     "hd_weight_upload", "hd_weight_upload_device", "hd_weight_free", "hd_weight_info", "hd_weight_download",
     "hd_dequantize", "hd_qgemv", "hd_qgemv_swiglu", "hd_qgemv_host", "hd_qgemm", "hd_qgemm_host", "hd_matmul_f32",
     "hd_rmsnorm", "hd_rmsnorm_graph", "hd_rope_neox", "hd_rope_interleaved", "hd_softmax_rows", "hd_swiglu",
-    "hd_add", "hd_argmax_rows", "hd_embed", "hd_kv_append", "hd_attention_decode", "hd_attention_prefill",
+    "hd_add", "hd_argmax_rows", "hd_argmax_rows_noalloc", "hd_embed", "hd_kv_append", "hd_attention_decode", "hd_attention_prefill",
     "hd_dot_i8", "hd_fused_qdot_qadd_qacc_i8", "hd_decoder_create", "hd_decoder_free", "hd_decoder_generate",
 ]
 
@@ -67,6 +67,7 @@ def lib() -> C.CDLL:
         "hd_rope_neox": [V, V, V, I, I, I, F], "hd_rope_interleaved": [V, V, V, V, V, I64, I],
         "hd_softmax_rows": [V, V, I64, I], "hd_swiglu": [V, V, V, V, I64], "hd_add": [V, V, V, V, I64],
         "hd_argmax_rows": [V, V, I64, I64, V], "hd_embed": [V, V, V, I, V],
+        "hd_argmax_rows_noalloc": [V, I64, I64, V, V],
         "hd_kv_append": [V, V, V, V, V, V, I, I, I, I, I],
         "hd_attention_decode": [V, V, V, V, V, I, I, I, I, I, V],
         "hd_attention_prefill": [V, V, V, V, I, I, I, I, I, I, V],

@@ -157,6 +157,22 @@ int hd_add(hd_ctx *ctx, const float *a_dev, const float *b_dev, float *out_dev, 
 /* First index of each row's maximum, strict > (ArgMaxSampler::sample,
  * runtime/sampler/argmax.rs:8-24); 0 for n == 0. */
 int hd_argmax_rows(hd_ctx *ctx, const float *x_dev, int64_t rows, int64_t n, int32_t *idx_dev);
+/* Argmax of each row with no device allocation and no context.  It has no
+ * counterpart in the reference.  It is for callers that cannot let a library
+ * call cudaMalloc: runtimes that own all device memory through their own pool
+ * or arena, and latency-critical paths that cannot afford cudaMalloc's
+ * implicit synchronization.  Same result as hd_argmax_rows (first maximum
+ * wins, strict >; 0 for n == 0 or a NaN at index 0), enqueued on `stream` (a
+ * cudaStream_t; NULL = the legacy default stream) for the current device.
+ * Its scratch is one static device array of HD_ARGMAX_NOALLOC_SCRATCH_BYTES
+ * that each GPU loading the library keeps until exit.  rows above
+ * HD_ARGMAX_NOALLOC_MAX_ROWS are rejected with HD_E_SHAPE (n is not limited).
+ * The first call on a device looks up the array's device address
+ * (cudaGetSymbolAddress) and should come before any stream capture.  All
+ * calls share the array: calls that overlap on the GPU race. */
+#define HD_ARGMAX_NOALLOC_MAX_ROWS 4096
+#define HD_ARGMAX_NOALLOC_SCRATCH_BYTES 212992
+int hd_argmax_rows_noalloc(const float *x_dev, int64_t rows, int64_t n, int32_t *idx_dev, void *stream);
 /* Embedding rows dequantized from a quantized table (embedding_lookup,
  * core/tensor_ops/embedding.rs:4-17): ids outside [0, rows) give zeros.
  * out_dev [n][cols]. */
