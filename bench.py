@@ -142,6 +142,15 @@ def run_ours(args, rank, world, local):
 
     torch.cuda.set_device(local)
     ctx = hc.Context(local)
+    if args.only:
+        fns = {"prefill": lambda: prefill_workload(ctx, args), "dequant": lambda: dequant_workload(ctx),
+               "decode": lambda: decode_workload(ctx, args, rank, world),
+               "layer7b": lambda: layer7b_workload(ctx, args, rank, world)}
+        r = fns[args.only]()
+        if rank == 0:
+            print(json.dumps({"workload": args.only, "n_gpus": world, "result": r}), flush=True)
+        ctx.close()
+        return
     hbm, _, peak_kind = peaks()
     l2 = torch.cuda.get_device_properties(local).L2_cache_size
     # Weights: `copies` device copies per type, together > 3x L2 per case.
@@ -236,6 +245,18 @@ def run_ours(args, rank, world, local):
     if rank == 0 and world == 1 and not args.no_cpu:
         cpu = cpu_baseline_sample(raws, budget_s=args.cpu_seconds)
 
+    # Secondary workloads (outside the timed region of the headline).
+    extra = {}
+    if not args.no_extra:
+        for name, fn in (("prefill_qgemm", lambda: prefill_workload(ctx, args)),
+                         ("dequant_q8_0", lambda: dequant_workload(ctx)),
+                         ("decode_q05b", lambda: decode_workload(ctx, args, rank, world)),
+                         ("layer7b_sharded", lambda: layer7b_workload(ctx, args, rank, world))):
+            try:
+                extra[name] = fn()
+            except Exception as e:  # report, keep the headline
+                extra[name] = {"error": f"{type(e).__name__}: {e}"}
+
     res = {
         "metric": METRIC, "value": round(value, 1), "unit": "GB/s", "n_gpus": world, "steps": args.steps,
         "warmup": args.warmup, "ms_per_step": round(ms_all / args.steps, 4), "higher_is_better": True,
@@ -248,10 +269,210 @@ def run_ours(args, rank, world, local):
         "roofline": roofline, "breakdown": breakdown, "gpu_launches": launches,
         "e2e": e2e, "cpu_baseline": cpu, "clocks": clk.summary(),
         "wall_ms_timed_region": round(total_ms, 3),
+        "workloads": extra,
     }
     if rank == 0:
         print(json.dumps(res), flush=True)
     ctx.close()
+
+
+def _median(v):
+    return float(np.median(np.array(v)))
+
+
+def prefill_workload(ctx, args, reps=5):
+    """Config 3: prefill Q-GEMM, Q5_0 [4864 x 896] and Q4_K [896 x 4864] times
+    X [T x K] for T = 128, 512, 2048.  Each timed GEMM follows a 256 MB L2
+    flush; median of `reps` CUDA-event timings on the launching stream."""
+    import torch
+
+    _, bf16, kind = peaks()
+    flush = torch.empty(256 << 20, dtype=torch.uint8, device="cuda")
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    out = {"unit": "TFLOP/s", "peak_bf16_tflops": bf16, "peak_kind": kind, "l2_policy": "256 MB flush before each rep"}
+    for (t, N, K) in [(S.GGML_Q5_0, 4864, 896), (S.GGML_Q4_K, 896, 4864)]:
+        w = ctx.weight(t, S.gen_weight(t, N, K, seed=2 + t), N, K)
+        for T in (128, 512, 2048):
+            X = torch.from_numpy(S.gen_activations(T, K, 7)).cuda()
+            Y = torch.empty(T, N, device="cuda")
+            row = {}
+            for prec, nm in ((1, "bf16_tc"), (0, "fp32")):
+                for _ in range(2):
+                    ctx.qgemm(w, X, Y, precision=prec)
+                ts = []
+                for _ in range(reps):
+                    flush.zero_()
+                    e0.record()
+                    ctx.qgemm(w, X, Y, precision=prec)
+                    e1.record()
+                    torch.cuda.synchronize()
+                    ts.append(e0.elapsed_time(e1))
+                ms = _median(ts)
+                tf = 2.0 * T * N * K / (ms * 1e-3) / 1e12
+                row[nm] = {"ms": round(ms, 4), "tflops": round(tf, 2)}
+                if prec == 1:
+                    row[nm]["frac_of_bf16_peak"] = round(tf / bf16, 4)
+            ctx.check_device_errors()
+            out[f"{S.TYPE_NAME[t]}_{N}x{K}_T{T}"] = row
+    return out
+
+
+def dequant_workload(ctx, copies=160):
+    """Config 1: Q8_0 [896 x 896] full dequant (bit-exact f32 out) and its B=1
+    GEMV, rotating over `copies` weights and outputs (> L2)."""
+    import torch
+
+    hbm, _, kind = peaks()
+    t, N, K = S.GGML_Q8_0, 896, 896
+    raw = S.gen_weight(t, N, K, seed=1)
+    ws = [ctx.weight(t, raw, N, K) for _ in range(copies)]
+    outs = [torch.empty(N * K, device="cuda") for _ in range(copies)]
+    x = torch.from_numpy(S.gen_activations(1, K, 11)).cuda()
+    y = torch.empty(1, N, device="cuda")
+    res = {}
+    for nm, fn, byts in (("dequant", lambda i: ctx.dequantize(ws[i], outs[i]), S.nbytes(t, N, K) + 4 * N * K),
+                         ("gemv_b1", lambda i: ctx.qgemv(ws[i], x, y), S.nbytes(t, N, K) + 4 * K + 4 * N)):
+        for i in range(copies):
+            fn(i)
+        torch.cuda.synchronize()
+        g = torch.cuda.CUDAGraph()
+        s = torch.cuda.Stream()
+        with torch.cuda.graph(g, stream=s):
+            ctx.set_stream(torch.cuda.current_stream().cuda_stream)
+            for i in range(copies):
+                fn(i)
+        ctx.set_stream(torch.cuda.current_stream().cuda_stream)
+        for _ in range(3):
+            g.replay()
+        e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        e0.record()
+        for _ in range(10):
+            g.replay()
+        e1.record()
+        torch.cuda.synchronize()
+        us = e0.elapsed_time(e1) * 1e3 / (10 * copies)
+        res[nm] = {"us_per_launch": round(us, 3), "gbs": round(byts / (us * 1e-6) / 1e9, 1),
+                   "frac_of_hbm": round(byts / (us * 1e-6) / 1e9 / hbm, 4), "bytes_per_launch": byts}
+    for w in ws:
+        w.free()
+    res["peak_kind"] = kind
+    return res
+
+
+def decode_workload(ctx, args, rank, world):
+    """Config 4: Qwen2.5-0.5B-shaped decoder with random weights -- prefill 512
+    ids, greedy 128 tokens -- at batch 1, and 256 sequences split over the
+    ranks (replicated weights, no collective)."""
+    import hacedle_cuda as hc
+
+    hbm, _, kind = peaks()
+    model = S.gen_decoder(S.QWEN05B, seed=4)
+    n_prompt, n_gen = 512, 128
+    res = {"unit": "tokens/s", "n_prompt": n_prompt, "n_gen": n_gen, "peak_kind": kind}
+    w_bytes = 386_849_280  # packed weights + f32 bias/norm vectors read per decode step
+    seqs_list = [1] + ([max(1, args.decode_batch // world)] if args.decode_batch > 0 else [])
+    dec = hc.Decoder(ctx, model, max_ctx=n_prompt + n_gen, max_seqs=max(seqs_list))
+    for S_ in seqs_list:
+        prompts = np.stack([S.gen_prompt(n_prompt, S.QWEN05B["vocab"], seed=4 + s) for s in range(S_)])
+        prec = hc.PREC_FP32 if S_ == 1 else hc.PREC_BF16_TC
+        toks, dms, pms = dec.generate(prompts, n_gen, precision=prec)
+        step_ms = dms / (n_gen - 1)
+        tps = S_ * (n_gen - 1) / (dms * 1e-3)
+        ent = {"seqs_per_gpu": S_, "decode_ms": round(dms, 3), "ms_per_step": round(step_ms, 4),
+               "tokens_per_s_per_gpu": round(tps, 1), "tokens_per_s_all_gpus": round(tps * world, 1),
+               "prefill_ms": round(pms, 3), "prefill_precision": "fp32" if prec == hc.PREC_FP32 else "bf16_tc",
+               "weight_gbs_per_step": round(w_bytes / (step_ms * 1e-3) / 1e9, 1),
+               "frac_of_hbm": round(w_bytes / (step_ms * 1e-3) / 1e9 / hbm, 4)}
+        if S_ == 1:
+            gold = os.path.join(ROOT, "tests", "golden", "decoder_q05b_tokens.json")
+            if os.path.exists(gold):
+                ent["greedy_tokens_match_oracle"] = toks[0].tolist() == json.load(open(gold))["tokens"]
+        res[f"seqs{S_}"] = ent
+    dec.free()
+    return res
+
+
+def layer7b_workload(ctx, args, rank, world, reps=5):
+    """Config 5: the seven projections of a Qwen2.5-7B-shaped layer (q/k/v/o and
+    gate/up Q4_K, down Q6_K), output rows sharded over the ranks.  Each rank
+    computes its rows (GEMV at B=1, tcgen05 GEMM at B=64 and 512), then the
+    outputs are all-gathered over NVLink (NCCL) and reassembled on the device.
+    Total work is fixed (strong scaling); times are max over ranks, after a
+    256 MB L2 flush before every rep."""
+    import torch
+
+    import hacedle_cuda as hc
+    from hacedle_cuda import shard
+
+    hbm, bf16, kind = peaks()
+    H, F, nq, nkv = 3584, 18944, 28 * 128, 4 * 128
+    mats = [("q", S.GGML_Q4_K, nq, H), ("k", S.GGML_Q4_K, nkv, H), ("v", S.GGML_Q4_K, nkv, H),
+            ("o", S.GGML_Q4_K, H, nq), ("gate", S.GGML_Q4_K, F, H), ("up", S.GGML_Q4_K, F, H),
+            ("down", S.GGML_Q6_K, H, F)]
+    ws = []
+    for i, (nm, t, N, K) in enumerate(mats):
+        raw = S.gen_weight(t, N, K, seed=50 + i)
+        ws.append((nm, t, N, K, ctx.weight(t, shard.row_slice(raw, t, N, K, rank, world), N // world, K)))
+    w_total = sum(S.nbytes(t, N, K) for _, t, N, K in mats)
+    flops_per_tok = sum(2 * N * K for _, t, N, K in mats)
+    flush = torch.empty(256 << 20, dtype=torch.uint8, device="cuda")
+    res = {"scaling": "strong", "ranks": world, "weight_bytes_layer": w_total, "peak_kind": kind,
+           "exchange": "NCCL all_gather_into_tensor (torch.distributed) + hd_gather_columns" if world > 1 else "none"}
+    for B in (1, 64, 512):
+        xs = {K: torch.from_numpy(S.gen_activations(B, K, 60)).cuda() for K in (H, F)}
+        ys = [torch.empty(B, N // world, device="cuda") for _, _, N, _, _ in ws]
+        gath = [torch.empty(world, B, N // world, device="cuda") for _, _, N, _, _ in ws]
+        full = [torch.empty(B, N, device="cuda") for _, _, N, _, _ in ws]
+
+        def compute():
+            for (nm, t, N, K, w), y in zip(ws, ys):
+                if B <= 16:
+                    ctx.qgemv(w, xs[K], y)
+                else:
+                    ctx.qgemm(w, xs[K], y, precision=hc.PREC_BF16_TC)
+
+        def exchange():
+            import torch.distributed as dist
+            for (nm, t, N, K, w), y, g, f in zip(ws, ys, gath, full):
+                if world > 1:
+                    dist.all_gather_into_tensor(g.view(-1), y.view(-1))
+                    ctx.gather_columns(g, f, world, B, N // world)
+                else:
+                    f.copy_(y)
+
+        for _ in range(2):
+            compute()
+            exchange()
+        torch.cuda.synchronize()
+        c_ms, t_ms = [], []
+        ev = [torch.cuda.Event(enable_timing=True) for _ in range(3)]
+        for _ in range(reps):
+            flush.zero_()
+            barrier(world)
+            ev[0].record()
+            compute()
+            ev[1].record()
+            exchange()
+            ev[2].record()
+            torch.cuda.synchronize()
+            c_ms.append(ev[0].elapsed_time(ev[1]))
+            t_ms.append(ev[0].elapsed_time(ev[2]))
+        ctx.check_device_errors()
+        cm = max_over_ranks(_median(c_ms), world)
+        tm = max_over_ranks(_median(t_ms), world)
+        ent = {"compute_ms": round(cm, 4), "exchange_ms": round(tm - cm, 4), "total_ms": round(tm, 4),
+               "allgather_bytes": int(4 * B * sum(N for _, _, N, _ in mats) * (world - 1) // world)}
+        if B == 1:
+            ent["gbs"] = round(w_total / (tm * 1e-3) / 1e9, 1)
+            ent["compute_gbs_per_gpu"] = round(w_total / world / (cm * 1e-3) / 1e9, 1)
+            ent["frac_of_hbm_compute"] = round(w_total / world / (cm * 1e-3) / 1e9 / hbm, 4)
+        else:
+            ent["tflops"] = round(flops_per_tok * B / (tm * 1e-3) / 1e12, 2)
+            ent["compute_tflops_per_gpu"] = round(flops_per_tok * B / world / (cm * 1e-3) / 1e12, 2)
+        res[f"B{B}"] = ent
+    for *_, w in ws:
+        w.free()
+    return res
 
 
 def e2e_host(ctx, weights, args):
@@ -347,6 +568,10 @@ def main():
     ap.add_argument("--cpu-seconds", type=float, default=10.0)
     ap.add_argument("--no-cpu", action="store_true")
     ap.add_argument("--no-e2e", action="store_true")
+    ap.add_argument("--no-extra", action="store_true", help="headline GEMV sweep only")
+    ap.add_argument("--only", choices=["prefill", "dequant", "decode", "layer7b"], help="run one secondary workload")
+    ap.add_argument("--decode-batch", type=int, default=256,
+                    help="sequences decoded together, split over the ranks (0: batch 1 only)")
     args = ap.parse_args()
     args.warmup = max(args.warmup, 3) if args.impl == "ours" else args.warmup
     if args.impl == "reference":

@@ -3,11 +3,15 @@
 // Cache layout [seq][max_ctx][n_kv][head_dim] f32, the KvCache layout of
 // core/ops/block.rs:241-282 with a leading sequence index.
 //
-// One CTA per (query row, kv head) serves the n_heads/n_kv query heads that
-// share that kv head, so every K/V row is read once for all of them.  Scores
-// go to shared memory, softmax is the exact two-pass form of
-// NativeBackend::softmax (max, sum of exp, exp/sum), then each thread sums
-// p_i * v_i[d] over positions for its (head, d) outputs.
+// A CTA serves the rep = n_heads/n_kv query heads that share one kv head, so
+// each K/V row is read once for all of them, over a range of 64-position
+// chunks: K and V chunks are staged in shared memory, scores are full
+// head_dim dot products, and the softmax runs online across chunks (running
+// max, rescaled sum and output).  For decode, where there are few query rows,
+// a row's positions are split over P CTAs; each writes its (max, sum, output)
+// partial to the workspace and the last to arrive (atomic ticket) combines
+// them in chunk order, so the result is deterministic.  The result equals
+// NativeBackend::softmax followed by sum_i p_i v_i up to rounding order.
 #include "hd_internal.cuh"
 
 namespace {
@@ -33,83 +37,169 @@ __global__ void k_kv_append(const float *__restrict__ k, const float *__restrict
 //   decode  (lens != null): cseq = r, len = lens[r]
 //   prefill (lens == null): rows are seqT consecutive tokens per sequence,
 //                           cseq = r / seqT, len = pos0 + r % seqT + 1
+constexpr int CH = 64;     // positions per chunk
+constexpr int ANT = 128;   // threads per CTA
+constexpr int MAXREP = 16;
+
 template <int HD>
-__global__ void __launch_bounds__(128) k_attention(const float *__restrict__ q, const float *__restrict__ kc,
+__global__ void __launch_bounds__(ANT) k_attention(const float *__restrict__ q, const float *__restrict__ kc,
                                                    const float *__restrict__ vc, const int32_t *__restrict__ lens,
                                                    int pos0, int seqT, int n_heads, int n_kv, int max_ctx,
-                                                   float scale, float *__restrict__ out) {
+                                                   float scale, int P, int cpc, float *ws, int *tickets,
+                                                   float *__restrict__ out) {
     extern __shared__ float sm[];
+    constexpr int KP = HD + 1;                      // padded K row
+    constexpr int OPT = (MAXREP * HD + ANT - 1) / ANT;
     pdl_wait();
     pdl_trigger();
-    const int r = blockIdx.x, kvh = blockIdx.y;
+    const int r = blockIdx.x, kvh = blockIdx.y, p = blockIdx.z;
     const int rep = n_heads / n_kv, h0 = kvh * rep;
     const int cseq = lens ? r : r / seqT;
     int L = lens ? lens[r] : pos0 + r % seqT + 1;
     L = L < 0 ? 0 : L > max_ctx ? max_ctx : L;
-    float *qs = sm;               // [rep][HD]
-    float *sc = sm + rep * HD;    // [rep][L]
+    const int nchunks = (L + CH - 1) / CH;
+    const int Pr = nchunks == 0 ? 1 : (nchunks + cpc - 1) / cpc;
+    if (p >= Pr) return;
     const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
+    float *qs = sm;                                        // [rep][KP]
+    float *Ks = qs + rep * KP;                             // [CH][KP]
+    float *Vs = sm + ((rep * KP + CH * KP + 3) & ~3);      // [CH][HD], 16-byte aligned for float4 stores
+    float *S = Vs + CH * HD;                               // [rep][CH]
+    float *mrun = S + rep * CH, *lrun = mrun + MAXREP, *alpha = lrun + MAXREP;
     const float *qr = q + ((int64_t)r * n_heads + h0) * HD;
-    for (int i = tid; i < rep * HD; i += 128) qs[i] = qr[i];
-    __syncthreads();
+    for (int i = tid; i < rep * HD; i += ANT) qs[(i / HD) * KP + i % HD] = qr[i];
+    if (tid < rep) {
+        mrun[tid] = -INFINITY;
+        lrun[tid] = 0.f;
+    }
+    const int npairs = rep * HD;
+    float o[OPT];
+#pragma unroll
+    for (int k = 0; k < OPT; k++) o[k] = 0.f;
     const int64_t cbase = (int64_t)cseq * max_ctx;
-    constexpr int PL = HD / 32;  // dims per lane
-    for (int p = warp; p < L; p += 4) {
-        const float *kp = kc + ((cbase + p) * n_kv + kvh) * HD;
-        float kv[PL];
+    const int c1 = min(nchunks, (p + 1) * cpc);
+    for (int c = p * cpc; c < c1; c++) {
+        const int j0 = c * CH, nj = min(CH, L - j0);
+        __syncthreads();
+        for (int i = tid; i < nj * (HD / 4); i += ANT) {
+            const int j = i / (HD / 4), d4 = i % (HD / 4);
+            const int64_t g = ((cbase + j0 + j) * n_kv + kvh) * HD + 4 * d4;
+            const float4 kv = *(const float4 *)(kc + g), vv = *(const float4 *)(vc + g);
+            float *kd = Ks + j * KP + 4 * d4;
+            kd[0] = kv.x; kd[1] = kv.y; kd[2] = kv.z; kd[3] = kv.w;
+            *(float4 *)(Vs + j * HD + 4 * d4) = vv;
+        }
+        __syncthreads();
+        for (int i = tid; i < rep * nj; i += ANT) {
+            const int h = i / nj, j = i % nj;
+            const float *qh = qs + h * KP, *kj = Ks + j * KP;
+            float sc = 0.f;
+#pragma unroll 16
+            for (int d = 0; d < HD; d++) sc = fmaf(qh[d], kj[d], sc);
+            S[h * CH + j] = __fdiv_rn(sc, scale);
+        }
+        __syncthreads();
+        for (int h = warp; h < rep; h += ANT / 32) {
+            float *row = S + h * CH;
+            float mc = -INFINITY;
+            for (int j = lane; j < nj; j += 32) mc = fmaxf(mc, row[j]);
 #pragma unroll
-        for (int j = 0; j < PL; j++) kv[j] = kp[lane + 32 * j];
-        for (int h = 0; h < rep; h++) {
-            float s = 0.f;
+            for (int off = 16; off > 0; off >>= 1) mc = fmaxf(mc, __shfl_xor_sync(0xffffffffu, mc, off));
+            const float mold = mrun[h], mnew = fmaxf(mold, mc);
+            float sum = 0.f;
+            for (int j = lane; j < nj; j += 32) {
+                const float e = expf(row[j] - mnew);
+                row[j] = e;
+                sum += e;
+            }
 #pragma unroll
-            for (int j = 0; j < PL; j++) s = fmaf(qs[h * HD + lane + 32 * j], kv[j], s);
+            for (int off = 16; off > 0; off >>= 1) sum += __shfl_xor_sync(0xffffffffu, sum, off);
+            __syncwarp();
+            if (lane == 0) {
+                const float a = mold == -INFINITY ? 0.f : expf(mold - mnew);
+                alpha[h] = a;
+                lrun[h] = lrun[h] * a + sum;
+                mrun[h] = mnew;
+            }
+        }
+        __syncthreads();
 #pragma unroll
-            for (int o = 16; o > 0; o >>= 1) s += __shfl_xor_sync(0xffffffffu, s, o);
-            if (lane == 0) sc[h * L + p] = __fdiv_rn(s, scale);
+        for (int k = 0; k < OPT; k++) {
+            const int i = tid + k * ANT;
+            if (i < npairs) {
+                const int h = i / HD, d = i % HD;
+                const float *ph = S + h * CH;
+                float acc = o[k] * alpha[h];
+                for (int j = 0; j < nj; j++) acc = fmaf(ph[j], Vs[j * HD + d], acc);
+                o[k] = acc;
+            }
         }
     }
     __syncthreads();
-    for (int h = warp; h < rep; h += 4) {
-        float *row = sc + h * L;
-        float m = -INFINITY;
-        for (int p = lane; p < L; p += 32) m = fmaxf(m, row[p]);
+    if (Pr == 1) {
 #pragma unroll
-        for (int o = 16; o > 0; o >>= 1) m = fmaxf(m, __shfl_xor_sync(0xffffffffu, m, o));
-        float s = 0.f;
-        for (int p = lane; p < L; p += 32) s += expf(row[p] - m);
-#pragma unroll
-        for (int o = 16; o > 0; o >>= 1) s += __shfl_xor_sync(0xffffffffu, s, o);
-        for (int p = lane; p < L; p += 32) row[p] = expf(row[p] - m) / s;
+        for (int k = 0; k < OPT; k++) {
+            const int i = tid + k * ANT;
+            if (i < npairs) {
+                const int h = i / HD, d = i % HD;
+                out[((int64_t)r * n_heads + h0 + h) * HD + d] = L > 0 ? o[k] / lrun[h] : 0.f;
+            }
+        }
+        return;
     }
+    // Split row: publish (max, sum, output) and let the last CTA combine.
+    const int W = HD + 2;
+    float *part = ws + (((int64_t)r * n_kv + kvh) * P) * rep * W;
+#pragma unroll
+    for (int k = 0; k < OPT; k++) {
+        const int i = tid + k * ANT;
+        if (i < npairs) __stcg(part + (int64_t)p * rep * W + (i / HD) * W + i % HD, o[k]);
+    }
+    if (tid < rep) {
+        __stcg(part + (int64_t)p * rep * W + tid * W + HD, mrun[tid]);
+        __stcg(part + (int64_t)p * rep * W + tid * W + HD + 1, lrun[tid]);
+    }
+    __threadfence();
     __syncthreads();
-    for (int i = tid; i < rep * HD; i += 128) {
+    __shared__ int last;
+    if (tid == 0) last = (atomicAdd(tickets + r * n_kv + kvh, 1) == Pr - 1);
+    __syncthreads();
+    if (!last) return;
+    __threadfence();
+    for (int i = tid; i < npairs; i += ANT) {
         const int h = i / HD, d = i % HD;
-        const float *pr = sc + h * L;
-        const float *vp = vc + (cbase * n_kv + kvh) * HD + d;
-        float s0 = 0.f, s1 = 0.f;
-        int p = 0;
-        for (; p + 1 < L; p += 2) {
-            s0 = fmaf(pr[p], vp[(int64_t)p * n_kv * HD], s0);
-            s1 = fmaf(pr[p + 1], vp[(int64_t)(p + 1) * n_kv * HD], s1);
+        float M = -INFINITY;
+        for (int pp = 0; pp < Pr; pp++) M = fmaxf(M, __ldcg(part + (int64_t)pp * rep * W + h * W + HD));
+        float O = 0.f, Ls = 0.f;
+        for (int pp = 0; pp < Pr; pp++) {
+            const float *pt = part + (int64_t)pp * rep * W + h * W;
+            const float e = expf(__ldcg(pt + HD) - M);
+            O = fmaf(__ldcg(pt + d), e, O);
+            Ls = fmaf(__ldcg(pt + HD + 1), e, Ls);
         }
-        if (p < L) s0 = fmaf(pr[p], vp[(int64_t)p * n_kv * HD], s0);
-        out[((int64_t)r * n_heads + h0 + h) * HD + d] = s0 + s1;
+        out[((int64_t)r * n_heads + h0 + h) * HD + d] = O / Ls;
     }
+    if (tid == 0) tickets[r * n_kv + kvh] = 0;
 }
 
 template <int HD>
-cudaError_t launch_attn(hd_ctx *ctx, int rows, int n_heads, int n_kv, int maxlen, const float *q, const float *kc,
-                        const float *vc, const int32_t *lens, int pos0, int seqT, int max_ctx, float *out) {
-    int rep = n_heads / n_kv;
-    size_t smem = (size_t)rep * (HD + maxlen) * sizeof(float);
+size_t attn_smem(int rep) {
+    return (size_t)(((rep * (HD + 1) + CH * (HD + 1) + 3) & ~3) + CH * HD + rep * CH + 3 * MAXREP) * sizeof(float);
+}
+
+template <int HD>
+cudaError_t launch_attn(hd_ctx *ctx, int rows, int n_heads, int n_kv, int P, int cpc, const float *q,
+                        const float *kc, const float *vc, const int32_t *lens, int pos0, int seqT, int max_ctx,
+                        float *out) {
+    const int rep = n_heads / n_kv;
+    const size_t smem = attn_smem<HD>(rep);
     if (smem > 48 * 1024) {
-        cudaError_t e = cudaFuncSetAttribute(k_attention<HD>, cudaFuncAttributeMaxDynamicSharedMemorySize,
-                                             (int)smem);
+        cudaError_t e = cudaFuncSetAttribute(k_attention<HD>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
         if (e != cudaSuccess) return e;
     }
-    float scale = sqrtf((float)HD);
-    return hd_launch(ctx, k_attention<HD>, dim3(rows, n_kv), dim3(128), smem, q, kc, vc, lens, pos0, seqT, n_heads,
-                     n_kv, max_ctx, scale, out);
+    const float scale = sqrtf((float)HD);
+    return hd_launch(ctx, k_attention<HD>, dim3(rows, n_kv, P), dim3(ANT), smem, q, kc, vc, lens, pos0, seqT,
+                     n_heads, n_kv, max_ctx, scale, P, cpc, (float *)ctx->ws, ctx->tickets, out);
 }
 
 }  // namespace
@@ -118,18 +208,32 @@ int hd_attention_run(hd_ctx *ctx, const float *q, const float *kc, const float *
                      int pos0, int seqT, int n_heads, int n_kv, int hd, int max_ctx, int maxlen, float *out,
                      const char *name) {
     if (!ctx || !q || !kc || !vc || !out) return hd_fail(ctx, HD_E_ARG, "%s: null argument", name);
-    HD_REQUIRE(ctx, n_heads > 0 && n_kv > 0 && n_heads % n_kv == 0, HD_E_SHAPE,
-               "%s: n_heads %d is not a multiple of n_kv %d", name, n_heads, n_kv);
+    HD_REQUIRE(ctx, n_heads > 0 && n_kv > 0 && n_heads % n_kv == 0 && n_heads / n_kv <= MAXREP, HD_E_SHAPE,
+               "%s: n_heads %d must be a multiple of n_kv %d, at most %d per kv head", name, n_heads, n_kv, MAXREP);
     HD_REQUIRE(ctx, max_ctx > 0 && maxlen <= max_ctx, HD_E_SHAPE, "%s: length beyond max_ctx", name);
-    size_t smem = (size_t)(n_heads / n_kv) * (hd + maxlen) * sizeof(float);
-    HD_REQUIRE(ctx, smem <= 200 * 1024, HD_E_UNSUPPORTED, "%s: %d positions x %d heads exceed shared memory", name,
-               maxlen, n_heads / n_kv);
+    HD_REQUIRE(ctx, hd == 32 || hd == 64 || hd == 128, HD_E_UNSUPPORTED, "%s: head_dim %d (32, 64 or 128)", name, hd);
     if (rows == 0) return HD_OK;
+    // Decode: split positions so that about two CTAs per SM are busy.
+    const int maxchunks = (maxlen + CH - 1) / CH > 0 ? (maxlen + CH - 1) / CH : 1;
+    int P = 1;
+    if (lens) {
+        const int64_t ctas = (int64_t)rows * n_kv;
+        const int64_t want = (2 * (int64_t)ctx->sm_count + ctas - 1) / ctas;
+        P = (int)(want < maxchunks ? want : maxchunks);
+        if (P < 1) P = 1;
+    }
+    const int cpc = (maxchunks + P - 1) / P;
+    P = (maxchunks + cpc - 1) / cpc;
+    HD_REQUIRE(ctx, P <= 65535, HD_E_SHAPE, "%s: too many position splits", name);
+    if (P > 1) {
+        const size_t need = (size_t)rows * n_kv * P * (n_heads / n_kv) * (hd + 2) * sizeof(float);
+        int rc = hd_ensure_workspace(ctx, need, (size_t)rows * n_kv);
+        if (rc) return rc;
+    }
     cudaError_t e;
-    if (hd == 64) e = launch_attn<64>(ctx, rows, n_heads, n_kv, maxlen, q, kc, vc, lens, pos0, seqT, max_ctx, out);
-    else if (hd == 128) e = launch_attn<128>(ctx, rows, n_heads, n_kv, maxlen, q, kc, vc, lens, pos0, seqT, max_ctx, out);
-    else if (hd == 32) e = launch_attn<32>(ctx, rows, n_heads, n_kv, maxlen, q, kc, vc, lens, pos0, seqT, max_ctx, out);
-    else return hd_fail(ctx, HD_E_UNSUPPORTED, "%s: head_dim %d (32, 64 or 128 supported)", name, hd);
+    if (hd == 64) e = launch_attn<64>(ctx, rows, n_heads, n_kv, P, cpc, q, kc, vc, lens, pos0, seqT, max_ctx, out);
+    else if (hd == 128) e = launch_attn<128>(ctx, rows, n_heads, n_kv, P, cpc, q, kc, vc, lens, pos0, seqT, max_ctx, out);
+    else e = launch_attn<32>(ctx, rows, n_heads, n_kv, P, cpc, q, kc, vc, lens, pos0, seqT, max_ctx, out);
     if (e != cudaSuccess) return hd_fail(ctx, HD_E_CUDA, "%s: %s", name, cudaGetErrorString(e));
     return HD_OK;
 }

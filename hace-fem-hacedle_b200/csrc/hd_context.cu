@@ -1,6 +1,7 @@
 // hd_context.cu -- context lifetime, errors, workspace and launch accounting.
 #include <cstdarg>
 #include <cstdio>
+#include <cstdlib>
 #include <cmath>
 #include <vector>
 
@@ -44,6 +45,9 @@ extern "C" int hd_ctx_create(int device, hd_ctx **out) {
         return HD_E_CUDA;
     }
     c->stream = c->own_stream;
+    // HACEDLE_PDL=0 turns programmatic dependent launch off (plain stream order).
+    const char *pdl = getenv("HACEDLE_PDL");
+    c->pdl = !(pdl && pdl[0] == '0');
     if (cudaMalloc(&c->flag, 64) != cudaSuccess || cudaMemset(c->flag, 0, 64) != cudaSuccess) {
         cudaStreamDestroy(c->own_stream);
         delete c;
@@ -64,6 +68,7 @@ extern "C" int hd_ctx_destroy(hd_ctx *ctx) {
     cudaFree(ctx->hbuf_y);
     cudaFree(ctx->flag);
     cudaFree(ctx->scratch);
+    cudaFree(ctx->xbf);
     if (ctx->own_stream) cudaStreamDestroy(ctx->own_stream);
     delete ctx;
     return HD_OK;

@@ -305,11 +305,17 @@ extern "C" int hd_decoder_generate(hd_decoder *d, const int32_t *prompts, int S,
     }
     std::vector<int32_t> hp(R);
     for (int i = 0; i < R; i++) hp[i] = i % n_prompt;
-    cudaStream_t st = ctx->stream;
+    // Work runs on the context's own non-blocking stream, ordered after the
+    // caller's stream: stream capture is not allowed on the legacy default
+    // stream, which a caller may have selected.
+    cudaStream_t user = ctx->stream, st = ctx->own_stream;
     cudaEvent_t e0, e1, e2;
     cudaEventCreate(&e0);
     cudaEventCreate(&e1);
     cudaEventCreate(&e2);
+    cudaEventRecord(e0, user);
+    cudaStreamWaitEvent(st, e0, 0);
+    ctx->stream = st;
     cudaGraph_t graph = nullptr;
     cudaGraphExec_t exec = nullptr;
     float t_pre = 0.f, t_dec = 0.f;
@@ -355,6 +361,7 @@ extern "C" int hd_decoder_generate(hd_decoder *d, const int32_t *prompts, int S,
             }
             rc = decode_step(d, S, n_gen, HD_PREC_FP32);
             cudaError_t ce = cudaStreamEndCapture(st, &graph);
+            cudaGetLastError();
             if (rc) break;
             if (ce != cudaSuccess || cudaGraphInstantiate(&exec, graph, 0) != cudaSuccess) {
                 rc = hd_fail(ctx, HD_E_CUDA, "hd_decoder_generate: graph: %s", cudaGetErrorString(ce));
@@ -380,6 +387,7 @@ extern "C" int hd_decoder_generate(hd_decoder *d, const int32_t *prompts, int S,
     if (exec) cudaGraphExecDestroy(exec);
     if (graph) cudaGraphDestroy(graph);
     cudaStreamSynchronize(st);
+    ctx->stream = user;
     cudaEventDestroy(e0);
     cudaEventDestroy(e1);
     cudaEventDestroy(e2);

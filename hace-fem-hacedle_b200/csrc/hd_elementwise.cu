@@ -216,6 +216,17 @@ __global__ void __launch_bounds__(NT) k_argmax(const float *__restrict__ x, int6
     }
 }
 
+__global__ void k_gather_columns(const float *__restrict__ src, float *__restrict__ dst, int G, int B, int64_t n) {
+    pdl_wait();
+    pdl_trigger();
+    int64_t i = (int64_t)blockIdx.x * blockDim.x + threadIdx.x;
+    int64_t total = (int64_t)G * B * n;
+    if (i >= total) return;
+    int64_t j = i % n, gb = i / n;
+    int b = (int)(gb % B), g = (int)(gb / B);
+    dst[(int64_t)b * G * n + (int64_t)g * n + j] = src[i];
+}
+
 inline unsigned blocks_for(int64_t n, int nt) { return (unsigned)((n + nt - 1) / nt); }
 
 }  // namespace
@@ -308,5 +319,13 @@ extern "C" int hd_argmax_rows(hd_ctx *ctx, const float *x, int64_t rows, int64_t
     int64_t *pi = (int64_t *)(pv + ((rows * nc + 1) & ~(int64_t)1));
     HD_CUDA_TRY(ctx, hd_launch(ctx, k_argmax<256>, dim3((unsigned)nc, (unsigned)rows), dim3(256), 0, x, n, chunk, pv,
                                pi, ctx->tickets, idx));
+    return HD_OK;
+}
+
+extern "C" int hd_gather_columns(hd_ctx *ctx, const float *src, float *dst, int G, int B, int64_t n) {
+    if (!ctx || !src || !dst) return hd_fail(ctx, HD_E_ARG, "hd_gather_columns: null argument");
+    HD_REQUIRE(ctx, G > 0 && B > 0 && n > 0, HD_E_SHAPE, "hd_gather_columns: bad shape");
+    int64_t total = (int64_t)G * B * n;
+    HD_CUDA_TRY(ctx, hd_launch(ctx, k_gather_columns, dim3(blocks_for(total, 256)), dim3(256), 0, src, dst, G, B, n));
     return HD_OK;
 }

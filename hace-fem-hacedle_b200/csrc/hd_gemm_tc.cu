@@ -25,6 +25,8 @@
 // waiting; the MMA warp always commits the accumulator barrier so that the
 // epilogue's wait also covers any MMAs still in flight, and TMEM is freed
 // before exit on every path.
+#include <cuda.h>
+
 #include "hd_internal.cuh"
 
 namespace {
@@ -334,16 +336,358 @@ cudaError_t launch_tc(hd_ctx *ctx, const hd_weight *w, const float *X, float *Y,
                      (int)w->cols, ctx->flag);
 }
 
+
+// ------------------------------------------------------------------- v2
+// Same MMA/TMEM structure, with every operand streamed asynchronously:
+// activations are converted to bf16 once and arrive by TMA (2-D tiled copy,
+// SWIZZLE_128B, straight into the layout the MMA reads); the raw quantized
+// bytes of each 128-row x 2-unit stage arrive by 1-D bulk copies, STAGES
+// ahead of use.  Eight warps dequantize shared -> shared (raw bytes -> bf16
+// swizzled rows), one warp issues the copies, one warp owns TMEM and the
+// MMAs.  Requires rows % 128 == 0 (every bulk copy is a whole, 16-byte
+// aligned span of 128 rows); other shapes use the v1 kernel above.
+
+template <int TYPE>
+struct Raw {
+    // byte offsets inside a stage's raw region (unit h = 0/1 of the pair)
+    static constexpr int Q = 0;                                        // q[h]
+    static constexpr int QB = TYPE == HD_TYPE_Q8_0 ? 4096 : 2048;      // bytes per unit of q (128 rows)
+    static constexpr int AUX = 2 * QB;                                 // Q5_0 qh[h] 512 B, Q6_K highs[h] 1 KB
+    static constexpr int AUXB = TYPE == HD_TYPE_Q5_0 ? 512 : TYPE == HD_TYPE_Q6_K ? 1024 : 0;
+    static constexpr int META = AUX + 2 * AUXB;                        // Q8_0/Q5_0 d[h] 256 B; Q4_K/Q6_K 2 KB per sb
+    static constexpr int METAB = (TYPE == HD_TYPE_Q8_0 || TYPE == HD_TYPE_Q5_0) ? 256 : 2048;
+    static constexpr int METAN = (TYPE == HD_TYPE_Q8_0 || TYPE == HD_TYPE_Q5_0) ? 2 : 1;
+    static constexpr int DSB = META + METAN * METAB;                   // Q6_K d 256 B
+    static constexpr int END = DSB + (TYPE == HD_TYPE_Q6_K ? 256 : 0);
+    static constexpr int BYTES = (END + 1023) & ~1023;
+};
+
+__device__ __forceinline__ void bulk_g2s(uint32_t dst, const void *src, uint32_t bytes, uint32_t bar) {
+    asm volatile("cp.async.bulk.shared::cluster.global.mbarrier::complete_tx::bytes [%0], [%1], %2, [%3];" ::"r"(dst),
+                 "l"(src), "r"(bytes), "r"(bar)
+                 : "memory");
+}
+__device__ __forceinline__ void tma_2d(uint32_t dst, const CUtensorMap *tm, int x, int y, uint32_t bar) {
+    asm volatile(
+        "cp.async.bulk.tensor.2d.shared::cluster.global.mbarrier::complete_tx::bytes [%0], [%1, {%2, %3}], [%4];" ::"r"(
+            dst),
+        "l"((uint64_t)tm), "r"(x), "r"(y), "r"(bar)
+        : "memory");
+}
+__device__ __forceinline__ void mbar_expect_tx(uint32_t bar, uint32_t bytes) {
+    asm volatile("mbarrier.arrive.expect_tx.shared::cta.b64 _, [%0], %1;" ::"r"(bar), "r"(bytes) : "memory");
+}
+
+// 32 values of unit u (pair half h) of row r from a stage's raw bytes.
+template <int TYPE>
+__device__ __forceinline__ void raw_values(const uint8_t *raw, int r, int h, int u, float (&v)[32]) {
+    using R = Raw<TYPE>;
+    if constexpr (TYPE == HD_TYPE_Q8_0) {
+        const uint4 *p = (const uint4 *)(raw + R::Q + h * R::QB + r * 32);
+        uint4 a = p[0], b = p[1];
+        float d = h2f(*(const uint16_t *)(raw + R::META + h * R::METAB + r * 2));
+        uint32_t wd[8] = {a.x, a.y, a.z, a.w, b.x, b.y, b.z, b.w};
+#pragma unroll
+        for (int i = 0; i < 8; i++) {
+            uint32_t x = wd[i] ^ 0x80808080u;
+#pragma unroll
+            for (int c = 0; c < 4; c++) v[4 * i + c] = (mag(x, c) - 8388736.0f) * d;
+        }
+    } else if constexpr (TYPE == HD_TYPE_Q5_0) {
+        uint4 a = *(const uint4 *)(raw + R::Q + h * R::QB + r * 16);
+        uint32_t qh = *(const uint32_t *)(raw + R::AUX + h * R::AUXB + r * 4);
+        float d = h2f(*(const uint16_t *)(raw + R::META + h * R::METAB + r * 2));
+        uint32_t wd[4] = {a.x, a.y, a.z, a.w};
+#pragma unroll
+        for (int i = 0; i < 4; i++) {
+            uint32_t lo = (wd[i] & 0x0F0F0F0Fu) | ((qh >> i) & 0x10101010u);
+            uint32_t hi = ((wd[i] >> 4) & 0x0F0F0F0Fu) | ((qh << (4 - i)) & 0x10101010u);
+#pragma unroll
+            for (int c = 0; c < 4; c++) {
+                v[4 * i + c] = (mag(lo, c) - 8388624.0f) * d;
+                v[16 + 4 * i + c] = (mag(hi, c) - 8388624.0f) * d;
+            }
+        }
+    } else if constexpr (TYPE == HD_TYPE_Q4_K) {
+        uint4 a = *(const uint4 *)(raw + R::Q + h * R::QB + r * 16);
+        uint4 m = *(const uint4 *)(raw + R::META + r * 16);
+        int sc, mn;
+        q4k_sm_regs(u & 7, m.y, m.z, m.w, sc, mn);
+        float d1 = h2f((uint16_t)(m.x & 0xFFFF)) * (float)sc, m1 = h2f((uint16_t)(m.x >> 16)) * (float)mn;
+        uint32_t wd[4] = {a.x, a.y, a.z, a.w};
+#pragma unroll
+        for (int i = 0; i < 4; i++) {
+            uint32_t lo = wd[i] & 0x0F0F0F0Fu, hi = (wd[i] >> 4) & 0x0F0F0F0Fu;
+#pragma unroll
+            for (int c = 0; c < 4; c++) {
+                v[4 * i + c] = (mag(lo, c) - 8388608.0f) * d1 - m1;
+                v[16 + 4 * i + c] = (mag(hi, c) - 8388608.0f) * d1 - m1;
+            }
+        }
+    } else {
+        uint4 a = *(const uint4 *)(raw + R::Q + h * R::QB + r * 16);
+        uint2 hb = *(const uint2 *)(raw + R::AUX + h * R::AUXB + r * 8);
+        const int8_t *scp = (const int8_t *)(raw + R::META + r * 16);
+        float d = h2f(*(const uint16_t *)(raw + R::DSB + r * 2));
+        int s0 = 2 * (u & 7);
+        float dl = d * (float)scp[s0], dh = d * (float)scp[s0 + 1];
+        uint32_t wd[4] = {a.x, a.y, a.z, a.w};
+#pragma unroll
+        for (int i = 0; i < 4; i++) {
+            int sh = 4 - 2 * i;
+            uint32_t hx = sh >= 0 ? (hb.x << sh) : (hb.x >> -sh), hy = sh >= 0 ? (hb.y << sh) : (hb.y >> -sh);
+            uint32_t lo = (wd[i] & 0x0F0F0F0Fu) | (hx & 0x30303030u);
+            uint32_t hi = ((wd[i] >> 4) & 0x0F0F0F0Fu) | (hy & 0x30303030u);
+#pragma unroll
+            for (int c = 0; c < 4; c++) {
+                v[4 * i + c] = (mag(lo, c) - 8388640.0f) * dl;
+                v[16 + 4 * i + c] = (mag(hi, c) - 8388640.0f) * dh;
+            }
+        }
+    }
+}
+
+template <int TYPE, int BT>
+struct TC2 {
+    static constexpr int STAGES = BT >= 256 ? 3 : 4;
+    static constexpr int XB = BT * 128;                       // bf16 activation tile
+    static constexpr int STAGE = A_BYTES + XB + Raw<TYPE>::BYTES;
+    static constexpr size_t SMEM = (size_t)STAGES * STAGE + 1024;
+};
+
+template <int TYPE, int BT>
+__global__ void __launch_bounds__(320, 1) k_qgemm_tc2(WView w, const __grid_constant__ CUtensorMap tmx,
+                                                     float *__restrict__ Y, int T, int N, int *flag) {
+    using C = TC2<TYPE, BT>;
+    using R = Raw<TYPE>;
+    constexpr int ST = C::STAGES;
+    extern __shared__ uint8_t smem_raw[];
+    __shared__ __align__(8) uint64_t load_full[ST], a_full[ST], stage_empty[ST], acc_bar;
+    __shared__ uint32_t tmem_base_sh;
+
+    const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+    const int n0 = blockIdx.x * 128, t0 = blockIdx.y * BT;
+    const int units = w.units, ksteps = (units + 1) / 2;
+    uint8_t *base = (uint8_t *)(((uintptr_t)smem_raw + 1023) & ~(uintptr_t)1023);
+
+    if (threadIdx.x == 0) {
+        for (int s = 0; s < ST; s++) {
+            mbar_init(smem_u32(&load_full[s]), 1);
+            mbar_init(smem_u32(&a_full[s]), 256);
+            mbar_init(smem_u32(&stage_empty[s]), 1);
+        }
+        mbar_init(smem_u32(&acc_bar), 1);
+        asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
+        asm volatile("prefetch.tensormap [%0];" ::"l"((uint64_t)&tmx) : "memory");
+    }
+    if (warp == 9) {
+        asm volatile("tcgen05.alloc.cta_group::1.sync.aligned.shared::cta.b32 [%0], %1;" ::"r"(smem_u32(&tmem_base_sh)),
+                     "r"(BT));
+        asm volatile("tcgen05.relinquish_alloc_permit.cta_group::1.sync.aligned;");
+    }
+    tc_fence_before();
+    __syncthreads();
+    tc_fence_after();
+    const uint32_t tmem = tmem_base_sh;
+    pdl_wait();
+    pdl_trigger();
+
+    if (warp == 8) {
+        // ---- copy engine driver
+        if (lane == 0) {
+            for (int ks = 0; ks < ksteps; ks++) {
+                const int s = ks % ST, round = ks / ST;
+                if (!mbar_wait(smem_u32(&stage_empty[s]), (round & 1) ^ 1, flag)) break;
+                uint8_t *stg = base + s * C::STAGE;
+                const uint32_t bar = smem_u32(&load_full[s]);
+                const int ua = 2 * ks, ub = 2 * ks + 1;
+                const bool has_b = ub < units;
+                uint32_t bytes = C::XB + (has_b ? 2 : 1) * (R::QB + R::AUXB);
+                if (R::METAN == 2) bytes += (has_b ? 2 : 1) * R::METAB;
+                else bytes += R::METAB;
+                if (TYPE == HD_TYPE_Q6_K) bytes += 256;
+                mbar_expect_tx(bar, bytes);
+                tma_2d(smem_u32(stg + A_BYTES), &tmx, ks * BK, t0, bar);
+                uint8_t *raw = stg + A_BYTES + C::XB;
+                for (int h = 0; h < (has_b ? 2 : 1); h++) {
+                    const int u = ua + h;
+                    const int64_t ur = (int64_t)u * w.rows + n0;
+                    bulk_g2s(smem_u32(raw + R::Q + h * R::QB), w.q + ur * (R::QB / 128), R::QB, bar);
+                    if (R::AUXB) bulk_g2s(smem_u32(raw + R::AUX + h * R::AUXB), w.aux + ur * (R::AUXB / 128), R::AUXB, bar);
+                    if (R::METAN == 2) bulk_g2s(smem_u32(raw + R::META + h * R::METAB), w.meta + ur * 2, R::METAB, bar);
+                }
+                if (R::METAN == 1) {
+                    const int64_t sr = (int64_t)(ua >> 3) * w.rows + n0;
+                    bulk_g2s(smem_u32(raw + R::META), w.meta + sr * 16, R::METAB, bar);
+                    if (TYPE == HD_TYPE_Q6_K) bulk_g2s(smem_u32(raw + R::DSB), w.dsb + sr, 256, bar);
+                }
+            }
+        }
+        __syncwarp();
+    } else if (warp == 9) {
+        // ---- MMA issuer
+        if (lane == 0) {
+            constexpr uint32_t idesc = idesc_bf16(BT);
+            for (int ks = 0; ks < ksteps; ks++) {
+                const int s = ks % ST, round = ks / ST;
+                if (!mbar_wait(smem_u32(&a_full[s]), round & 1, flag)) break;
+                tc_fence_after();
+                uint8_t *stg = base + s * C::STAGE;
+                const uint32_t a0 = smem_u32(stg), b0 = smem_u32(stg + A_BYTES);
+#pragma unroll
+                for (int kk = 0; kk < BK / 16; kk++) {
+                    uint64_t ad = sw128_desc(a0 + kk * 32), bd = sw128_desc(b0 + kk * 32);
+                    uint32_t acc = (ks > 0 || kk > 0) ? 1u : 0u;
+                    asm volatile(
+                        "{\n .reg .pred p;\n setp.ne.b32 p, %4, 0;\n"
+                        " tcgen05.mma.cta_group::1.kind::f16 [%0], %1, %2, %3, p;\n}\n" ::"r"(tmem),
+                        "l"(ad), "l"(bd), "r"(idesc), "r"(acc));
+                }
+                asm volatile("tcgen05.commit.cta_group::1.mbarrier::arrive::one.shared::cluster.b64 [%0];" ::"r"(
+                                 smem_u32(&stage_empty[s]))
+                             : "memory");
+            }
+            asm volatile("tcgen05.commit.cta_group::1.mbarrier::arrive::one.shared::cluster.b64 [%0];" ::"r"(
+                             smem_u32(&acc_bar))
+                         : "memory");
+        }
+        __syncwarp();
+    } else {
+        // ---- dequantizers: thread (row r, unit half h) of each stage
+        const int r = threadIdx.x & 127, h = threadIdx.x >> 7;
+        for (int ks = 0; ks < ksteps; ks++) {
+            const int s = ks % ST, round = ks / ST;
+            if (!mbar_wait(smem_u32(&load_full[s]), round & 1, flag)) break;
+            uint8_t *stg = base + s * C::STAGE;
+            const int u = 2 * ks + h;
+            float v[32];
+            if (u < units) {
+                raw_values<TYPE>(stg + A_BYTES + C::XB, r, h, u, v);
+            } else {
+#pragma unroll
+                for (int j = 0; j < 32; j++) v[j] = 0.f;
+            }
+            store_sw128(stg, r, 4 * h, v);
+            fence_async_smem();
+            mbar_arrive(smem_u32(&a_full[s]));
+        }
+    }
+
+    // ---- epilogue: warps 0-7
+    if (warp < 8) {
+        const bool ok = mbar_wait(smem_u32(&acc_bar), 0, flag);
+        tc_fence_after();
+        const int q = warp & 3, half = warp >> 2;
+        const int64_t n = n0 + 32 * q + lane;
+        for (int c0 = half * (BT / 2); c0 < (half + 1) * (BT / 2); c0 += 16) {
+            uint32_t rr[16];
+            const uint32_t taddr = tmem + ((uint32_t)(32 * q) << 16) + (uint32_t)c0;
+            asm volatile(
+                "tcgen05.ld.sync.aligned.32x32b.x16.b32 {%0,%1,%2,%3,%4,%5,%6,%7,%8,%9,%10,%11,%12,%13,%14,%15}, "
+                "[%16];"
+                : "=r"(rr[0]), "=r"(rr[1]), "=r"(rr[2]), "=r"(rr[3]), "=r"(rr[4]), "=r"(rr[5]), "=r"(rr[6]),
+                  "=r"(rr[7]), "=r"(rr[8]), "=r"(rr[9]), "=r"(rr[10]), "=r"(rr[11]), "=r"(rr[12]), "=r"(rr[13]),
+                  "=r"(rr[14]), "=r"(rr[15])
+                : "r"(taddr));
+            asm volatile("tcgen05.wait::ld.sync.aligned;" ::: "memory");
+            if (ok && n < N) {
+#pragma unroll
+                for (int j = 0; j < 16; j++) {
+                    const int t = t0 + c0 + j;
+                    if (t < T) Y[(int64_t)t * N + n] = __uint_as_float(rr[j]);
+                }
+            }
+        }
+    }
+    tc_fence_before();
+    __syncthreads();
+    if (warp == 9) {
+        tc_fence_after();
+        asm volatile("tcgen05.dealloc.cta_group::1.sync.aligned.b32 %0, %1;" ::"r"(tmem), "r"(BT));
+    }
+}
+
+__global__ void k_to_bf16(const float *__restrict__ x, __nv_bfloat16 *__restrict__ y, int64_t n) {
+    pdl_wait();
+    pdl_trigger();
+    int64_t i = ((int64_t)blockIdx.x * blockDim.x + threadIdx.x) * 4;
+    if (i + 3 < n) {
+        float4 v = *(const float4 *)(x + i);
+        __nv_bfloat162 a = __floats2bfloat162_rn(v.x, v.y), b = __floats2bfloat162_rn(v.z, v.w);
+        *(__nv_bfloat162 *)(y + i) = a;
+        *(__nv_bfloat162 *)(y + i + 2) = b;
+    } else {
+        for (; i < n; i++) y[i] = __float2bfloat16_rn(x[i]);
+    }
+}
+
+// cuTensorMapEncodeTiled, looked up through the runtime so the library does
+// not link the driver library (it still loads on machines without a GPU).
+typedef CUresult (*EncodeTiledFn)(CUtensorMap *, CUtensorMapDataType, cuuint32_t, void *, const cuuint64_t *,
+                                  const cuuint64_t *, const cuuint32_t *, const cuuint32_t *, CUtensorMapInterleave,
+                                  CUtensorMapSwizzle, CUtensorMapL2promotion, CUtensorMapFloatOOBfill);
+EncodeTiledFn encode_tiled() {
+    static EncodeTiledFn fn = nullptr;
+    if (!fn) {
+        void *p = nullptr;
+        cudaDriverEntryPointQueryResult q;
+        if (cudaGetDriverEntryPoint("cuTensorMapEncodeTiled", &p, cudaEnableDefault, &q) == cudaSuccess &&
+            q == cudaDriverEntryPointSuccess)
+            fn = (EncodeTiledFn)p;
+    }
+    return fn;
+}
+
+template <int TYPE, int BT>
+cudaError_t launch_tc2(hd_ctx *ctx, const hd_weight *w, const CUtensorMap &tm, float *Y, int T) {
+    constexpr size_t smem = TC2<TYPE, BT>::SMEM;
+    cudaError_t e = cudaFuncSetAttribute(k_qgemm_tc2<TYPE, BT>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
+    if (e != cudaSuccess) return e;
+    dim3 grid((unsigned)(w->rows / 128), (unsigned)((T + BT - 1) / BT));
+    return hd_launch(ctx, k_qgemm_tc2<TYPE, BT>, grid, dim3(320), smem, wview(w), tm, Y, T, (int)w->rows, ctx->flag);
+}
+
 }  // namespace
 
-// Token tile: the widest of 64/128/256 that still gives every SM a tile.
+// Token tile: 128 (64 for short inputs), or 256 when that still gives two
+// tiles per SM.  rows % 128 == 0 uses the streamed v2 kernel.
 int hd_qgemm_tc(hd_ctx *ctx, const hd_weight *w, const float *X, float *Y, int T) {
     HD_REQUIRE(ctx, w->cols % 8 == 0, HD_E_SHAPE, "hd_qgemm: K must be a multiple of 8");
     const int64_t mt = (w->rows + 127) / 128;
+    cudaError_t e = cudaSuccess;
+    if (w->rows % 128 == 0 && getenv("HACEDLE_TC_V1") == nullptr) {
+        // bf16 copy of the activations for the TMA
+        const size_t need = (size_t)T * w->cols * sizeof(__nv_bfloat16);
+        int rc = hd_ensure_hbuf(ctx, &ctx->xbf, &ctx->xbf_bytes, (need + 3) / 4 * 4);
+        if (rc) return rc;
+        const int64_t n = (int64_t)T * w->cols;
+        e = hd_launch(ctx, k_to_bf16, dim3((unsigned)((n / 4 + 255) / 256 + 1)), dim3(256), 0, X,
+                      (__nv_bfloat16 *)ctx->xbf, n);
+        if (e != cudaSuccess) return hd_fail(ctx, HD_E_CUDA, "hd_qgemm (bf16 convert): %s", cudaGetErrorString(e));
+        int bt = T <= 64 ? 64 : 128;
+        if (T > 128 && mt * ((T + 255) / 256) >= 2 * ctx->sm_count) bt = 256;
+        CUtensorMap tm;
+        cuuint64_t dims[2] = {(cuuint64_t)w->cols, (cuuint64_t)T};
+        cuuint64_t strides[1] = {(cuuint64_t)w->cols * 2};
+        cuuint32_t box[2] = {(cuuint32_t)BK, (cuuint32_t)bt};
+        cuuint32_t estr[2] = {1, 1};
+        EncodeTiledFn enc = encode_tiled();
+        if (!enc) return hd_fail(ctx, HD_E_CUDA, "hd_qgemm: cuTensorMapEncodeTiled is not available");
+        CUresult cr = enc(&tm, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 2, ctx->xbf, dims, strides, box,
+                                             estr, CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B,
+                                             CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+        if (cr != CUDA_SUCCESS) return hd_fail(ctx, HD_E_CUDA, "hd_qgemm: cuTensorMapEncodeTiled failed (%d)", (int)cr);
+        HD_TYPE_SWITCH(w->type, TT, {
+            if (bt == 64) e = launch_tc2<TT, 64>(ctx, w, tm, Y, T);
+            else if (bt == 128) e = launch_tc2<TT, 128>(ctx, w, tm, Y, T);
+            else e = launch_tc2<TT, 256>(ctx, w, tm, Y, T);
+        });
+        if (e != cudaSuccess) return hd_fail(ctx, HD_E_CUDA, "hd_qgemm (tcgen05 v2): %s", cudaGetErrorString(e));
+        return HD_OK;
+    }
     int bt = 64;
     if (T > 64 && mt * ((T + 127) / 128) >= ctx->sm_count) bt = 128;
     if (T > 128 && mt * ((T + 255) / 256) >= 2 * ctx->sm_count) bt = 256;
-    cudaError_t e = cudaSuccess;
     HD_TYPE_SWITCH(w->type, TT, {
         if (bt == 64) e = launch_tc<TT, 64>(ctx, w, X, Y, T);
         else if (bt == 128) e = launch_tc<TT, 128>(ctx, w, X, Y, T);

@@ -2,39 +2,38 @@
 // a gate/up pair) for b < B <= 16, fp32 accumulation, weights unpacked in
 // registers straight from the unit-major layout.
 //
-// Work split.  A CTA owns RC consecutive output rows over the whole of K (or
-// over one of S slices of K when K is very long for few rows).  Its NT = RC*G
-// threads form G groups: thread t owns row t % RC and the units
+// Work split.  A CTA owns RC consecutive output rows over the whole of K.
+// Its NT = RC*G threads form G groups: thread t owns row t % RC and the units
 // t / RC, t / RC + G, ...; lanes on consecutive rows read one unit of
 // consecutive rows as one contiguous span of the unit-major layout.  RC is
-// about rows / SMs, so there is roughly one CTA per SM and every CTA streams
-// its whole slice of W with all of its loads in flight at once.
+// about rows / SMs but small enough that each thread holds about one unit, so
+// an SM runs ~28 warps (up to 1024 threads per CTA at batch <= 2) and all of
+// its weight loads are in flight at once.
 //
 // Reduction.  Per-row partial sums meet in shared memory and are added in a
-// fixed order (group 0, 1, ..., G-1), so results are bitwise reproducible.
-// With S > 1 the CTAs of a row tile publish partials to the workspace and the
-// last to arrive (atomic ticket) adds them in split order and resets the
-// ticket.
+// fixed order (groups of 16, then the group sums), so results are bitwise
+// reproducible.
 //
 // x.  Activations are read from global memory through L1 after the
 // dependency wait; lanes that share a unit read the same addresses (a
-// broadcast).  Q4_K's per-unit sums of x, needed for its min term, are
-// computed once per CTA into shared memory.
+// broadcast).  Sums of x over each half unit, which carry the quant offsets
+// (see unit_fma), are computed once per CTA into shared memory.
 //
 // Overlap.  The first chunk of each thread's weight loads is issued before
 // griddepcontrol.wait: under programmatic dependent launch those loads run
 // while the previous kernel in the stream is still finishing.  Nothing the
 // previous kernel writes is read or written before the wait.
 //
-// Unpacking.  Bytes become floats exactly via byte_perm into 0x4B0000bb
-// (= 2^23 + byte) and one subtraction of 2^23 + offset; Q5_0's fifth bit and
-// Q6_K's two high bits are merged into the bytes by one shift and one mask
-// thanks to the re-ordering done at upload (hd_internal.cuh).
+// Unpacking.  One byte_perm turns a quant byte into the float 2 + q/64
+// exactly; Q5_0's fifth bit and Q6_K's two high bits are merged into the bytes
+// by one shift and one mask thanks to the re-ordering done at upload
+// (hd_internal.cuh).
+#include <cstdlib>
+
 #include "hd_internal.cuh"
 
 namespace {
 
-constexpr int UC = 4;  // units per thread per register chunk
 
 struct GemvArgs {
     WView w0, w1;          // w1: the up weight of a SwiGLU pair
@@ -42,11 +41,8 @@ struct GemvArgs {
     float *y;              // [B][ldy]
     const float *bias;     // [N] or null
     const float *residual; // [B][ldy] or null
-    float *ws;             // split-K partials [S][NB][Neff]
-    int *tickets;          // [tiles]
     int B, N, ldy, K;
     int RC, G;             // rows per CTA, unit groups per CTA
-    int U, S;              // units per split, splits
     int pair;              // 1: SwiGLU of (w0, w1)
 };
 template <int TYPE>
@@ -116,9 +112,25 @@ __device__ __forceinline__ float dot4(float a0, float a1, float a2, float a3, co
 
 // acc[b] += unit(u) . x[b][unit]; xs points at this unit's 32 floats of batch
 // row 0, batch rows `xstride4` float4s apart.
+// The float 2 + byte/64, exact for byte < 128: byte c of v goes to bits
+// 16..23 under the exponent byte 0x40 (one byte_perm, no subtraction).  The
+// constant 2 is removed per unit with the sum of x (see unit_fma).
+__device__ __forceinline__ float f2q(uint32_t v, int c) {
+    return __uint_as_float(__byte_perm(v, 0x40000000u, 0x7044u | ((uint32_t)c << 8)));
+}
+
+// acc[b] += unit(u) . x[b][unit].  xs points at this unit's 32 floats of batch
+// row 0 (float4), batch rows `xstride4` float4s apart; xh holds the sums of
+// x over the unit's two 16-value halves, batch rows `xh_stride` apart.
+//
+// Q5_0, Q4_K and Q6_K form S = sum_j f_j x_j with f_j = 2 + q_j/64, so
+// sum_j q_j x_j = 64 S - 128 X (X = sum_j x_j) and each type's offset folds
+// into the X term:  Q5_0  d (64 S - 144 X);  Q4_K  64 d1 S - (128 d1 + m1) X;
+// Q6_K  dl (64 S_lo - 160 X_lo) + dh (64 S_hi - 160 X_hi).  Q8_0 (signed
+// bytes) uses 2^23 + byte and one subtraction per value.
 template <int TYPE, int NB>
 __device__ __forceinline__ void unit_fma(const URegs<TYPE> &g, int u, const float4 *xs, int xstride4,
-                                         const float *xsum, int xsum_stride, float (&acc)[NB]) {
+                                         const float *xh, int xh_stride, float (&acc)[NB]) {
     if constexpr (TYPE == HD_TYPE_Q8_0) {
         float s[NB];
 #pragma unroll
@@ -134,51 +146,7 @@ __device__ __forceinline__ void unit_fma(const URegs<TYPE> &g, int u, const floa
         float d = h2f((uint16_t)g.d);
 #pragma unroll
         for (int b = 0; b < NB; b++) acc[b] = fmaf(d, s[b], acc[b]);
-    } else if constexpr (TYPE == HD_TYPE_Q5_0) {
-        float s[NB];
-#pragma unroll
-        for (int b = 0; b < NB; b++) s[b] = 0.f;
-#pragma unroll
-        for (int wd = 0; wd < 4; wd++) {
-            uint32_t v = w4(g.a, wd);
-            uint32_t lo = (v & 0x0F0F0F0Fu) | ((g.qh >> wd) & 0x10101010u);
-            uint32_t hi = ((v >> 4) & 0x0F0F0F0Fu) | ((g.qh << (4 - wd)) & 0x10101010u);
-            const float o = 8388624.0f;  // 2^23 + 16
-            float l0 = mag(lo, 0) - o, l1 = mag(lo, 1) - o, l2 = mag(lo, 2) - o, l3 = mag(lo, 3) - o;
-            float h0 = mag(hi, 0) - o, h1 = mag(hi, 1) - o, h2 = mag(hi, 2) - o, h3 = mag(hi, 3) - o;
-#pragma unroll
-            for (int b = 0; b < NB; b++) {
-                float t = dot4(l0, l1, l2, l3, xs[b * xstride4 + wd], s[b]);
-                s[b] = dot4(h0, h1, h2, h3, xs[b * xstride4 + 4 + wd], t);
-            }
-        }
-        float d = h2f((uint16_t)g.d);
-#pragma unroll
-        for (int b = 0; b < NB; b++) acc[b] = fmaf(d, s[b], acc[b]);
-    } else if constexpr (TYPE == HD_TYPE_Q4_K) {
-        float s[NB];
-#pragma unroll
-        for (int b = 0; b < NB; b++) s[b] = 0.f;
-#pragma unroll
-        for (int wd = 0; wd < 4; wd++) {
-            uint32_t v = w4(g.a, wd);
-            uint32_t lo = v & 0x0F0F0F0Fu, hi = (v >> 4) & 0x0F0F0F0Fu;
-            const float o = 8388608.0f;  // 2^23
-            float l0 = mag(lo, 0) - o, l1 = mag(lo, 1) - o, l2 = mag(lo, 2) - o, l3 = mag(lo, 3) - o;
-            float h0 = mag(hi, 0) - o, h1 = mag(hi, 1) - o, h2 = mag(hi, 2) - o, h3 = mag(hi, 3) - o;
-#pragma unroll
-            for (int b = 0; b < NB; b++) {
-                float t = dot4(l0, l1, l2, l3, xs[b * xstride4 + wd], s[b]);
-                s[b] = dot4(h0, h1, h2, h3, xs[b * xstride4 + 4 + wd], t);
-            }
-        }
-        int sc, m;
-        q4k_sm_regs(u & 7, g.m.y, g.m.z, g.m.w, sc, m);
-        float d = h2f((uint16_t)(g.m.x & 0xFFFF)), dmin = h2f((uint16_t)(g.m.x >> 16));
-        float d1 = d * (float)sc, m1 = dmin * (float)m;
-#pragma unroll
-        for (int b = 0; b < NB; b++) acc[b] = fmaf(d1, s[b], fmaf(-m1, xsum[b * xsum_stride], acc[b]));
-    } else {  // Q6_K
+    } else if constexpr (TYPE == HD_TYPE_Q6_K) {
         float sl[NB], sh[NB];
 #pragma unroll
         for (int b = 0; b < NB; b++) sl[b] = sh[b] = 0.f;
@@ -187,9 +155,8 @@ __device__ __forceinline__ void unit_fma(const URegs<TYPE> &g, int u, const floa
             uint32_t v = w4(g.a, wd);
             uint32_t lo = (v & 0x0F0F0F0Fu) | (shl_or_shr(g.h.x, 4 - 2 * wd) & 0x30303030u);
             uint32_t hi = ((v >> 4) & 0x0F0F0F0Fu) | (shl_or_shr(g.h.y, 4 - 2 * wd) & 0x30303030u);
-            const float o = 8388640.0f;  // 2^23 + 32
-            float l0 = mag(lo, 0) - o, l1 = mag(lo, 1) - o, l2 = mag(lo, 2) - o, l3 = mag(lo, 3) - o;
-            float h0 = mag(hi, 0) - o, h1 = mag(hi, 1) - o, h2 = mag(hi, 2) - o, h3 = mag(hi, 3) - o;
+            float l0 = f2q(lo, 0), l1 = f2q(lo, 1), l2 = f2q(lo, 2), l3 = f2q(lo, 3);
+            float h0 = f2q(hi, 0), h1 = f2q(hi, 1), h2 = f2q(hi, 2), h3 = f2q(hi, 3);
 #pragma unroll
             for (int b = 0; b < NB; b++) {
                 sl[b] = dot4(l0, l1, l2, l3, xs[b * xstride4 + wd], sl[b]);
@@ -202,28 +169,80 @@ __device__ __forceinline__ void unit_fma(const URegs<TYPE> &g, int u, const floa
         float d = h2f((uint16_t)g.d);
         float dl = d * (float)c0, dh = d * (float)c1;
 #pragma unroll
-        for (int b = 0; b < NB; b++) acc[b] = fmaf(dl, sl[b], fmaf(dh, sh[b], acc[b]));
+        for (int b = 0; b < NB; b++) {
+            const float xl = xh[b * xh_stride], xr = xh[b * xh_stride + 1];
+            acc[b] = fmaf(dl, fmaf(64.f, sl[b], -160.f * xl), acc[b]);
+            acc[b] = fmaf(dh, fmaf(64.f, sh[b], -160.f * xr), acc[b]);
+        }
+    } else {  // Q5_0, Q4_K: one scale per unit
+        float s[NB];
+#pragma unroll
+        for (int b = 0; b < NB; b++) s[b] = 0.f;
+#pragma unroll
+        for (int wd = 0; wd < 4; wd++) {
+            uint32_t v = w4(g.a, wd), lo, hi;
+            if constexpr (TYPE == HD_TYPE_Q5_0) {
+                lo = (v & 0x0F0F0F0Fu) | ((g.qh >> wd) & 0x10101010u);
+                hi = ((v >> 4) & 0x0F0F0F0Fu) | ((g.qh << (4 - wd)) & 0x10101010u);
+            } else {
+                lo = v & 0x0F0F0F0Fu;
+                hi = (v >> 4) & 0x0F0F0F0Fu;
+            }
+            float l0 = f2q(lo, 0), l1 = f2q(lo, 1), l2 = f2q(lo, 2), l3 = f2q(lo, 3);
+            float h0 = f2q(hi, 0), h1 = f2q(hi, 1), h2 = f2q(hi, 2), h3 = f2q(hi, 3);
+#pragma unroll
+            for (int b = 0; b < NB; b++) {
+                float t = dot4(l0, l1, l2, l3, xs[b * xstride4 + wd], s[b]);
+                s[b] = dot4(h0, h1, h2, h3, xs[b * xstride4 + 4 + wd], t);
+            }
+        }
+        if constexpr (TYPE == HD_TYPE_Q5_0) {
+            float d = h2f((uint16_t)g.d);
+#pragma unroll
+            for (int b = 0; b < NB; b++) {
+                const float X = xh[b * xh_stride] + xh[b * xh_stride + 1];
+                acc[b] = fmaf(d, fmaf(64.f, s[b], -144.f * X), acc[b]);
+            }
+        } else {
+            int sc, m;
+            q4k_sm_regs(u & 7, g.m.y, g.m.z, g.m.w, sc, m);
+            float d = h2f((uint16_t)(g.m.x & 0xFFFF)), dmin = h2f((uint16_t)(g.m.x >> 16));
+            float d1 = d * (float)sc, m1 = dmin * (float)m;
+#pragma unroll
+            for (int b = 0; b < NB; b++) {
+                const float X = xh[b * xh_stride] + xh[b * xh_stride + 1];
+                acc[b] = fmaf(64.f * d1, s[b], fmaf(-(128.f * d1 + m1), X, acc[b]));
+            }
+        }
     }
 }
 
 __device__ __forceinline__ float silu_mul(float g, float u) { return g / (1.0f + expf(-g)) * u; }
 
+// Threads per CTA and units per register chunk for a padded batch NB; a
+// SwiGLU pair (P = 1) holds two weights' registers, so half the threads.
+template <int NB, int P>
+struct GemvShape {
+    static constexpr int MAXT = (NB <= 2 ? 1024 : NB <= 4 ? 512 : 256) >> P;
+    static constexpr int UCT = NB <= 2 ? 2 : 4;
+};
+
 template <int TYPE, int NB, int P>
-__global__ void __launch_bounds__(256) k_qgemv(GemvArgs a) {
+__global__ void __launch_bounds__(GemvShape<NB, P>::MAXT) k_qgemv(GemvArgs a) {
+    constexpr int UCT = GemvShape<NB, P>::UCT;
     extern __shared__ float sm[];
     const int t = threadIdx.x, NT = blockDim.x;
     const int RC = a.RC, G = a.G;
-    const int tile = blockIdx.x, split = blockIdx.y;
+    const int tile = blockIdx.x;
     const int r = t % RC, g = t / RC;
     const int64_t row = (int64_t)tile * RC + r;
     const bool ok = row < a.N && g < G;
-    const int u0 = split * a.U;
-    const int u1 = min(a.w0.units, u0 + a.U);
+    const int u0 = 0, u1 = a.w0.units, nu = u1 - u0;
     const WView wa = a.w0, wb = a.w1;
 
-    URegs<TYPE> cur[UC][P + 1];
+    URegs<TYPE> cur[UCT][P + 1];
 #pragma unroll
-    for (int c = 0; c < UC; c++) {
+    for (int c = 0; c < UCT; c++) {
         const int u = u0 + g + c * G;
 #pragma unroll
         for (int p = 0; p <= P; p++) {
@@ -234,23 +253,23 @@ __global__ void __launch_bounds__(256) k_qgemv(GemvArgs a) {
     pdl_trigger();
     pdl_wait();
 
-    // Q4_K: sum of x over every unit of this CTA's K range, per batch row.
-    float *xsum = sm;                         // [NB][U]
-    float *red = sm + (TYPE == HD_TYPE_Q4_K ? NB * a.U : 0);  // [NT][P+1][NB]
-    if constexpr (TYPE == HD_TYPE_Q4_K) {
-        const int nu = u1 - u0;
-        for (int i = t; i < NB * nu; i += NT) {
-            const int b = i / nu, ul = i % nu;
-            float s = 0.f;
+    // Sums of x over each 16-value half unit, per batch row: [NB][nu][2].
+    float *xh = sm;
+    float *red = sm + (TYPE == HD_TYPE_Q8_0 ? 0 : NB * nu * 2);   // [NT][P+1][NB]
+    float *red2 = red + NT * (P + 1) * NB;                            // [RC*NB*(P+1)][nch]
+    if constexpr (TYPE != HD_TYPE_Q8_0) {
+        for (int i = t; i < NB * nu * 2; i += NT) {
+            const int b = i / (nu * 2), ul = (i >> 1) % nu, hf = i & 1;
+            float sx = 0.f;
             if (b < a.B) {
-                const float4 *p = (const float4 *)(a.x + (int64_t)b * a.K + (int64_t)(u0 + ul) * 32);
+                const float4 *p4 = (const float4 *)(a.x + (int64_t)b * a.K + (int64_t)(u0 + ul) * 32 + hf * 16);
 #pragma unroll
-                for (int j = 0; j < 8; j++) {
-                    float4 v = p[j];
-                    s += (v.x + v.y) + (v.z + v.w);
+                for (int j = 0; j < 4; j++) {
+                    const float4 v = p4[j];
+                    sx += (v.x + v.y) + (v.z + v.w);
                 }
             }
-            xsum[b * a.U + ul] = s;
+            xh[i] = sx;
         }
         __syncthreads();
     }
@@ -261,11 +280,11 @@ __global__ void __launch_bounds__(256) k_qgemv(GemvArgs a) {
 #pragma unroll
         for (int b = 0; b < NB; b++) acc[p][b] = 0.f;
 
-    const int xs4 = a.K / 4;  // float4 per batch row of x
-    for (int base = u0 + g; base < u1; base += UC * G) {
+    const int xs4 = a.K / 4;
+    for (int base = u0 + g; base < u1; base += UCT * G) {
         if (base != u0 + g) {
 #pragma unroll
-            for (int c = 0; c < UC; c++) {
+            for (int c = 0; c < UCT; c++) {
                 const int u = base + c * G;
 #pragma unroll
                 for (int p = 0; p <= P; p++) {
@@ -275,118 +294,120 @@ __global__ void __launch_bounds__(256) k_qgemv(GemvArgs a) {
             }
         }
 #pragma unroll
-        for (int c = 0; c < UC; c++) {
+        for (int c = 0; c < UCT; c++) {
             const int u = base + c * G;
             if (ok && u < u1) {
                 const float4 *xp = (const float4 *)(a.x + (int64_t)u * 32);
 #pragma unroll
                 for (int p = 0; p <= P; p++)
-                    unit_fma<TYPE, NB>(cur[c][p], u, xp, xs4, xsum + (u - u0), a.U, acc[p]);
+                    unit_fma<TYPE, NB>(cur[c][p], u, xp, xs4, xh + (u - u0) * 2, nu * 2, acc[p]);
             }
         }
     }
 
-    // Per-row sums over the G groups, in group order.
+    // Per-row sums over the G groups in a fixed order: groups of 16 first
+    // (when G > 16), then the group sums.
 #pragma unroll
     for (int p = 0; p <= P; p++)
 #pragma unroll
         for (int b = 0; b < NB; b++) red[(t * (P + 1) + p) * NB + b] = acc[p][b];
     __syncthreads();
-
-    const int64_t neff = P ? 2 * (int64_t)a.N : (int64_t)a.N;
-    auto epilogue = [&](int64_t rw, int b, float v, float vu) {
-        if (P) {
-            a.y[(int64_t)b * a.ldy + rw] = silu_mul(v, vu);
-        } else {
-            if (a.bias) v = v + a.bias[rw];
-            if (a.residual) v = a.residual[(int64_t)b * a.ldy + rw] + v;
-            a.y[(int64_t)b * a.ldy + rw] = v;
-        }
-    };
-    const int nout = RC * a.B;
-    if (a.S == 1) {
-        for (int j = t; j < nout; j += NT) {
-            const int rr = j % RC, b = j / RC;
-            const int64_t rw = (int64_t)tile * RC + rr;
-            if (rw >= a.N) continue;
-            float v[P + 1];
-#pragma unroll
-            for (int p = 0; p <= P; p++) {
-                float s = 0.f;
-                for (int gg = 0; gg < G; gg++) s += red[((gg * RC + rr) * (P + 1) + p) * NB + b];
-                v[p] = s;
-            }
-            epilogue(rw, b, v[0], v[P]);
-        }
-        return;
-    }
-
-    // Split-K: publish this CTA's row sums, the last CTA of the tile reduces.
-    for (int j = t; j < nout; j += NT) {
-        const int rr = j % RC, b = j / RC;
-        const int64_t rw = (int64_t)tile * RC + rr;
-        if (rw >= a.N) continue;
-#pragma unroll
-        for (int p = 0; p <= P; p++) {
+    const int nout = RC * a.B * (P + 1);
+    const int nch = (G + 15) / 16;
+    if (nch > 1) {
+        for (int i = t; i < nout * nch; i += NT) {
+            const int o = i / nch, c = i % nch;
+            const int rr = o % RC, bp = o / RC, b = bp % a.B, p = bp / a.B;
             float s = 0.f;
-            for (int gg = 0; gg < G; gg++) s += red[((gg * RC + rr) * (P + 1) + p) * NB + b];
-            __stcg(a.ws + ((int64_t)split * NB + b) * neff + (p ? a.N + rw : rw), s);
+            for (int gg = c * 16; gg < min(G, c * 16 + 16); gg++) s += red[((gg * RC + rr) * (P + 1) + p) * NB + b];
+            red2[o * nch + c] = s;
         }
+        __syncthreads();
     }
-    __threadfence();
-    __syncthreads();
-    __shared__ int last;
-    if (t == 0) last = (atomicAdd(a.tickets + tile, 1) == a.S - 1);
-    __syncthreads();
-    if (!last) return;
-    __threadfence();
-    for (int j = t; j < nout; j += NT) {
-        const int rr = j % RC, b = j / RC;
+    for (int i = t; i < RC * a.B; i += NT) {
+        const int rr = i % RC, b = i / RC;
         const int64_t rw = (int64_t)tile * RC + rr;
         if (rw >= a.N) continue;
         float v[P + 1];
 #pragma unroll
         for (int p = 0; p <= P; p++) {
             float s = 0.f;
-            for (int sp = 0; sp < a.S; sp++) s += __ldcg(a.ws + ((int64_t)sp * NB + b) * neff + (p ? a.N + rw : rw));
+            if (nch > 1) {
+                const int o = (p * a.B + b) * RC + rr;
+                for (int c = 0; c < nch; c++) s += red2[o * nch + c];
+            } else {
+                for (int gg = 0; gg < G; gg++) s += red[((gg * RC + rr) * (P + 1) + p) * NB + b];
+            }
             v[p] = s;
         }
-        epilogue(rw, b, v[0], v[P]);
+        if (P) {
+            a.y[(int64_t)b * a.ldy + rw] = silu_mul(v[0], v[P]);
+        } else {
+            float o = v[0];
+            if (a.bias) o = o + a.bias[rw];
+            if (a.residual) o = a.residual[(int64_t)b * a.ldy + rw] + o;
+            a.y[(int64_t)b * a.ldy + rw] = o;
+        }
     }
-    if (t == 0) a.tickets[tile] = 0;
 }
 
 struct Plan {
-    int nb, RC, G, nt, U, S, tiles;
+    int nb, RC, G, nt, tiles;
     size_t smem;
 };
 
 int pad_batch(int B) { return B <= 1 ? 1 : B <= 2 ? 2 : B <= 4 ? 4 : B <= 8 ? 8 : 16; }
+int max_threads(int nb, bool pair) { return (nb <= 2 ? 1024 : nb <= 4 ? 512 : 256) >> (pair ? 1 : 0); }
 
-// RC ~ rows / SMs (one CTA per SM), G groups of RC threads (NT <= 256, no more
-// groups than units).  Split K only when the row tiles alone leave most SMs
-// idle and every split still gives each group a unit or more.
+// Launch shape, from a sweep of rows-per-CTA x threads-per-CTA on B200 in a
+// PDL chain of back-to-back GEMVs:
+//  - about 2 units per thread (4 at batch >= 8 or for very tall matrices);
+//  - CTAs small enough in registers (<= 512 threads at batch <= 2, 128
+//    above) that the next kernel's CTA fits beside them, so its weight
+//    prefetch overlaps this one -- unless the row tiles leave SMs idle anyway;
+//  - 8..32 rows per CTA (whole 32-byte sectors, x broadcast across lanes),
+//    at most about rows / SMs rounded up to a power of two.
+// HACEDLE_GEMV_NT / HACEDLE_GEMV_RC override the thread cap and the rows per
+// CTA (tuning knobs).
+static int env_int(const char *name, int dflt) {
+    const char *v = getenv(name);
+    return (v && *v) ? atoi(v) : dflt;
+}
+static int pow2ceil(int x) {
+    int p = 1;
+    while (p < x) p <<= 1;
+    return p;
+}
+
 Plan plan_gemv(int N, int units, int B, bool pair, int sms) {
     Plan p;
     p.nb = pad_batch(B);
-    int RC = (N + sms - 1) / sms;
-    RC = RC < 1 ? 1 : RC > 32 ? 32 : RC;
-    int G = 256 / RC;
+    const int MT = max_threads(p.nb, pair);
+    const bool tall = N >= 64 * sms;
+    const int upt = (p.nb >= 8 || tall) ? 4 : 2;
+    int G = pow2ceil((units + upt - 1) / upt);
     if (G > units) G = units;
+    const int ntcap = p.nb <= 2 ? 512 : 128;
+    int rc_hi = pow2ceil((N + sms - 1) / sms);
+    rc_hi = rc_hi < 8 ? 8 : rc_hi > 32 ? 32 : rc_hi;
+    int RC = ntcap / G;
+    RC = RC < 8 ? 8 : RC > rc_hi ? rc_hi : RC;
+    const int nt_env = env_int("HACEDLE_GEMV_NT", 0), rc_env = env_int("HACEDLE_GEMV_RC", 0);
+    if (rc_env >= 1 && rc_env <= 32) RC = rc_env;
+    int cap = MT;
+    if (nt_env >= 32 && nt_env < cap) cap = nt_env;
+    if (RC > cap) RC = cap;
+    if (nt_env >= 32) G = cap / RC < units ? cap / RC : units;
+    if (RC * G > cap) G = cap / RC;
+    if (G < 1) G = 1;
+    if (RC > N) RC = N;
     p.RC = RC;
     p.G = G;
     p.nt = RC * G;
     p.tiles = (N + RC - 1) / RC;
-    int S = 1;
-    if (p.tiles * 2 < sms && units >= 2 * G) {
-        S = (sms + p.tiles - 1) / p.tiles;
-        if (S > units / G) S = units / G;
-        if (S < 1) S = 1;
-    }
-    p.U = (units + S - 1) / S;
-    p.S = (units + p.U - 1) / p.U;
-    const int P1 = pair ? 2 : 1;
-    p.smem = (size_t)p.nt * P1 * p.nb * sizeof(float) + (size_t)p.nb * p.U * sizeof(float);
+    const int P1 = pair ? 2 : 1, nch = (G + 15) / 16;
+    p.smem = ((size_t)p.nb * units * 2 + (size_t)p.nt * P1 * p.nb + (size_t)RC * p.nb * P1 * (nch > 1 ? nch : 0)) *
+             sizeof(float);
     return p;
 }
 
@@ -397,7 +418,7 @@ cudaError_t launch_inst(hd_ctx *ctx, const Plan &p, const GemvArgs &a) {
                                              (int)p.smem);
         if (e != cudaSuccess) return e;
     }
-    return hd_launch(ctx, k_qgemv<TYPE, NB, P>, dim3(p.tiles, p.S), dim3(p.nt), p.smem, a);
+    return hd_launch(ctx, k_qgemv<TYPE, NB, P>, dim3(p.tiles), dim3(p.nt), p.smem, a);
 }
 
 template <int TYPE>
@@ -435,11 +456,6 @@ int run_gemv(hd_ctx *ctx, const hd_weight *w, const hd_weight *w_up, const float
         return rc;
     }
     Plan p = plan_gemv((int)w->rows, w->units, B, w_up != nullptr, ctx->sm_count);
-    if (p.S > 1) {
-        size_t neff = (size_t)w->rows * (w_up ? 2 : 1);
-        int rc = hd_ensure_workspace(ctx, (size_t)p.S * p.nb * neff * sizeof(float), (size_t)p.tiles);
-        if (rc) return rc;
-    }
     GemvArgs a;
     a.w0 = wview(w);
     a.w1 = w_up ? wview(w_up) : a.w0;
@@ -447,16 +463,12 @@ int run_gemv(hd_ctx *ctx, const hd_weight *w, const hd_weight *w_up, const float
     a.y = y;
     a.bias = bias;
     a.residual = residual;
-    a.ws = (float *)ctx->ws;
-    a.tickets = ctx->tickets;
     a.B = B;
     a.N = (int)w->rows;
     a.ldy = (int)w->rows;
     a.K = (int)w->cols;
     a.RC = p.RC;
     a.G = p.G;
-    a.U = p.U;
-    a.S = p.S;
     a.pair = w_up ? 1 : 0;
     cudaError_t e = cudaSuccess;
     HD_TYPE_SWITCH(w->type, T, e = launch_type<T>(ctx, p, a));

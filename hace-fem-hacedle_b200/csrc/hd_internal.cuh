@@ -52,6 +52,8 @@ struct hd_ctx {
     int *flag = nullptr;             // device error flag for bounded waits
     float *scratch = nullptr;        // gate/up outputs when a SwiGLU pair runs unfused
     size_t scratch_bytes = 0;
+    float *xbf = nullptr;            // bf16 copy of GEMM activations (TMA source)
+    size_t xbf_bytes = 0;
 };
 
 struct hd_weight {

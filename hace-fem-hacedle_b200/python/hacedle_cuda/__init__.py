@@ -30,7 +30,7 @@ EXPORTS = [
     "hd_dequantize", "hd_qgemv", "hd_qgemv_swiglu", "hd_qgemv_host", "hd_qgemm", "hd_qgemm_host", "hd_matmul_f32",
     "hd_rmsnorm", "hd_rmsnorm_graph", "hd_rope_neox", "hd_rope_interleaved", "hd_softmax_rows", "hd_swiglu",
     "hd_add", "hd_argmax_rows", "hd_argmax_rows_noalloc", "hd_embed", "hd_kv_append", "hd_attention_decode", "hd_attention_prefill",
-    "hd_dot_i8", "hd_fused_qdot_qadd_qacc_i8", "hd_decoder_create", "hd_decoder_free", "hd_decoder_generate",
+    "hd_dot_i8", "hd_fused_qdot_qadd_qacc_i8", "hd_gather_columns", "hd_decoder_create", "hd_decoder_free", "hd_decoder_generate",
 ]
 
 
@@ -68,6 +68,7 @@ def lib() -> C.CDLL:
         "hd_softmax_rows": [V, V, I64, I], "hd_swiglu": [V, V, V, V, I64], "hd_add": [V, V, V, V, I64],
         "hd_argmax_rows": [V, V, I64, I64, V], "hd_embed": [V, V, V, I, V],
         "hd_argmax_rows_noalloc": [V, I64, I64, V, V],
+        "hd_gather_columns": [V, V, V, I, I, I64],
         "hd_kv_append": [V, V, V, V, V, V, I, I, I, I, I],
         "hd_attention_decode": [V, V, V, V, V, I, I, I, I, I, V],
         "hd_attention_prefill": [V, V, V, V, I, I, I, I, I, I, V],
@@ -225,6 +226,9 @@ class Context:
         n = x.shape[-1]
         rows = x.numel() // n if n else idx.numel()
         self._check(lib().hd_argmax_rows(self.h, _ptr(x), rows, n, _ptr(idx)))
+
+    def gather_columns(self, src, dst, G: int, B: int, n: int):
+        self._check(lib().hd_gather_columns(self.h, _ptr(src), _ptr(dst), G, B, n))
 
     def embed(self, table: Weight, ids, out):
         self._check(lib().hd_embed(self.h, table.h, _ptr(ids), ids.numel(), _ptr(out)))

@@ -178,6 +178,12 @@ int hd_argmax_rows_noalloc(const float *x_dev, int64_t rows, int64_t n, int32_t 
  * out_dev [n][cols]. */
 int hd_embed(hd_ctx *ctx, const hd_weight *table, const int32_t *ids_dev, int n, float *out_dev);
 
+/* Reassembles row-sharded outputs after an all-gather: src_dev [G][B][n]
+ * (rank g's [B][n] slice of output rows g*n..g*n+n-1) -> dst_dev [B][G*n].
+ * The reference has no multi-GPU path; this is the exchange step of the
+ * row-sharded 7B-shaped layer. */
+int hd_gather_columns(hd_ctx *ctx, const float *src_dev, float *dst_dev, int G, int B, int64_t n);
+
 /* ------------------------------------------------------- KV and attention */
 /* Device KV cache (KvCache::append, core/ops/block.rs:268-282, KvArena
  * runtime/kv_cache.rs:8-34): caches are [seq][max_ctx][n_kv][head_dim] f32;
