@@ -145,7 +145,8 @@ def run_ours(args, rank, world, local):
     if args.only:
         fns = {"prefill": lambda: prefill_workload(ctx, args), "dequant": lambda: dequant_workload(ctx),
                "decode": lambda: decode_workload(ctx, args, rank, world),
-               "layer7b": lambda: layer7b_workload(ctx, args, rank, world)}
+               "layer7b": lambda: layer7b_workload(ctx, args, rank, world),
+               "gemv_shapes": lambda: gemv_shapes_workload(ctx, args)}
         r = fns[args.only]()
         if rank == 0:
             print(json.dumps({"workload": args.only, "n_gpus": world, "result": r}), flush=True)
@@ -232,9 +233,15 @@ def run_ours(args, rank, world, local):
     roofline = {"bound": "hbm", "achieved": round(achieved, 1), "peak": hbm, "unit": "GB/s",
                 "frac": round(achieved / hbm, 4), "traffic": None, "peak_kind": peak_kind,
                 "kernel": "k_qgemv", "algorithmic_bytes_per_step": step_bytes}
-    trf = os.path.join(ROOT, "profiles", "gemv_traffic.json")
+    # DRAM bytes of one captured launch (ncu --set full, Q5_0 batch 1), with its
+    # algorithmic bytes: profiles/qgemv_q5_0_b1_ncu.md.
+    trf = os.path.join(ROOT, "profiles", "qgemv_q5_0_b1_ncu.md")
     if os.path.exists(trf):
-        roofline["traffic"] = json.load(open(trf)).get("bytes_per_launch_avg")
+        kv = dict(ln.split(":", 1) for ln in open(trf) if ln.startswith(("dram_bytes_per_launch", "algorithmic_bytes")))
+        if kv:
+            roofline["traffic"] = int(kv["dram_bytes_per_launch"])
+            roofline["traffic_kernel"] = "k_qgemv<Q5_0,B=1> on 4864x896"
+            roofline["traffic_algorithmic_bytes"] = int(kv["algorithmic_bytes_per_launch"])
 
     # End to end through the host-buffer C-ABI call.
     e2e = None
@@ -475,6 +482,53 @@ def layer7b_workload(ctx, args, rank, world, reps=5):
     return res
 
 
+def gemv_shapes_workload(ctx, args):
+    """Sweep of the GEMV launch shape (rows per CTA x thread cap, through the
+    HACEDLE_GEMV_RC / HACEDLE_GEMV_NT planner overrides) for the config-2
+    matrices and the tied LM head: microseconds per launch in a CUDA-graph
+    chain of launches over weight copies larger than L2 (PDL on)."""
+    import torch
+
+    l2 = torch.cuda.get_device_properties(0).L2_cache_size
+    res = {}
+    cases = CASES + [(S.GGML_Q8_0, 151936, 896)]
+    for (t, N, K) in cases:
+        nb = S.nbytes(t, N, K)
+        raw = S.gen_weight(t, N, K, seed=2 + t)
+        ws = [ctx.weight(t, raw, N, K) for _ in range(max(4, int(np.ceil(3 * l2 / nb))))]
+        for B in ((1, 4, 16) if N < 100000 else (1,)):
+            x = torch.from_numpy(S.gen_activations(B, K, 5)).cuda()
+            y = torch.empty(B, N, device="cuda")
+            for nt, rc in [(0, 0)] + [(nt, rc) for nt in (128, 256, 512, 1024) for rc in (2, 4, 8, 16, 32)]:
+                os.environ["HACEDLE_GEMV_NT"], os.environ["HACEDLE_GEMV_RC"] = str(nt), str(rc)
+                for w in ws:
+                    ctx.qgemv(w, x, y)
+                torch.cuda.synchronize()
+                g, st = torch.cuda.CUDAGraph(), torch.cuda.Stream()
+                with torch.cuda.graph(g, stream=st):
+                    ctx.set_stream(torch.cuda.current_stream().cuda_stream)
+                    for w in ws:
+                        ctx.qgemv(w, x, y)
+                ctx.set_stream(torch.cuda.current_stream().cuda_stream)
+                for _ in range(3):
+                    g.replay()
+                e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+                e0.record()
+                for _ in range(10):
+                    g.replay()
+                e1.record()
+                torch.cuda.synchronize()
+                us = e0.elapsed_time(e1) * 1e3 / (10 * len(ws))
+                key = f"{S.TYPE_NAME[t]}_{N}x{K}_B{B}"
+                res.setdefault(key, {})["default" if nt == 0 else f"nt{nt}_rc{rc}"] = round(us, 3)
+                del g
+        for w in ws:
+            w.free()
+    os.environ.pop("HACEDLE_GEMV_NT", None)
+    os.environ.pop("HACEDLE_GEMV_RC", None)
+    return res
+
+
 def e2e_host(ctx, weights, args):
     """Same sweep through hd_qgemv_host with host buffers (one weight copy per
     case is enough: x and y cross PCIe every call, weights are device-resident)."""
@@ -569,7 +623,8 @@ def main():
     ap.add_argument("--no-cpu", action="store_true")
     ap.add_argument("--no-e2e", action="store_true")
     ap.add_argument("--no-extra", action="store_true", help="headline GEMV sweep only")
-    ap.add_argument("--only", choices=["prefill", "dequant", "decode", "layer7b"], help="run one secondary workload")
+    ap.add_argument("--only", choices=["prefill", "dequant", "decode", "layer7b", "gemv_shapes"],
+                    help="run one secondary workload")
     ap.add_argument("--decode-batch", type=int, default=256,
                     help="sequences decoded together, split over the ranks (0: batch 1 only)")
     args = ap.parse_args()
