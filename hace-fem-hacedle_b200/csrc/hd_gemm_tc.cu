@@ -1,7 +1,9 @@
 // hd_gemm_tc.cu -- prefill Q-GEMM on the 5th-generation tensor cores.
 //
 // Y[t][n] = sum_k X[t][k] W[n][k] with W a quantized GGUF weight and X fp32.
-// One CTA computes a 128 (weight rows) x BT (tokens) tile with
+// Two kernels: the persistent, streamed v3 kernel (described at its
+// definition) for weights with rows % 128 == 0, and the v1 kernel below for
+// any shape.  In v1 one CTA computes a 128 (weight rows) x BT (tokens) tile with
 // tcgen05.mma.cta_group::1.kind::f16 (bf16 operands, fp32 accumulator in
 // TMEM: 128 lanes = weight rows, BT columns = tokens).
 //
@@ -25,6 +27,7 @@
 // waiting; the MMA warp always commits the accumulator barrier so that the
 // epilogue's wait also covers any MMAs still in flight, and TMEM is freed
 // before exit on every path.
+#include <cstdlib>
 #include <cuda.h>
 
 #include "hd_internal.cuh"
@@ -54,17 +57,33 @@ __device__ __forceinline__ bool mbar_try(uint32_t bar, uint32_t parity) {
         : "memory");
     return ok != 0;
 }
-// Bounded wait: true when the phase completed, false (flag set) on expiry.
-__device__ __forceinline__ bool mbar_wait(uint32_t bar, uint32_t parity, int *flag) {
+// Bounded wait: true when the phase completed, false on expiry (which sets
+// the flag) or once another thread has set the flag.  The flag and the clock
+// are looked at every 64th try, so that waiting threads do not flood the
+// memory pipeline with loads of the flag.  Roles off the critical path pass
+// sleep_ns > 0 and back off between tries, leaving issue slots to the warps
+// that convert weights and issue MMAs.
+__device__ __forceinline__ bool mbar_wait(uint32_t bar, uint32_t parity, int *flag, unsigned sleep_ns = 0) {
     if (mbar_try(bar, parity)) return true;
-    long long t0 = clock64();
-    while (!mbar_try(bar, parity)) {
-        if (clock64() - t0 > SPIN_LIMIT || *(volatile int *)flag) {
-            atomicExch(flag, HD_E_TIMEOUT);
-            return false;
+    const long long t0 = clock64();
+    for (unsigned it = 1;; it++) {
+        if (sleep_ns) __nanosleep(sleep_ns);
+        if (mbar_try(bar, parity)) return true;
+        if ((it & 63) == 0) {
+            if (*(volatile int *)flag) return false;
+            if (clock64() - t0 > SPIN_LIMIT) {
+                atomicExch(flag, HD_E_TIMEOUT);
+                return false;
+            }
         }
     }
-    return true;
+}
+// Bounded by time only: for waits on the CTA's own asynchronous work (copies,
+// MMAs) that must end before the CTA exits, also after an error.
+__device__ __forceinline__ void mbar_wait_quiet(uint32_t bar, uint32_t parity) {
+    const long long t0 = clock64();
+    while (!mbar_try(bar, parity))
+        if (clock64() - t0 > SPIN_LIMIT) return;
 }
 __device__ __forceinline__ void fence_async_smem() { asm volatile("fence.proxy.async.shared::cta;" ::: "memory"); }
 __device__ __forceinline__ void tc_fence_before() { asm volatile("tcgen05.fence::before_thread_sync;" ::: "memory"); }
@@ -337,36 +356,36 @@ cudaError_t launch_tc(hd_ctx *ctx, const hd_weight *w, const float *X, float *Y,
 }
 
 
-// ------------------------------------------------------------------- v2
-// Same MMA/TMEM structure, with every operand streamed asynchronously:
-// activations are converted to bf16 once and arrive by TMA (2-D tiled copy,
-// SWIZZLE_128B, straight into the layout the MMA reads); the raw quantized
-// bytes of each 128-row x 2-unit stage arrive by 1-D bulk copies, STAGES
-// ahead of use.  Eight warps dequantize shared -> shared (raw bytes -> bf16
-// swizzled rows), one warp issues the copies, one warp owns TMEM and the
-// MMAs.  Requires rows % 128 == 0 (every bulk copy is a whole, 16-byte
-// aligned span of 128 rows); other shapes use the v1 kernel above.
+// ------------------------------------------------------------------- v3
+// Persistent and streamed.  Each SM runs one CTA that walks work items
+// (128 weight rows x BT tokens, optionally one of two K halves) with three
+// concurrent pipelines:
+//   weights: the dequantizer threads copy their own raw quant bytes from
+//     global memory with coalesced cp.async, PD K-steps ahead of use, into
+//     per-thread shared slots, convert them to bf16 and store them with
+//     tcgen05.st into one of AS weight stages in tensor memory;
+//   activations: the bf16 tile of each K-step arrives by one TMA copy
+//     (SWIZZLE_128B K-major) into the X ring (XS stages); NXW copy warps take
+//     the steps in turn;
+//   MMA: one thread issues 4 tcgen05.mma (K = 16, A from tensor memory, B
+//     from shared memory) per step into one of two TMEM accumulators and
+//     releases weight and X stages by tcgen05.commit.
+// Why this shape.  (1) Shared-memory bandwidth (~128 B per cycle per SM) is
+// the scarce resource: the MMA alone reads its shared operands at ~96 B per
+// cycle at full rate, so bf16 weights written to and read from shared memory
+// (32 KB per 64-deep step) and an epilogue transposed through it held a
+// 64-deep step near 1000 cycles against 512 of MMA.  Weights in tensor memory
+// and an epilogue straight from registers leave the activations as the only
+// large shared-memory stream.  (2) The bulk-copy (TMA) operations that one
+// warp issues are processed one after another at ~500-700 cycles each
+// whatever their size, while those of different warps overlap; hence one
+// whole activation tile per operation and several copy warps.
+// Tensor memory (512 columns) holds two BT-column accumulators and the
+// weight stages, so BT is at most 208 (2 x 208 + 3 x 32 = 512).
+// Warps: 0-15 dequantize (thread = weight row x unit of the step x value
+// half), 16-18 activation copies, 19 TMEM + MMA, 20-23 epilogue.  Requires rows % 128 == 0;
+// other shapes use the v1 kernel above.
 
-template <int TYPE>
-struct Raw {
-    // byte offsets inside a stage's raw region (unit h = 0/1 of the pair)
-    static constexpr int Q = 0;                                        // q[h]
-    static constexpr int QB = TYPE == HD_TYPE_Q8_0 ? 4096 : 2048;      // bytes per unit of q (128 rows)
-    static constexpr int AUX = 2 * QB;                                 // Q5_0 qh[h] 512 B, Q6_K highs[h] 1 KB
-    static constexpr int AUXB = TYPE == HD_TYPE_Q5_0 ? 512 : TYPE == HD_TYPE_Q6_K ? 1024 : 0;
-    static constexpr int META = AUX + 2 * AUXB;                        // Q8_0/Q5_0 d[h] 256 B; Q4_K/Q6_K 2 KB per sb
-    static constexpr int METAB = (TYPE == HD_TYPE_Q8_0 || TYPE == HD_TYPE_Q5_0) ? 256 : 2048;
-    static constexpr int METAN = (TYPE == HD_TYPE_Q8_0 || TYPE == HD_TYPE_Q5_0) ? 2 : 1;
-    static constexpr int DSB = META + METAN * METAB;                   // Q6_K d 256 B
-    static constexpr int END = DSB + (TYPE == HD_TYPE_Q6_K ? 256 : 0);
-    static constexpr int BYTES = (END + 1023) & ~1023;
-};
-
-__device__ __forceinline__ void bulk_g2s(uint32_t dst, const void *src, uint32_t bytes, uint32_t bar) {
-    asm volatile("cp.async.bulk.shared::cluster.global.mbarrier::complete_tx::bytes [%0], [%1], %2, [%3];" ::"r"(dst),
-                 "l"(src), "r"(bytes), "r"(bar)
-                 : "memory");
-}
 __device__ __forceinline__ void tma_2d(uint32_t dst, const CUtensorMap *tm, int x, int y, uint32_t bar) {
     asm volatile(
         "cp.async.bulk.tensor.2d.shared::cluster.global.mbarrier::complete_tx::bytes [%0], [%1, {%2, %3}], [%4];" ::"r"(
@@ -378,111 +397,244 @@ __device__ __forceinline__ void mbar_expect_tx(uint32_t bar, uint32_t bytes) {
     asm volatile("mbarrier.arrive.expect_tx.shared::cta.b64 _, [%0], %1;" ::"r"(bar), "r"(bytes) : "memory");
 }
 
-// 32 values of unit u (pair half h) of row r from a stage's raw bytes.
+// Raw words of one unit of one row (decoded into bf16 by dq_store).
+struct DqRaw {
+    uint4 q0, q1;  // packed quants (q1: bytes 16-31, Q8_0 only)
+    uint4 m;       // Q4_K: d, dmin, 12 scale bytes; Q6_K: 16 int8 sub-scales
+    uint2 hb;      // Q6_K high bit pairs
+    uint32_t qh;   // Q5_0 fifth bits
+    uint32_t d;    // Q8_0 / Q5_0 block scale, Q6_K super-block scale (fp16 bits in the low half)
+};
+
+// Per-thread raw slots of the dequantizers, structure of arrays over the 256
+// threads of the role: region Q (16 B each), M (16 B: Q8_0 quant bytes 16-31,
+// Q4_K/Q6_K scales), HB (8 B, Q6_K high bits), W0 (4 B: Q5_0 fifth bits) and
+// W1 (4 B: the aligned 32-bit word holding the fp16 scale).
 template <int TYPE>
-__device__ __forceinline__ void raw_values(const uint8_t *raw, int r, int h, int u, float (&v)[32]) {
-    using R = Raw<TYPE>;
+struct RawSlot {
+    static constexpr int Q = 0, M = 16 * 256;
+    static constexpr bool HAS_M = TYPE != HD_TYPE_Q5_0;
+    static constexpr int HB = M + (HAS_M ? 16 * 256 : 0);
+    static constexpr bool HAS_HB = TYPE == HD_TYPE_Q6_K;
+    static constexpr int W0 = HB + (HAS_HB ? 8 * 256 : 0);
+    static constexpr bool HAS_W0 = TYPE == HD_TYPE_Q5_0;
+    static constexpr int W1 = W0 + (HAS_W0 ? 4 * 256 : 0);
+    static constexpr bool HAS_W1 = TYPE != HD_TYPE_Q4_K;
+    static constexpr int BYTES = W1 + (HAS_W1 ? 4 * 256 : 0);
+};
+
+__device__ __forceinline__ void cp_async16(uint32_t dst, const void *src) {
+    asm volatile("cp.async.cg.shared.global [%0], [%1], 16;" ::"r"(dst), "l"(src) : "memory");
+}
+__device__ __forceinline__ void cp_async8(uint32_t dst, const void *src) {
+    asm volatile("cp.async.ca.shared.global [%0], [%1], 8;" ::"r"(dst), "l"(src) : "memory");
+}
+__device__ __forceinline__ void cp_async4(uint32_t dst, const void *src) {
+    asm volatile("cp.async.ca.shared.global [%0], [%1], 4;" ::"r"(dst), "l"(src) : "memory");
+}
+__device__ __forceinline__ void cp_async_commit() { asm volatile("cp.async.commit_group;" ::: "memory"); }
+template <int N>
+__device__ __forceinline__ void cp_async_wait() { asm volatile("cp.async.wait_group %0;" ::"n"(N) : "memory"); }
+
+// Starts the asynchronous copies of the raw bytes of unit u of weight row
+// `row` into entry e of a raw slot (global -> shared, no registers held).
+// The two threads of an entry share the work: part 0 copies the 16 quant
+// bytes (Q8_0: bytes 0-15), part 1 the rest (Q8_0: bytes 16-31 and scale).
+template <int TYPE>
+__device__ __forceinline__ void dq_fetch(const WView &w, int64_t row, int u, uint8_t *slot, int e, int part) {
+    using RS = RawSlot<TYPE>;
+    const int64_t ur = (int64_t)u * w.rows + row;
+    const uint32_t sb = smem_u32(slot);
+    if (part == 0) {
+        cp_async16(sb + RS::Q + 16 * e, w.q + ur * (TYPE == HD_TYPE_Q8_0 ? 32 : 16));
+        return;
+    }
     if constexpr (TYPE == HD_TYPE_Q8_0) {
-        const uint4 *p = (const uint4 *)(raw + R::Q + h * R::QB + r * 32);
-        uint4 a = p[0], b = p[1];
-        float d = h2f(*(const uint16_t *)(raw + R::META + h * R::METAB + r * 2));
-        uint32_t wd[8] = {a.x, a.y, a.z, a.w, b.x, b.y, b.z, b.w};
-#pragma unroll
-        for (int i = 0; i < 8; i++) {
-            uint32_t x = wd[i] ^ 0x80808080u;
-#pragma unroll
-            for (int c = 0; c < 4; c++) v[4 * i + c] = (mag(x, c) - 8388736.0f) * d;
-        }
+        cp_async16(sb + RS::M + 16 * e, w.q + ur * 32 + 16);
+        cp_async4(sb + RS::W1 + 4 * e, (const unsigned short *)w.meta + (ur & ~(int64_t)1));
     } else if constexpr (TYPE == HD_TYPE_Q5_0) {
-        uint4 a = *(const uint4 *)(raw + R::Q + h * R::QB + r * 16);
-        uint32_t qh = *(const uint32_t *)(raw + R::AUX + h * R::AUXB + r * 4);
-        float d = h2f(*(const uint16_t *)(raw + R::META + h * R::METAB + r * 2));
-        uint32_t wd[4] = {a.x, a.y, a.z, a.w};
-#pragma unroll
-        for (int i = 0; i < 4; i++) {
-            uint32_t lo = (wd[i] & 0x0F0F0F0Fu) | ((qh >> i) & 0x10101010u);
-            uint32_t hi = ((wd[i] >> 4) & 0x0F0F0F0Fu) | ((qh << (4 - i)) & 0x10101010u);
-#pragma unroll
-            for (int c = 0; c < 4; c++) {
-                v[4 * i + c] = (mag(lo, c) - 8388624.0f) * d;
-                v[16 + 4 * i + c] = (mag(hi, c) - 8388624.0f) * d;
-            }
-        }
+        cp_async4(sb + RS::W0 + 4 * e, (const unsigned int *)w.aux + ur);
+        cp_async4(sb + RS::W1 + 4 * e, (const unsigned short *)w.meta + (ur & ~(int64_t)1));
     } else if constexpr (TYPE == HD_TYPE_Q4_K) {
-        uint4 a = *(const uint4 *)(raw + R::Q + h * R::QB + r * 16);
-        uint4 m = *(const uint4 *)(raw + R::META + r * 16);
-        int sc, mn;
-        q4k_sm_regs(u & 7, m.y, m.z, m.w, sc, mn);
-        float d1 = h2f((uint16_t)(m.x & 0xFFFF)) * (float)sc, m1 = h2f((uint16_t)(m.x >> 16)) * (float)mn;
-        uint32_t wd[4] = {a.x, a.y, a.z, a.w};
+        cp_async16(sb + RS::M + 16 * e, w.meta + ((int64_t)(u >> 3) * w.rows + row) * 16);
+    } else {
+        const int64_t sr = (int64_t)(u >> 3) * w.rows + row;
+        cp_async8(sb + RS::HB + 8 * e, (const uint2 *)w.aux + ur);
+        cp_async16(sb + RS::M + 16 * e, w.meta + sr * 16);
+        cp_async4(sb + RS::W1 + 4 * e, w.dsb + (sr & ~(int64_t)1));
+    }
+}
+
+// Reads back what value half `part` of entry e needs; `odd` selects the fp16
+// half of the 32-bit scale word (the parity of the element's index).
+template <int TYPE>
+__device__ __forceinline__ void dq_read(const uint8_t *slot, int e, int part, bool odd, DqRaw &g) {
+    using RS = RawSlot<TYPE>;
+    g.q0 = *(const uint4 *)(slot + ((TYPE == HD_TYPE_Q8_0 && part) ? RS::M : RS::Q) + 16 * e);
+    if constexpr (TYPE == HD_TYPE_Q4_K || TYPE == HD_TYPE_Q6_K) g.m = *(const uint4 *)(slot + RS::M + 16 * e);
+    if constexpr (RS::HAS_HB) g.hb = *(const uint2 *)(slot + RS::HB + 8 * e);
+    if constexpr (RS::HAS_W0) g.qh = *(const uint32_t *)(slot + RS::W0 + 4 * e);
+    if constexpr (RS::HAS_W1) g.d = (*(const uint32_t *)(slot + RS::W1 + 4 * e)) >> (odd ? 16 : 0);
+}
+
+// bf16x2 pairs straight from quant bytes (Q5_0, Q4_K, Q6_K: q < 128).  One
+// byte_perm places two bytes under the bf16 exponent byte 0x43, giving the
+// exact values 128 + q; one __hsub2 removes 128 + offset exactly; the scale is
+// applied in bf16 (for the bf16 tensor-core path only).
+__device__ __forceinline__ __nv_bfloat162 pair_bf16(uint32_t v, uint32_t sel) {
+    uint32_t b = __byte_perm(v, 0x43434343u, sel);
+    return *reinterpret_cast<__nv_bfloat162 *>(&b);
+}
+__device__ __forceinline__ uint32_t bits2(__nv_bfloat162 x) { return *reinterpret_cast<uint32_t *>(&x); }
+
+// Values 16*part .. 16*part+15 of unit u (zeros when !valid) as 8 packed
+// bf16 pairs, word j = values (16*part + 2j, +1), the lower K index in the
+// low half.  For Q8_0, g.q0 holds the 16 quant bytes of that half.
+template <int TYPE>
+__device__ __forceinline__ void dq_words(int u, int part, bool valid, const DqRaw &g, uint32_t (&o)[8]) {
+    if (!valid) {
+#pragma unroll
+        for (int j = 0; j < 8; j++) o[j] = 0u;
+    } else if constexpr (TYPE == HD_TYPE_Q8_0) {
+        const float d = h2f((uint16_t)g.d);
+        const uint32_t wd[4] = {g.q0.x, g.q0.y, g.q0.z, g.q0.w};
 #pragma unroll
         for (int i = 0; i < 4; i++) {
-            uint32_t lo = wd[i] & 0x0F0F0F0Fu, hi = (wd[i] >> 4) & 0x0F0F0F0Fu;
-#pragma unroll
-            for (int c = 0; c < 4; c++) {
-                v[4 * i + c] = (mag(lo, c) - 8388608.0f) * d1 - m1;
-                v[16 + 4 * i + c] = (mag(hi, c) - 8388608.0f) * d1 - m1;
-            }
+            const uint32_t x = wd[i] ^ 0x80808080u;
+            o[2 * i] = pack_bf16((mag(x, 0) - 8388736.0f) * d, (mag(x, 1) - 8388736.0f) * d);
+            o[2 * i + 1] = pack_bf16((mag(x, 2) - 8388736.0f) * d, (mag(x, 3) - 8388736.0f) * d);
         }
     } else {
-        uint4 a = *(const uint4 *)(raw + R::Q + h * R::QB + r * 16);
-        uint2 hb = *(const uint2 *)(raw + R::AUX + h * R::AUXB + r * 8);
-        const int8_t *scp = (const int8_t *)(raw + R::META + r * 16);
-        float d = h2f(*(const uint16_t *)(raw + R::DSB + r * 2));
-        int s0 = 2 * (u & 7);
-        float dl = d * (float)scp[s0], dh = d * (float)scp[s0 + 1];
-        uint32_t wd[4] = {a.x, a.y, a.z, a.w};
+        float sc, mn = 0.f;
+        if constexpr (TYPE == HD_TYPE_Q5_0) {
+            sc = h2f((uint16_t)g.d);
+        } else if constexpr (TYPE == HD_TYPE_Q4_K) {
+            int s6, m6;
+            q4k_sm_regs(u & 7, g.m.y, g.m.z, g.m.w, s6, m6);
+            sc = h2f((uint16_t)(g.m.x & 0xFFFF)) * (float)s6;
+            mn = -h2f((uint16_t)(g.m.x >> 16)) * (float)m6;
+        } else {
+            // sub-scale 2(u&7) + part: byte 2(u&1) + part of word (u&7)/2
+            const uint32_t sw = (u & 4) ? ((u & 2) ? g.m.w : g.m.z) : ((u & 2) ? g.m.y : g.m.x);
+            sc = h2f((uint16_t)g.d) * (float)(int8_t)((sw >> (8 * (2 * (u & 1) + part))) & 0xFF);
+        }
+        const uint32_t wd[4] = {g.q0.x, g.q0.y, g.q0.z, g.q0.w};
+        const __nv_bfloat162 off =
+            __float2bfloat162_rn(TYPE == HD_TYPE_Q5_0 ? 144.f : TYPE == HD_TYPE_Q4_K ? 128.f : 160.f);
+        const __nv_bfloat162 mlo = __float2bfloat162_rn(mn), s2 = __float2bfloat162_rn(sc);
 #pragma unroll
         for (int i = 0; i < 4; i++) {
-            int sh = 4 - 2 * i;
-            uint32_t hx = sh >= 0 ? (hb.x << sh) : (hb.x >> -sh), hy = sh >= 0 ? (hb.y << sh) : (hb.y >> -sh);
-            uint32_t lo = (wd[i] & 0x0F0F0F0Fu) | (hx & 0x30303030u);
-            uint32_t hi = ((wd[i] >> 4) & 0x0F0F0F0Fu) | (hy & 0x30303030u);
-#pragma unroll
-            for (int c = 0; c < 4; c++) {
-                v[4 * i + c] = (mag(lo, c) - 8388640.0f) * dl;
-                v[16 + 4 * i + c] = (mag(hi, c) - 8388640.0f) * dh;
+            uint32_t b;
+            if constexpr (TYPE == HD_TYPE_Q5_0) {
+                b = part ? (((wd[i] >> 4) & 0x0F0F0F0Fu) | ((g.qh << (4 - i)) & 0x10101010u))
+                         : ((wd[i] & 0x0F0F0F0Fu) | ((g.qh >> i) & 0x10101010u));
+            } else if constexpr (TYPE == HD_TYPE_Q4_K) {
+                b = (wd[i] >> (4 * part)) & 0x0F0F0F0Fu;
+            } else {
+                const int sh = 4 - 2 * i;
+                const uint32_t hsel = part ? g.hb.y : g.hb.x;
+                const uint32_t hx = sh >= 0 ? (hsel << sh) : (hsel >> -sh);
+                b = ((wd[i] >> (4 * part)) & 0x0F0F0F0Fu) | (hx & 0x30303030u);
             }
+            o[2 * i] = bits2(__hfma2(__hsub2(pair_bf16(b, 0x5140u), off), s2, mlo));
+            o[2 * i + 1] = bits2(__hfma2(__hsub2(pair_bf16(b, 0x7362u), off), s2, mlo));
         }
     }
 }
 
+// Stores 8 words per thread into 8 consecutive TMEM columns of the thread's
+// lane (warp w reaches lanes 32*(w%4)..), and waits for the store.
+__device__ __forceinline__ void tmem_st8(uint32_t taddr, const uint32_t (&o)[8]) {
+    asm volatile("tcgen05.st.sync.aligned.32x32b.x8.b32 [%0], {%1,%2,%3,%4,%5,%6,%7,%8};" ::"r"(taddr), "r"(o[0]),
+                 "r"(o[1]), "r"(o[2]), "r"(o[3]), "r"(o[4]), "r"(o[5]), "r"(o[6]), "r"(o[7])
+                 : "memory");
+    asm volatile("tcgen05.wait::st.sync.aligned;" ::: "memory");
+}
+
+constexpr int DQ_WARPS = 16, DQ_THREADS = DQ_WARPS * 32;
+constexpr int NXW = 3;                                  // activation copy warps
+constexpr int W_X = DQ_WARPS, W_MMA = W_X + NXW, W_EPI = W_MMA + 1;
+constexpr int TC3_THREADS = (W_EPI + 4) * 32;
+
+// Shared memory: XS activation stages and PD raw slots for the dequantizers
+// (the weight bytes of PD K-steps in flight).  Tensor memory (512 columns):
+// two fp32 accumulators of BT columns, then AS bf16 weight stages of 32
+// columns (128 rows x 64 K values, two per column) that the MMA reads as A.
 template <int TYPE, int BT>
-struct TC2 {
-    static constexpr int STAGES = BT >= 256 ? 3 : 4;
-    static constexpr int XB = BT * 128;                       // bf16 activation tile
-    static constexpr int STAGE = A_BYTES + XB + Raw<TYPE>::BYTES;
-    static constexpr size_t SMEM = (size_t)STAGES * STAGE + 1024;
+struct TC3 {
+    static constexpr int XB = BT * BK * 2;
+    static constexpr int RB = RawSlot<TYPE>::BYTES;
+    static constexpr int AS = (512 - 2 * BT) / 32 > 4 ? 4 : (512 - 2 * BT) / 32;
+    static constexpr int A_COL = 2 * BT;
+    static_assert(AS >= 2, "tensor memory plan");
+    static constexpr int XS = BT >= 192 ? 6 : 8;
+    static constexpr int R_OFF = XS * XB;
+    static constexpr int FREE = 227 * 1024 - 1024 - 512 - R_OFF;
+    static constexpr int PD = FREE / RB > 6 ? 6 : FREE / RB;
+    static_assert(PD >= 2, "shared memory plan");
+    static constexpr size_t SMEM = (size_t)R_OFF + PD * RB + 1024;
 };
 
+// The (item, K-step) sequence of this CTA: items blockIdx.x, +gridDim.x, ...;
+// item = tile + ntiles * (K part); steps k0..k1-1 of its K part.  row0 is
+// the first weight row of the item's tile (divisions once per item).
+struct StepCursor {
+    int item, ks, k1, row0;
+    __device__ __forceinline__ void range(int ntiles, int ntm, int kper, int ksteps) {
+        ks = (item / ntiles) * kper;
+        k1 = min(ksteps, ks + kper);
+        row0 = ((item % ntiles) % ntm) * 128;
+    }
+    __device__ __forceinline__ void start(int nitems, int ntiles, int ntm, int kper, int ksteps) {
+        item = blockIdx.x;
+        if (item < nitems) range(ntiles, ntm, kper, ksteps);
+    }
+    __device__ __forceinline__ void next(int nitems, int ntiles, int ntm, int kper, int ksteps) {
+        if (++ks < k1) return;
+        item += gridDim.x;
+        if (item < nitems) range(ntiles, ntm, kper, ksteps);
+    }
+};
+
+// Persistent: an item is a tile (row tile fastest, so CTAs running at the
+// same time share an activation tile in L2) and, when the tiles alone would
+// leave SMs idle, one of two K halves (KS = 2: both halves add into Y, zeroed
+// beforehand; two addends onto zero commute, so the sum is order-independent).
 template <int TYPE, int BT>
-__global__ void __launch_bounds__(320, 1) k_qgemm_tc2(WView w, const __grid_constant__ CUtensorMap tmx,
-                                                     float *__restrict__ Y, int T, int N, int *flag) {
-    using C = TC2<TYPE, BT>;
-    using R = Raw<TYPE>;
-    constexpr int ST = C::STAGES;
+__global__ void __launch_bounds__(TC3_THREADS, 1)
+    k_qgemm_tc3(WView w, const __grid_constant__ CUtensorMap tmx, float *__restrict__ Y, int T, int N, int ntm,
+                int ntiles, int KS, int *flag) {
+    using C = TC3<TYPE, BT>;
+    constexpr int XS = C::XS, AS = C::AS, PD = C::PD;
     extern __shared__ uint8_t smem_raw[];
-    __shared__ __align__(8) uint64_t load_full[ST], a_full[ST], stage_empty[ST], acc_bar;
+    __shared__ __align__(8) uint64_t x_full[XS], x_empty[XS], a_full[AS], a_empty[AS];
+    __shared__ __align__(8) uint64_t acc_full[2], acc_empty[2], fin_bar;
     __shared__ uint32_t tmem_base_sh;
 
     const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
-    const int n0 = blockIdx.x * 128, t0 = blockIdx.y * BT;
     const int units = w.units, ksteps = (units + 1) / 2;
     uint8_t *base = (uint8_t *)(((uintptr_t)smem_raw + 1023) & ~(uintptr_t)1023);
 
     if (threadIdx.x == 0) {
-        for (int s = 0; s < ST; s++) {
-            mbar_init(smem_u32(&load_full[s]), 1);
-            mbar_init(smem_u32(&a_full[s]), 256);
-            mbar_init(smem_u32(&stage_empty[s]), 1);
+        for (int s = 0; s < XS; s++) {
+            mbar_init(smem_u32(&x_full[s]), 1);
+            mbar_init(smem_u32(&x_empty[s]), 1);
         }
-        mbar_init(smem_u32(&acc_bar), 1);
+        for (int s = 0; s < AS; s++) {
+            mbar_init(smem_u32(&a_full[s]), DQ_THREADS);
+            mbar_init(smem_u32(&a_empty[s]), 1);
+        }
+        for (int i = 0; i < 2; i++) {
+            mbar_init(smem_u32(&acc_full[i]), 1);
+            mbar_init(smem_u32(&acc_empty[i]), 128);
+        }
+        mbar_init(smem_u32(&fin_bar), 1);
         asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
         asm volatile("prefetch.tensormap [%0];" ::"l"((uint64_t)&tmx) : "memory");
     }
-    if (warp == 9) {
+    if (warp == W_MMA) {
         asm volatile("tcgen05.alloc.cta_group::1.sync.aligned.shared::cta.b32 [%0], %1;" ::"r"(smem_u32(&tmem_base_sh)),
-                     "r"(BT));
+                     "r"(512));
         asm volatile("tcgen05.relinquish_alloc_permit.cta_group::1.sync.aligned;");
     }
     tc_fence_before();
@@ -492,118 +644,177 @@ __global__ void __launch_bounds__(320, 1) k_qgemm_tc2(WView w, const __grid_cons
     pdl_wait();
     pdl_trigger();
 
-    if (warp == 8) {
-        // ---- copy engine driver
+    const int kper = (ksteps + KS - 1) / KS, nitems = ntiles * KS;
+    if (warp < DQ_WARPS) {
+        // ---- dequantizers: thread (weight row r, unit h of the step, value
+        // half part).  The two threads of a (row, unit) entry copy its raw
+        // bytes (cp.async) into a raw slot PD - 1 steps ahead; a named barrier
+        // over the role makes every copy of step g visible before any thread
+        // reads it, and also tells that every thread is done with step g - 1,
+        // whose slot is then refilled.
+        const int e = threadIdx.x & 255, r = e & 127, h = e >> 7, part = threadIdx.x >> 8;
+        uint8_t *slots = base + C::R_OFF;
+        StepCursor cl, cc;  // fetch cursor PD - 1 steps ahead of the compute cursor
+        bool alive = true;
+        cl.start(nitems, ntiles, ntm, kper, ksteps);
+        cc = cl;
+        for (int j = 0; j < PD - 1; j++) {
+            if (cl.item < nitems) {
+                const int u = 2 * cl.ks + h;
+                if (u < units) dq_fetch<TYPE>(w, (int64_t)(cl.row0 + r), u, slots + j * C::RB, e, part);
+                cl.next(nitems, ntiles, ntm, kper, ksteps);
+            }
+            cp_async_commit();
+        }
+        for (int g = 0; cc.item < nitems; g++) {
+            const int as = g % AS;
+            cp_async_wait<PD - 2>();   // this thread's copies of step g have landed
+            asm volatile("bar.sync 1, %0;" ::"n"(DQ_THREADS) : "memory");
+            if (cl.item < nitems) {
+                const int ul = 2 * cl.ks + h;
+                if (ul < units)
+                    dq_fetch<TYPE>(w, (int64_t)(cl.row0 + r), ul, slots + ((g + PD - 1) % PD) * C::RB, e, part);
+                cl.next(nitems, ntiles, ntm, kper, ksteps);
+            }
+            cp_async_commit();
+            const int u = 2 * cc.ks + h;
+            DqRaw rg;
+            if (u < units) dq_read<TYPE>(slots + (g % PD) * C::RB, e, part, r & 1, rg);
+            uint32_t o[8];
+            dq_words<TYPE>(u, part, u < units, rg, o);
+            // After a failed wait the thread stops storing but keeps its place
+            // in the loop, so that every thread takes the named barrier
+            // equally often.
+            alive = alive && mbar_wait(smem_u32(&a_empty[as]), ((g / AS) & 1) ^ 1, flag);
+            if (alive) {
+                tc_fence_after();
+                tmem_st8(tmem + ((uint32_t)(32 * (warp & 3)) << 16) + (uint32_t)(C::A_COL + 32 * as + 16 * h + 8 * part),
+                         o);
+                tc_fence_before();
+            }
+            mbar_arrive(smem_u32(&a_full[as]));
+            cc.next(nitems, ntiles, ntm, kper, ksteps);
+        }
+        cp_async_wait<0>();
+    } else if (warp < W_MMA) {
+        // ---- activation copies: warp j issues the steps g with g % NXW == j
         if (lane == 0) {
-            for (int ks = 0; ks < ksteps; ks++) {
-                const int s = ks % ST, round = ks / ST;
-                if (!mbar_wait(smem_u32(&stage_empty[s]), (round & 1) ^ 1, flag)) break;
-                uint8_t *stg = base + s * C::STAGE;
-                const uint32_t bar = smem_u32(&load_full[s]);
-                const int ua = 2 * ks, ub = 2 * ks + 1;
-                const bool has_b = ub < units;
-                uint32_t bytes = C::XB + (has_b ? 2 : 1) * (R::QB + R::AUXB);
-                if (R::METAN == 2) bytes += (has_b ? 2 : 1) * R::METAB;
-                else bytes += R::METAB;
-                if (TYPE == HD_TYPE_Q6_K) bytes += 256;
-                mbar_expect_tx(bar, bytes);
-                tma_2d(smem_u32(stg + A_BYTES), &tmx, ks * BK, t0, bar);
-                uint8_t *raw = stg + A_BYTES + C::XB;
-                for (int h = 0; h < (has_b ? 2 : 1); h++) {
-                    const int u = ua + h;
-                    const int64_t ur = (int64_t)u * w.rows + n0;
-                    bulk_g2s(smem_u32(raw + R::Q + h * R::QB), w.q + ur * (R::QB / 128), R::QB, bar);
-                    if (R::AUXB) bulk_g2s(smem_u32(raw + R::AUX + h * R::AUXB), w.aux + ur * (R::AUXB / 128), R::AUXB, bar);
-                    if (R::METAN == 2) bulk_g2s(smem_u32(raw + R::META + h * R::METAB), w.meta + ur * 2, R::METAB, bar);
-                }
-                if (R::METAN == 1) {
-                    const int64_t sr = (int64_t)(ua >> 3) * w.rows + n0;
-                    bulk_g2s(smem_u32(raw + R::META), w.meta + sr * 16, R::METAB, bar);
-                    if (TYPE == HD_TYPE_Q6_K) bulk_g2s(smem_u32(raw + R::DSB), w.dsb + sr, 256, bar);
+            const int j = warp - W_X;
+            int g = 0, last[XS];
+            for (int s = 0; s < XS; s++) last[s] = -1;
+            bool alive = true;
+            for (int item = blockIdx.x; item < nitems && alive; item += gridDim.x) {
+                const int t0 = ((item % ntiles) / ntm) * BT;
+                const int k0 = (item / ntiles) * kper, k1 = min(ksteps, k0 + kper);
+                for (int ks = k0; ks < k1; ks++, g++) {
+                    if (g % NXW != j) continue;
+                    const int s = g % XS;
+                    if (!mbar_wait(smem_u32(&x_empty[s]), ((g / XS) & 1) ^ 1, flag, 64)) { alive = false; break; }
+                    const uint32_t bar = smem_u32(&x_full[s]);
+                    mbar_expect_tx(bar, C::XB);
+                    tma_2d(smem_u32(base + s * C::XB), &tmx, ks * BK, t0, bar);
+                    last[s] = g;
                 }
             }
+            // On an early exit, this warp's copies still in flight land before
+            // the CTA does (on a normal exit the MMA has consumed them all).
+            if (!alive)
+                for (int s = 0; s < XS; s++)
+                    if (last[s] >= 0) mbar_wait_quiet(smem_u32(&x_full[s]), (last[s] / XS) & 1);
         }
         __syncwarp();
-    } else if (warp == 9) {
+    } else if (warp == W_MMA) {
         // ---- MMA issuer
         if (lane == 0) {
             constexpr uint32_t idesc = idesc_bf16(BT);
-            for (int ks = 0; ks < ksteps; ks++) {
-                const int s = ks % ST, round = ks / ST;
-                if (!mbar_wait(smem_u32(&a_full[s]), round & 1, flag)) break;
+            int g = 0, li = 0;
+            bool alive = true;
+            for (int item = blockIdx.x; item < nitems && alive; item += gridDim.x, li++) {
+                const int buf = li & 1;
+                const int k0 = (item / ntiles) * kper, k1 = min(ksteps, k0 + kper);
+                if (!mbar_wait(smem_u32(&acc_empty[buf]), ((li >> 1) & 1) ^ 1, flag)) break;
                 tc_fence_after();
-                uint8_t *stg = base + s * C::STAGE;
-                const uint32_t a0 = smem_u32(stg), b0 = smem_u32(stg + A_BYTES);
+                const uint32_t d = tmem + (uint32_t)(buf * BT);
+                for (int ks = k0; ks < k1; ks++, g++) {
+                    const int xs = g % XS, as = g % AS;
+                    if (!mbar_wait(smem_u32(&x_full[xs]), (g / XS) & 1, flag) ||
+                        !mbar_wait(smem_u32(&a_full[as]), (g / AS) & 1, flag)) {
+                        alive = false;
+                        break;
+                    }
+                    tc_fence_after();
+                    const uint32_t a0 = tmem + (uint32_t)(C::A_COL + 32 * as), b0 = smem_u32(base + xs * C::XB);
 #pragma unroll
-                for (int kk = 0; kk < BK / 16; kk++) {
-                    uint64_t ad = sw128_desc(a0 + kk * 32), bd = sw128_desc(b0 + kk * 32);
-                    uint32_t acc = (ks > 0 || kk > 0) ? 1u : 0u;
-                    asm volatile(
-                        "{\n .reg .pred p;\n setp.ne.b32 p, %4, 0;\n"
-                        " tcgen05.mma.cta_group::1.kind::f16 [%0], %1, %2, %3, p;\n}\n" ::"r"(tmem),
-                        "l"(ad), "l"(bd), "r"(idesc), "r"(acc));
+                    for (int kk = 0; kk < BK / 16; kk++) {
+                        const uint64_t bd = sw128_desc(b0 + kk * 32);
+                        const uint32_t acc = (ks > k0 || kk > 0) ? 1u : 0u;
+                        asm volatile(
+                            "{\n .reg .pred p;\n setp.ne.b32 p, %4, 0;\n"
+                            " tcgen05.mma.cta_group::1.kind::f16 [%0], [%1], %2, %3, p;\n}\n" ::"r"(d),
+                            "r"(a0 + 8 * kk), "l"(bd), "r"(idesc), "r"(acc));
+                    }
+                    asm volatile("tcgen05.commit.cta_group::1.mbarrier::arrive::one.shared::cluster.b64 [%0];" ::"r"(
+                                     smem_u32(&x_empty[xs]))
+                                 : "memory");
+                    asm volatile("tcgen05.commit.cta_group::1.mbarrier::arrive::one.shared::cluster.b64 [%0];" ::"r"(
+                                     smem_u32(&a_empty[as]))
+                                 : "memory");
                 }
                 asm volatile("tcgen05.commit.cta_group::1.mbarrier::arrive::one.shared::cluster.b64 [%0];" ::"r"(
-                                 smem_u32(&stage_empty[s]))
+                                 smem_u32(&acc_full[buf]))
                              : "memory");
             }
+            // Completion of this commit covers every MMA issued above; it is
+            // awaited also after a timeout, before TMEM is freed.
             asm volatile("tcgen05.commit.cta_group::1.mbarrier::arrive::one.shared::cluster.b64 [%0];" ::"r"(
-                             smem_u32(&acc_bar))
+                             smem_u32(&fin_bar))
                          : "memory");
+            mbar_wait_quiet(smem_u32(&fin_bar), 0);
         }
         __syncwarp();
     } else {
-        // ---- dequantizers: thread (row r, unit half h) of each stage
-        const int r = threadIdx.x & 127, h = threadIdx.x >> 7;
-        for (int ks = 0; ks < ksteps; ks++) {
-            const int s = ks % ST, round = ks / ST;
-            if (!mbar_wait(smem_u32(&load_full[s]), round & 1, flag)) break;
-            uint8_t *stg = base + s * C::STAGE;
-            const int u = 2 * ks + h;
-            float v[32];
-            if (u < units) {
-                raw_values<TYPE>(stg + A_BYTES + C::XB, r, h, u, v);
-            } else {
-#pragma unroll
-                for (int j = 0; j < 32; j++) v[j] = 0.f;
-            }
-            store_sw128(stg, r, 4 * h, v);
-            fence_async_smem();
-            mbar_arrive(smem_u32(&a_full[s]));
-        }
-    }
-
-    // ---- epilogue: warps 0-7
-    if (warp < 8) {
-        const bool ok = mbar_wait(smem_u32(&acc_bar), 0, flag);
-        tc_fence_after();
-        const int q = warp & 3, half = warp >> 2;
-        const int64_t n = n0 + 32 * q + lane;
-        for (int c0 = half * (BT / 2); c0 < (half + 1) * (BT / 2); c0 += 16) {
-            uint32_t rr[16];
-            const uint32_t taddr = tmem + ((uint32_t)(32 * q) << 16) + (uint32_t)c0;
-            asm volatile(
-                "tcgen05.ld.sync.aligned.32x32b.x16.b32 {%0,%1,%2,%3,%4,%5,%6,%7,%8,%9,%10,%11,%12,%13,%14,%15}, "
-                "[%16];"
-                : "=r"(rr[0]), "=r"(rr[1]), "=r"(rr[2]), "=r"(rr[3]), "=r"(rr[4]), "=r"(rr[5]), "=r"(rr[6]),
-                  "=r"(rr[7]), "=r"(rr[8]), "=r"(rr[9]), "=r"(rr[10]), "=r"(rr[11]), "=r"(rr[12]), "=r"(rr[13]),
-                  "=r"(rr[14]), "=r"(rr[15])
-                : "r"(taddr));
-            asm volatile("tcgen05.wait::ld.sync.aligned;" ::: "memory");
-            if (ok && n < N) {
+        // ---- epilogue: warp quarter q reads TMEM lanes 32q.. (weight rows),
+        // 16 token columns at a time; each store instruction writes 32
+        // consecutive weight rows of one token (128 contiguous bytes of Y).
+        const int q = warp & 3;
+        int li = 0;
+        for (int item = blockIdx.x; item < nitems; item += gridDim.x, li++) {
+            const int buf = li & 1, tile = item % ntiles;
+            const int64_t n = (int64_t)(tile % ntm) * 128 + 32 * q + lane;
+            const int t0 = (tile / ntm) * BT;
+            const bool ok = mbar_wait(smem_u32(&acc_full[buf]), (li >> 1) & 1, flag, 128);
+            tc_fence_after();
+            for (int c0 = 0; ok && c0 < BT && t0 + c0 < T; c0 += 16) {
+                uint32_t rr[16];
+                const uint32_t taddr = tmem + ((uint32_t)(32 * q) << 16) + (uint32_t)(buf * BT + c0);
+                asm volatile(
+                    "tcgen05.ld.sync.aligned.32x32b.x16.b32 {%0,%1,%2,%3,%4,%5,%6,%7,%8,%9,%10,%11,%12,%13,%14,%15}, "
+                    "[%16];"
+                    : "=r"(rr[0]), "=r"(rr[1]), "=r"(rr[2]), "=r"(rr[3]), "=r"(rr[4]), "=r"(rr[5]), "=r"(rr[6]),
+                      "=r"(rr[7]), "=r"(rr[8]), "=r"(rr[9]), "=r"(rr[10]), "=r"(rr[11]), "=r"(rr[12]), "=r"(rr[13]),
+                      "=r"(rr[14]), "=r"(rr[15])
+                    : "r"(taddr));
+                asm volatile("tcgen05.wait::ld.sync.aligned;" ::: "memory");
 #pragma unroll
                 for (int j = 0; j < 16; j++) {
                     const int t = t0 + c0 + j;
-                    if (t < T) Y[(int64_t)t * N + n] = __uint_as_float(rr[j]);
+                    if (t < T) {
+                        float *dst = Y + (int64_t)t * N + n;
+                        if (KS == 1) *dst = __uint_as_float(rr[j]);
+                        else atomicAdd(dst, __uint_as_float(rr[j]));
+                    }
                 }
             }
+            tc_fence_before();
+            mbar_arrive(smem_u32(&acc_empty[buf]));
+            if (!ok) break;
         }
     }
     tc_fence_before();
     __syncthreads();
-    if (warp == 9) {
+    if (warp == W_MMA) {
         tc_fence_after();
-        asm volatile("tcgen05.dealloc.cta_group::1.sync.aligned.b32 %0, %1;" ::"r"(tmem), "r"(BT));
+        asm volatile("tcgen05.dealloc.cta_group::1.sync.aligned.b32 %0, %1;" ::"r"(tmem), "r"(512));
     }
 }
 
@@ -639,23 +850,29 @@ EncodeTiledFn encode_tiled() {
 }
 
 template <int TYPE, int BT>
-cudaError_t launch_tc2(hd_ctx *ctx, const hd_weight *w, const CUtensorMap &tm, float *Y, int T) {
-    constexpr size_t smem = TC2<TYPE, BT>::SMEM;
-    cudaError_t e = cudaFuncSetAttribute(k_qgemm_tc2<TYPE, BT>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
+cudaError_t launch_tc3(hd_ctx *ctx, const hd_weight *w, const CUtensorMap &tmx, float *Y, int T, int ks) {
+    constexpr size_t smem = TC3<TYPE, BT>::SMEM;
+    cudaError_t e = cudaFuncSetAttribute(k_qgemm_tc3<TYPE, BT>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
     if (e != cudaSuccess) return e;
-    dim3 grid((unsigned)(w->rows / 128), (unsigned)((T + BT - 1) / BT));
-    return hd_launch(ctx, k_qgemm_tc2<TYPE, BT>, grid, dim3(320), smem, wview(w), tm, Y, T, (int)w->rows, ctx->flag);
+    const int ntm = (int)(w->rows / 128), ntiles = ntm * ((T + BT - 1) / BT);
+    if (ks == 2) {
+        e = cudaMemsetAsync(Y, 0, (size_t)T * w->rows * sizeof(float), ctx->stream);
+        if (e != cudaSuccess) return e;
+    }
+    const int nitems = ntiles * ks;
+    const int grid = nitems < ctx->sm_count ? nitems : ctx->sm_count;
+    return hd_launch(ctx, k_qgemm_tc3<TYPE, BT>, dim3(grid), dim3(TC3_THREADS), smem, wview(w), tmx, Y, T,
+                     (int)w->rows, ntm, ntiles, ks, ctx->flag);
 }
 
 }  // namespace
 
-// Token tile: 128 (64 for short inputs), or 256 when that still gives two
-// tiles per SM.  rows % 128 == 0 uses the streamed v2 kernel.
+// rows % 128 == 0 uses the streamed v3 kernel, other shapes the v1 kernel.
 int hd_qgemm_tc(hd_ctx *ctx, const hd_weight *w, const float *X, float *Y, int T) {
     HD_REQUIRE(ctx, w->cols % 8 == 0, HD_E_SHAPE, "hd_qgemm: K must be a multiple of 8");
     const int64_t mt = (w->rows + 127) / 128;
     cudaError_t e = cudaSuccess;
-    if (w->rows % 128 == 0 && getenv("HACEDLE_TC_V1") == nullptr) {
+    if (w->rows % 128 == 0 && ((uintptr_t)Y & 15) == 0 && getenv("HACEDLE_TC_V1") == nullptr) {
         // bf16 copy of the activations for the TMA
         const size_t need = (size_t)T * w->cols * sizeof(__nv_bfloat16);
         int rc = hd_ensure_hbuf(ctx, &ctx->xbf, &ctx->xbf_bytes, (need + 3) / 4 * 4);
@@ -664,8 +881,26 @@ int hd_qgemm_tc(hd_ctx *ctx, const hd_weight *w, const float *X, float *Y, int T
         e = hd_launch(ctx, k_to_bf16, dim3((unsigned)((n / 4 + 255) / 256 + 1)), dim3(256), 0, X,
                       (__nv_bfloat16 *)ctx->xbf, n);
         if (e != cudaSuccess) return hd_fail(ctx, HD_E_CUDA, "hd_qgemm (bf16 convert): %s", cudaGetErrorString(e));
-        int bt = T <= 64 ? 64 : 128;
-        if (T > 128 && mt * ((T + 255) / 256) >= 2 * ctx->sm_count) bt = 256;
+        // Token tile and K split by a cost model: rounds of items per SM x
+        // steps per item x cycles per step (the MMA's 2*BT plus ~200 cycles of
+        // per-step overhead); ties go to the smaller tile.
+        const int ksteps = (int)((w->units + 1) / 2);
+        auto ksplit = [&](int cand) {
+            return (2 * mt * ((T + cand - 1) / cand) <= ctx->sm_count && w->units >= 8) ? 2 : 1;
+        };
+        int bt = 64;
+        double best = 1e30;
+        for (int cand : {64, 128, 208}) {
+            if (cand > 64 && T <= cand / 2) continue;
+            const int64_t tiles = mt * ((T + cand - 1) / cand);
+            const int ck = ksplit(cand);
+            const double rounds = (double)((tiles * ck + ctx->sm_count - 1) / ctx->sm_count);
+            const double cost = rounds * ((ksteps + ck - 1) / ck) * (2.0 * cand + 200.0);
+            if (cost < best - 1e-9) { best = cost; bt = cand; }
+        }
+        const char *bt_env = getenv("HACEDLE_TC_BT");
+        if (bt_env && (atoi(bt_env) == 64 || atoi(bt_env) == 128 || atoi(bt_env) == 208)) bt = atoi(bt_env);
+        const int ks = ksplit(bt);
         CUtensorMap tm;
         cuuint64_t dims[2] = {(cuuint64_t)w->cols, (cuuint64_t)T};
         cuuint64_t strides[1] = {(cuuint64_t)w->cols * 2};
@@ -678,11 +913,11 @@ int hd_qgemm_tc(hd_ctx *ctx, const hd_weight *w, const float *X, float *Y, int T
                                              CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
         if (cr != CUDA_SUCCESS) return hd_fail(ctx, HD_E_CUDA, "hd_qgemm: cuTensorMapEncodeTiled failed (%d)", (int)cr);
         HD_TYPE_SWITCH(w->type, TT, {
-            if (bt == 64) e = launch_tc2<TT, 64>(ctx, w, tm, Y, T);
-            else if (bt == 128) e = launch_tc2<TT, 128>(ctx, w, tm, Y, T);
-            else e = launch_tc2<TT, 256>(ctx, w, tm, Y, T);
+            if (bt == 64) e = launch_tc3<TT, 64>(ctx, w, tm, Y, T, ks);
+            else if (bt == 128) e = launch_tc3<TT, 128>(ctx, w, tm, Y, T, ks);
+            else e = launch_tc3<TT, 208>(ctx, w, tm, Y, T, ks);
         });
-        if (e != cudaSuccess) return hd_fail(ctx, HD_E_CUDA, "hd_qgemm (tcgen05 v2): %s", cudaGetErrorString(e));
+        if (e != cudaSuccess) return hd_fail(ctx, HD_E_CUDA, "hd_qgemm (tcgen05 v3): %s", cudaGetErrorString(e));
         return HD_OK;
     }
     int bt = 64;

@@ -4,6 +4,7 @@ contract), no bounded device wait expired, and bitwise-stable reruns."""
 import numpy as np
 import pytest
 
+import hacedle_cuda as hc
 from oracle import oracle as O
 from hacedle_cuda import synth as S
 
@@ -63,3 +64,43 @@ def test_qgemm_tc_prefill_2048(ctx):
     torch.cuda.synchronize()
     ref = Yf.cpu().numpy()
     assert np.abs(Y.cpu().numpy() - ref).max() / np.abs(ref).max() <= TOL
+
+
+@pytest.mark.parametrize("t,N,K,T", [(S.GGML_Q5_0, 256, 96, 70), (S.GGML_Q4_K, 384, 512, 257),
+                                     (S.GGML_Q6_K, 128, 768, 33), (S.GGML_Q8_0, 256, 160, 300),
+                                     (S.GGML_Q5_0, 128, 896, 64)])
+@pytest.mark.parametrize("bt", ["", "64", "128", "208"])
+def test_qgemm_tc_streamed_ragged_tiles(ctx, monkeypatch, t, N, K, T, bt):
+    """Streamed kernel (rows % 128 == 0): odd unit counts (a half-empty last K
+    step), token tails, the two-way K split of small grids, every token tile."""
+    import torch
+    if bt:
+        monkeypatch.setenv("HACEDLE_TC_BT", bt)
+    raw = S.gen_weight(t, N, K, 80 + N)
+    X = S.gen_activations(T, K, 81)
+    w = ctx.weight(t, raw, N, K)
+    Y = torch.full((T, N), float("nan"), device="cuda")
+    ctx.qgemm(w, torch.from_numpy(X).cuda(), Y, precision=1)
+    ctx.check_device_errors()
+    ref = X @ O.dequantize(t, raw, N * K).reshape(N, K).T
+    got = Y.cpu().numpy()
+    assert np.isfinite(got).all()
+    assert np.abs(got - ref).max() / np.abs(ref).max() <= TOL
+    Y2 = torch.full((T, N), float("nan"), device="cuda")
+    ctx.qgemm(w, torch.from_numpy(X).cuda(), Y2, precision=1)
+    torch.cuda.synchronize()
+    assert torch.equal(Y, Y2)
+
+
+def test_qgemm_rejects_unaligned_output(ctx):
+    """hd_qgemm wants 16-byte aligned X and Y (the TMA and vector-store paths
+    need it) and says so, without writing anything."""
+    import torch
+    t, N, K, T = S.GGML_Q5_0, 256, 256, 40
+    w = ctx.weight(t, S.gen_weight(t, N, K, 90), N, K)
+    X = torch.from_numpy(S.gen_activations(T, K, 91)).cuda()
+    big = torch.full((T * N + 1,), float("nan"), device="cuda")
+    with pytest.raises(hc.HdError) as ei:
+        ctx.qgemm(w, X, big[1:].view(T, N), precision=1)
+    assert ei.value.code == hc.HD_E_ARG
+    assert torch.isnan(big).all()
