@@ -351,6 +351,236 @@ __global__ void __launch_bounds__(GemvShape<NB, P>::MAXT) k_qgemv(GemvArgs a) {
     }
 }
 
+// ------------------------------------------------ batch 5..16 (padded 8, 16)
+// Register-blocked: the x loads, not the FMAs, bound the kernel above at
+// batch >= 8 (one float4 load per 4 FMAs).  Here lane l of warp w owns rows
+// 4l..4l+3 of a 128-row tile and one unit of K at a time, so each float4 of x
+// (the same address across the warp: one broadcast) feeds 16 FMAs.  Weights
+// are decoded chunk by chunk (4 values of 4 rows) into their exact fp32
+// values.  The (tile, unit) pairs are dealt out in tile-major order, 8 per
+// CTA (one per warp), so every SM gets the same work; warps of one tile meet
+// in shared memory, and a tile spread over several CTAs meets in the
+// workspace, where the last CTA to arrive adds the segments in CTA order --
+// fixed orders throughout, so results are bitwise reproducible.
+
+// Scales of one unit of one row: values 0-15 use s0, 16-31 use s1; Q4_K
+// subtracts mn.  Decoded once per unit, applied per value.
+struct URowScale {
+    float s0, s1, mn;
+};
+template <int TYPE>
+__device__ __forceinline__ URowScale unit_scale(const URegs<TYPE> &g, int u) {
+    URowScale r;
+    r.mn = 0.f;
+    if constexpr (TYPE == HD_TYPE_Q8_0 || TYPE == HD_TYPE_Q5_0) {
+        r.s0 = r.s1 = h2f((uint16_t)g.d);
+    } else if constexpr (TYPE == HD_TYPE_Q4_K) {
+        int sc, m;
+        q4k_sm_regs(u & 7, g.m.y, g.m.z, g.m.w, sc, m);
+        r.s0 = r.s1 = __fmul_rn(h2f((uint16_t)(g.m.x & 0xFFFF)), (float)sc);
+        r.mn = __fmul_rn(h2f((uint16_t)(g.m.x >> 16)), (float)m);
+    } else {
+        const int s0 = 2 * (u & 7);
+        const uint32_t scw = w4(g.sc, s0 >> 2);
+        const float d = h2f((uint16_t)g.d);
+        r.s0 = __fmul_rn(d, (float)(int8_t)((scw >> (8 * (s0 & 3))) & 255));
+        r.s1 = __fmul_rn(d, (float)(int8_t)((scw >> (8 * ((s0 & 3) + 1))) & 255));
+    }
+    return r;
+}
+
+// Values 4wd..4wd+3 of a unit, exact (the dequantized weights).
+template <int TYPE>
+__device__ __forceinline__ void chunk_vals(const URegs<TYPE> &g, const URowScale &sc, int wd, float (&v)[4]) {
+    const float s = wd < 4 ? sc.s0 : sc.s1;
+    if constexpr (TYPE == HD_TYPE_Q8_0) {
+        const uint32_t x = (wd < 4 ? w4(g.a, wd) : w4(g.b, wd - 4)) ^ 0x80808080u;
+#pragma unroll
+        for (int c = 0; c < 4; c++) v[c] = __fmul_rn(mag(x, c) - 8388736.0f, s);
+    } else if constexpr (TYPE == HD_TYPE_Q5_0) {
+        const uint32_t q = w4(g.a, wd & 3);
+        const uint32_t b = wd < 4 ? ((q & 0x0F0F0F0Fu) | ((g.qh >> wd) & 0x10101010u))
+                                  : (((q >> 4) & 0x0F0F0F0Fu) | ((g.qh << (8 - wd)) & 0x10101010u));
+#pragma unroll
+        for (int c = 0; c < 4; c++) v[c] = __fmul_rn(mag(b, c) - 8388624.0f, s);
+    } else if constexpr (TYPE == HD_TYPE_Q4_K) {
+        const uint32_t q = w4(g.a, wd & 3);
+        const uint32_t b = wd < 4 ? (q & 0x0F0F0F0Fu) : ((q >> 4) & 0x0F0F0F0Fu);
+#pragma unroll
+        for (int c = 0; c < 4; c++) v[c] = __fsub_rn(__fmul_rn(mag(b, c) - 8388608.0f, s), sc.mn);
+    } else {
+        const int i = wd & 3;
+        const uint32_t hsel = wd < 4 ? g.h.x : g.h.y;
+        const uint32_t b = ((w4(g.a, i) >> (wd < 4 ? 0 : 4)) & 0x0F0F0F0Fu) | (shl_or_shr(hsel, 4 - 2 * i) & 0x30303030u);
+#pragma unroll
+        for (int c = 0; c < 4; c++) v[c] = __fmul_rn(mag(b, c) - 8388640.0f, s);
+    }
+}
+
+template <int TYPE, int NB, int PT>
+__global__ void __launch_bounds__(32 * NB, 1)
+    k_qgemv_rb(GemvArgs a, int ntiles, int S, float *ws, int *tickets) {
+    constexpr bool per_tile = PT != 0;
+    constexpr int NT = 32 * NB;  // 8 unit slots x NB / 8 batch groups of 8
+    // x of each slot's unit [8][NB][32] during the main loop, then the
+    // per-slot partial sums [8][NB][128 rows]
+    extern __shared__ float sm[];
+    __shared__ int last;
+    // warp = (batch group bg, unit slot): rows of the tile x unit x 8 batch rows
+    const int warp = (threadIdx.x >> 5) & 7, bg = threadIdx.x >> 8, lane = threadIdx.x & 31;
+    const int units = a.w0.units;
+    const int nwu = ntiles * units, g0 = blockIdx.x * 8;
+    // Flattened: warp w takes pair g0 + w (one unit).  Per tile (tall
+    // matrices, at least one tile per SM): CTA = tile, warp w the units
+    // w, w + 8, ...
+    const int gw = g0 + warp;
+    const bool wok = per_tile || gw < nwu;
+    const int tile = per_tile ? (int)blockIdx.x : wok ? gw / units : 0;
+    const int ufirst = per_tile ? warp : wok ? gw - tile * units : units;
+    const int ustep = per_tile ? 8 : units;
+    const int64_t row0 = (int64_t)tile * 128 + 4 * lane;
+
+    URegs<TYPE> cur[4];
+#pragma unroll
+    for (int rr = 0; rr < 4; rr++) {
+        if (ufirst < units && row0 + rr < a.N) load_unit<TYPE>(a.w0, row0 + rr, ufirst, cur[rr]);
+        else zero_unit<TYPE>(cur[rr]);
+    }
+    pdl_trigger();
+    pdl_wait();
+
+    float acc[4][8];
+#pragma unroll
+    for (int rr = 0; rr < 4; rr++)
+#pragma unroll
+        for (int b = 0; b < 8; b++) acc[rr][b] = 0.f;
+    const int bbase = 8 * bg, nbw = a.B - bbase < 8 ? a.B - bbase : 8;  // this warp's batch rows
+    // flattened: one pass (straight-line code); per tile: the warp's units
+    for (int u = ufirst; u < units; u = per_tile ? u + ustep : units) {
+        if (per_tile && u != ufirst) {
+#pragma unroll
+            for (int rr = 0; rr < 4; rr++) {
+                if (row0 + rr < a.N) load_unit<TYPE>(a.w0, row0 + rr, u, cur[rr]);
+                else zero_unit<TYPE>(cur[rr]);
+            }
+        }
+        float4 *xs = (float4 *)sm + (warp * NB + bbase) * 8;
+        __syncwarp();
+        for (int i = lane; i < nbw * 8; i += 32)
+            xs[i] = __ldg((const float4 *)(a.x + (int64_t)(bbase + (i >> 3)) * a.K + (int64_t)u * 32) + (i & 7));
+        __syncwarp();
+        URowScale scl[4];
+#pragma unroll
+        for (int rr = 0; rr < 4; rr++) scl[rr] = unit_scale<TYPE>(cur[rr], u);
+#pragma unroll
+        for (int wd = 0; wd < 8; wd++) {
+            float v[4][4];
+#pragma unroll
+            for (int rr = 0; rr < 4; rr++) chunk_vals<TYPE>(cur[rr], scl[rr], wd, v[rr]);
+            // 4 batch rows at a time, component-major: 16 independent FMAs
+            // between two that share an accumulator
+#pragma unroll
+            for (int b0 = 0; b0 < 8; b0 += 4) {
+                if (b0 < nbw) {
+                    float xv[4][4];
+#pragma unroll
+                    for (int bb = 0; bb < 4; bb++) {
+                        const float4 t4 = b0 + bb < nbw ? xs[(b0 + bb) * 8 + wd] : make_float4(0.f, 0.f, 0.f, 0.f);
+                        xv[bb][0] = t4.x;
+                        xv[bb][1] = t4.y;
+                        xv[bb][2] = t4.z;
+                        xv[bb][3] = t4.w;
+                    }
+#pragma unroll
+                    for (int k = 0; k < 4; k++)
+#pragma unroll
+                        for (int rr = 0; rr < 4; rr++)
+#pragma unroll
+                            for (int bb = 0; bb < 4; bb++)
+                                acc[rr][b0 + bb] = fmaf(v[rr][k], xv[bb][k], acc[rr][b0 + bb]);
+                }
+            }
+        }
+    }
+    __syncthreads();  // x no longer needed: the buffer takes the partial sums
+#pragma unroll
+    for (int rr = 0; rr < 4; rr++)
+#pragma unroll
+        for (int b = 0; b < 8; b++) sm[(warp * NB + bbase + b) * 128 + 4 * lane + rr] = acc[rr][b];
+    __syncthreads();
+
+    // One segment per tile this CTA touches: its warps w0..w1-1 add up in
+    // order; a tile spread over several CTAs meets in the workspace, where the
+    // last CTA to arrive adds the segments in CTA order.  Workspace slot of a
+    // CTA's segment: its CTA index x S + the segment's rank in the CTA (only
+    // the first CTA of a tile can hold it as a later segment).
+    const int g1 = g0 + 8 < nwu ? g0 + 8 : nwu;
+    const int t_first = per_tile ? tile : g0 / units, t_last = per_tile ? tile : (g1 - 1) / units;
+    for (int t = t_first; t <= t_last; t++) {
+        const int w0 = per_tile ? 0 : (t * units > g0 ? t * units : g0) - g0;
+        const int w1 = per_tile ? 8 : ((t + 1) * units < g1 ? (t + 1) * units : g1) - g0;
+        const int cf = t * units / 8, cl = ((t + 1) * units - 1) / 8;
+        const int nseg = per_tile ? 1 : cl - cf + 1, slot = t - t_first;
+        for (int o = threadIdx.x; o < 128 * NB; o += NT) {
+            const int b = o >> 7, rl = o & 127;
+            const int64_t row = (int64_t)t * 128 + rl;
+            if (b >= a.B || row >= a.N) continue;
+            float s = 0.f;
+            for (int w = w0; w < w1; w++) s += sm[(w * NB + b) * 128 + rl];
+            if (nseg == 1) {
+                if (a.bias) s = s + a.bias[row];
+                if (a.residual) s = a.residual[(int64_t)b * a.ldy + row] + s;
+                a.y[(int64_t)b * a.ldy + row] = s;
+            } else {
+                __stcg(ws + (((int64_t)blockIdx.x * S + slot) * NB + b) * 128 + rl, s);
+            }
+        }
+        if (nseg == 1) continue;
+        __threadfence();
+        __syncthreads();
+        if (threadIdx.x == 0) last = (atomicAdd(tickets + t, 1) == nseg - 1);
+        __syncthreads();
+        if (last) {
+            __threadfence();
+            const int sf = t - cf * 8 / units;  // slot of the tile in its first CTA
+            // 4 rows per thread-step (16-byte loads), the partials of a step
+            // requested together, then added in CTA order
+            for (int o4 = threadIdx.x; o4 < 32 * NB; o4 += NT) {
+                const int b = o4 >> 5, r4 = (o4 & 31) * 4;
+                if (b >= a.B) continue;
+                const float4 *p = (const float4 *)(ws + (((int64_t)cf * S + sf) * NB + b) * 128 + r4);
+                float4 sum = __ldcg(p);
+                for (int c0 = cf + 1; c0 <= cl; c0 += 8) {
+                    float4 part[8];
+#pragma unroll
+                    for (int j = 0; j < 8; j++)
+                        if (c0 + j <= cl) part[j] = __ldcg((const float4 *)(ws + (((int64_t)(c0 + j) * S) * NB + b) * 128 + r4));
+#pragma unroll
+                    for (int j = 0; j < 8; j++)
+                        if (c0 + j <= cl) {
+                            sum.x += part[j].x;
+                            sum.y += part[j].y;
+                            sum.z += part[j].z;
+                            sum.w += part[j].w;
+                        }
+                }
+                const float sv[4] = {sum.x, sum.y, sum.z, sum.w};
+#pragma unroll
+                for (int k = 0; k < 4; k++) {
+                    const int64_t row = (int64_t)t * 128 + r4 + k;
+                    if (row >= a.N) break;
+                    float s = sv[k];
+                    if (a.bias) s = s + a.bias[row];
+                    if (a.residual) s = a.residual[(int64_t)b * a.ldy + row] + s;
+                    a.y[(int64_t)b * a.ldy + row] = s;
+                }
+            }
+            if (threadIdx.x == 0) tickets[t] = 0;
+        }
+        __syncthreads();
+    }
+}
+
 struct Plan {
     int nb, RC, G, nt, tiles;
     size_t smem;
@@ -437,6 +667,39 @@ cudaError_t launch_type(hd_ctx *ctx, const Plan &p, const GemvArgs &a) {
 int hd_ensure_hbuf(hd_ctx *ctx, float **buf, size_t *have, size_t need);
 namespace {
 
+template <int TYPE, int NB, int PT>
+cudaError_t launch_rb(hd_ctx *ctx, const GemvArgs &a, int ntiles, int ctas, int S) {
+    const size_t smem = (size_t)8 * NB * 128 * sizeof(float);
+    cudaError_t e = cudaFuncSetAttribute(k_qgemv_rb<TYPE, NB, PT>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                         (int)smem);
+    if (e != cudaSuccess) return e;
+    return hd_launch(ctx, k_qgemv_rb<TYPE, NB, PT>, dim3(ctas), dim3(32 * NB), smem, a, ntiles, S, ctx->ws,
+                     ctx->tickets);
+}
+
+// Batch 5..16: the (128-row tile, unit) pairs in tile-major order, 8 per CTA
+// (one per warp), so that the CTAs fill the SMs evenly; with at least one
+// tile per SM, one CTA per tile instead (no partial sums to combine).
+int run_gemv_rb(hd_ctx *ctx, const GemvArgs &a, int type, const char *name) {
+    const int nb = pad_batch(a.B);
+    const int ntiles = (a.N + 127) / 128, units = a.w0.units;
+    const int per_tile = ntiles >= ctx->sm_count ? 1 : 0;
+    const int64_t nwu = (int64_t)ntiles * units;
+    const int ctas = per_tile ? ntiles : (int)((nwu + 7) / 8);
+    const int S = (8 + units - 1) / units + 1;  // tiles one CTA can touch
+    if (!per_tile) {
+        int rc = hd_ensure_workspace(ctx, (size_t)ctas * S * nb * 128 * sizeof(float), (size_t)ntiles);
+        if (rc) return rc;
+    }
+    cudaError_t e = cudaSuccess;
+    HD_TYPE_SWITCH(type, T, {
+        if (per_tile) e = nb == 8 ? launch_rb<T, 8, 1>(ctx, a, ntiles, ctas, S) : launch_rb<T, 16, 1>(ctx, a, ntiles, ctas, S);
+        else e = nb == 8 ? launch_rb<T, 8, 0>(ctx, a, ntiles, ctas, S) : launch_rb<T, 16, 0>(ctx, a, ntiles, ctas, S);
+    });
+    if (e != cudaSuccess) return hd_fail(ctx, HD_E_CUDA, "%s: %s", name, cudaGetErrorString(e));
+    return HD_OK;
+}
+
 int run_gemv(hd_ctx *ctx, const hd_weight *w, const hd_weight *w_up, const float *x, float *y, int B,
              const float *bias, const float *residual, const char *name) {
     if (!ctx || !w || !x || !y) return hd_fail(ctx, HD_E_ARG, "%s: null argument", name);
@@ -455,7 +718,6 @@ int run_gemv(hd_ctx *ctx, const hd_weight *w, const hd_weight *w_up, const float
         if (!rc) rc = hd_swiglu(ctx, ctx->scratch, ctx->scratch + one, y, (int64_t)one);
         return rc;
     }
-    Plan p = plan_gemv((int)w->rows, w->units, B, w_up != nullptr, ctx->sm_count);
     GemvArgs a;
     a.w0 = wview(w);
     a.w1 = w_up ? wview(w_up) : a.w0;
@@ -467,9 +729,11 @@ int run_gemv(hd_ctx *ctx, const hd_weight *w, const hd_weight *w_up, const float
     a.N = (int)w->rows;
     a.ldy = (int)w->rows;
     a.K = (int)w->cols;
+    a.pair = w_up ? 1 : 0;
+    if (!w_up && pad_batch(B) >= 8 && getenv("HACEDLE_GEMV_RB") == nullptr) return run_gemv_rb(ctx, a, w->type, name);
+    Plan p = plan_gemv((int)w->rows, w->units, B, w_up != nullptr, ctx->sm_count);
     a.RC = p.RC;
     a.G = p.G;
-    a.pair = w_up ? 1 : 0;
     cudaError_t e = cudaSuccess;
     HD_TYPE_SWITCH(w->type, T, e = launch_type<T>(ctx, p, a));
     if (e != cudaSuccess) return hd_fail(ctx, HD_E_CUDA, "%s: %s", name, cudaGetErrorString(e));

@@ -24,7 +24,7 @@ def _oracle_tokens(model, prompts, n_gen):
     return np.stack([O.decoder_generate(model["cfg"], layers, on, emb, p, n_gen, threads=8) for p in prompts])
 
 
-@pytest.mark.parametrize("seqs,n_prompt,n_gen", [(1, 12, 10), (3, 7, 9), (20, 5, 4)])
+@pytest.mark.parametrize("seqs,n_prompt,n_gen", [(1, 12, 10), (3, 7, 9), (8, 6, 5), (20, 5, 4)])
 def test_small_decoder_matches_oracle(ctx, seqs, n_prompt, n_gen):
     model = S.gen_decoder(SMALL, seed=21)
     prompts = np.stack([S.gen_prompt(n_prompt, SMALL["vocab"], seed=30 + s) for s in range(seqs)])

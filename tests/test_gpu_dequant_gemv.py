@@ -182,3 +182,27 @@ def test_gemv_lm_head_q8_0(ctx):
     # The tied LM head shape: 151936 x 896 Q8_0 (144.6 MB), batch 1.
     y, ref = _gemv_case(ctx, S.GGML_Q8_0, 151936, 896, 1, 314)
     assert _rel_err(y, ref) <= REL_TOL
+
+
+@pytest.mark.parametrize("t,N,K,B,bias,residual", [(S.GGML_Q5_0, 1152, 896, 8, True, False),
+                                                    (S.GGML_Q4_K, 896, 4864, 12, False, True),
+                                                    (S.GGML_Q6_K, 4864, 4864, 16, True, True),
+                                                    (S.GGML_Q8_0, 384, 2048, 6, False, False),
+                                                    (S.GGML_Q5_0, 19000, 512, 16, False, True),
+                                                    (S.GGML_Q4_K, 18944, 256, 9, True, False)])
+def test_gemv_batched_register_blocked(ctx, t, N, K, B, bias, residual):
+    """Batch 5..16 (the register-blocked kernel): epilogues, the K split over
+    CTAs, the one-CTA-per-tile mode of tall matrices (>= 148 tiles of 128
+    rows), and bitwise-stable reruns."""
+    torch = _torch()
+    y, ref = _gemv_case(ctx, t, N, K, B, 200 + B, bias=bias, residual=residual)
+    assert _rel_err(y, ref) <= REL_TOL
+    raw = S.gen_weight(t, N, K, 300 + B)
+    w = ctx.weight(t, raw, N, K)
+    x = torch.from_numpy(S.gen_activations(B, K, 301)).cuda()
+    y1 = torch.empty(B, N, device="cuda")
+    y2 = torch.empty(B, N, device="cuda")
+    ctx.qgemv(w, x, y1)
+    ctx.qgemv(w, x, y2)
+    torch.cuda.synchronize()
+    assert torch.equal(y1, y2)
