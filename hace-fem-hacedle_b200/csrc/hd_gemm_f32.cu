@@ -1,9 +1,12 @@
 // hd_gemm_f32.cu -- fp32 CUDA-core GEMMs: the exact-weight prefill Q-GEMM
 // (HD_PREC_FP32: each weight is dequantized bit-exactly, then multiplied in
 // fp32) and the dense f32 matmul of the graph executor.
+#include <cstdlib>
+
 #include "hd_internal.cuh"
 
 int hd_qgemm_tc(hd_ctx *ctx, const hd_weight *w, const float *X, float *Y, int T);
+int hd_qgemm_rows_f32(hd_ctx *ctx, const hd_weight *w, const float *X, float *Y, int T);
 int hd_ensure_hbuf(hd_ctx *ctx, float **buf, size_t *have, size_t need);
 
 namespace {
@@ -141,7 +144,14 @@ extern "C" int hd_qgemm(hd_ctx *ctx, const hd_weight *w, const float *X, float *
     HD_REQUIRE(ctx, ((uintptr_t)X & 15) == 0 && ((uintptr_t)Y & 15) == 0, HD_E_ARG,
                "hd_qgemm: X and Y must be 16-byte aligned");
     if (T == 0) return HD_OK;
-    if (precision == HD_PREC_FP32) return hd_qgemm_f32(ctx, w, X, Y, T);
+    if (precision == HD_PREC_FP32) {
+        // up to 1024 rows (HACEDLE_ROWS_GEMV_MAX): groups of 16 rows on the
+        // batch Q-GEMV kernel, faster there; beyond, the 128 x 64 tiled kernel
+        const char *lim = getenv("HACEDLE_ROWS_GEMV_MAX");
+        const int maxrows = lim ? atoi(lim) : 1024;
+        if (T <= maxrows) return hd_qgemm_rows_f32(ctx, w, X, Y, T);
+        return hd_qgemm_f32(ctx, w, X, Y, T);
+    }
     if (precision == HD_PREC_BF16_TC) return hd_qgemm_tc(ctx, w, X, Y, T);
     return hd_fail(ctx, HD_E_ARG, "hd_qgemm: unknown precision %d", precision);
 }

@@ -428,6 +428,13 @@ __global__ void __launch_bounds__(32 * NB, 1)
     __shared__ int last;
     // warp = (batch group bg, unit slot): rows of the tile x unit x 8 batch rows
     const int warp = (threadIdx.x >> 5) & 7, bg = threadIdx.x >> 8, lane = threadIdx.x & 31;
+    // blockIdx.y: group of 16 rows of x (more than 16 rows: a batch of GEMVs)
+    const int grp = blockIdx.y, B = a.B - 16 * grp < 16 ? a.B - 16 * grp : 16;
+    const float *X = a.x + (int64_t)grp * 16 * a.K;
+    float *Yo = a.y + (int64_t)grp * 16 * a.ldy;
+    const float *Rs = a.residual ? a.residual + (int64_t)grp * 16 * a.ldy : nullptr;
+    int *tk = tickets + grp * ntiles;
+    const int64_t cta = (int64_t)grp * gridDim.x + blockIdx.x;
     const int units = a.w0.units;
     const int nwu = ntiles * units, g0 = blockIdx.x * 8;
     // Flattened: warp w takes pair g0 + w (one unit).  Per tile (tall
@@ -454,7 +461,7 @@ __global__ void __launch_bounds__(32 * NB, 1)
     for (int rr = 0; rr < 4; rr++)
 #pragma unroll
         for (int b = 0; b < 8; b++) acc[rr][b] = 0.f;
-    const int bbase = 8 * bg, nbw = a.B - bbase < 8 ? a.B - bbase : 8;  // this warp's batch rows
+    const int bbase = 8 * bg, nbw = B - bbase < 8 ? B - bbase : 8;  // this warp's batch rows
     // flattened: one pass (straight-line code); per tile: the warp's units
     for (int u = ufirst; u < units; u = per_tile ? u + ustep : units) {
         if (per_tile && u != ufirst) {
@@ -467,7 +474,7 @@ __global__ void __launch_bounds__(32 * NB, 1)
         float4 *xs = (float4 *)sm + (warp * NB + bbase) * 8;
         __syncwarp();
         for (int i = lane; i < nbw * 8; i += 32)
-            xs[i] = __ldg((const float4 *)(a.x + (int64_t)(bbase + (i >> 3)) * a.K + (int64_t)u * 32) + (i & 7));
+            xs[i] = __ldg((const float4 *)(X + (int64_t)(bbase + (i >> 3)) * a.K + (int64_t)u * 32) + (i & 7));
         __syncwarp();
         URowScale scl[4];
 #pragma unroll
@@ -524,21 +531,21 @@ __global__ void __launch_bounds__(32 * NB, 1)
         for (int o = threadIdx.x; o < 128 * NB; o += NT) {
             const int b = o >> 7, rl = o & 127;
             const int64_t row = (int64_t)t * 128 + rl;
-            if (b >= a.B || row >= a.N) continue;
+            if (b >= B || row >= a.N) continue;
             float s = 0.f;
             for (int w = w0; w < w1; w++) s += sm[(w * NB + b) * 128 + rl];
             if (nseg == 1) {
                 if (a.bias) s = s + a.bias[row];
-                if (a.residual) s = a.residual[(int64_t)b * a.ldy + row] + s;
-                a.y[(int64_t)b * a.ldy + row] = s;
+                if (Rs) s = Rs[(int64_t)b * a.ldy + row] + s;
+                Yo[(int64_t)b * a.ldy + row] = s;
             } else {
-                __stcg(ws + (((int64_t)blockIdx.x * S + slot) * NB + b) * 128 + rl, s);
+                __stcg(ws + ((cta * S + slot) * NB + b) * 128 + rl, s);
             }
         }
         if (nseg == 1) continue;
         __threadfence();
         __syncthreads();
-        if (threadIdx.x == 0) last = (atomicAdd(tickets + t, 1) == nseg - 1);
+        if (threadIdx.x == 0) last = (atomicAdd(tk + t, 1) == nseg - 1);
         __syncthreads();
         if (last) {
             __threadfence();
@@ -547,14 +554,15 @@ __global__ void __launch_bounds__(32 * NB, 1)
             // requested together, then added in CTA order
             for (int o4 = threadIdx.x; o4 < 32 * NB; o4 += NT) {
                 const int b = o4 >> 5, r4 = (o4 & 31) * 4;
-                if (b >= a.B) continue;
-                const float4 *p = (const float4 *)(ws + (((int64_t)cf * S + sf) * NB + b) * 128 + r4);
+                if (b >= B) continue;
+                const int64_t cbase = (int64_t)grp * gridDim.x;
+                const float4 *p = (const float4 *)(ws + (((cbase + cf) * S + sf) * NB + b) * 128 + r4);
                 float4 sum = __ldcg(p);
                 for (int c0 = cf + 1; c0 <= cl; c0 += 8) {
                     float4 part[8];
 #pragma unroll
                     for (int j = 0; j < 8; j++)
-                        if (c0 + j <= cl) part[j] = __ldcg((const float4 *)(ws + (((int64_t)(c0 + j) * S) * NB + b) * 128 + r4));
+                        if (c0 + j <= cl) part[j] = __ldcg((const float4 *)(ws + (((cbase + c0 + j) * S) * NB + b) * 128 + r4));
 #pragma unroll
                     for (int j = 0; j < 8; j++)
                         if (c0 + j <= cl) {
@@ -571,11 +579,11 @@ __global__ void __launch_bounds__(32 * NB, 1)
                     if (row >= a.N) break;
                     float s = sv[k];
                     if (a.bias) s = s + a.bias[row];
-                    if (a.residual) s = a.residual[(int64_t)b * a.ldy + row] + s;
-                    a.y[(int64_t)b * a.ldy + row] = s;
+                    if (Rs) s = Rs[(int64_t)b * a.ldy + row] + s;
+                    Yo[(int64_t)b * a.ldy + row] = s;
                 }
             }
-            if (threadIdx.x == 0) tickets[t] = 0;
+            if (threadIdx.x == 0) tk[t] = 0;
         }
         __syncthreads();
     }
@@ -668,12 +676,12 @@ int hd_ensure_hbuf(hd_ctx *ctx, float **buf, size_t *have, size_t need);
 namespace {
 
 template <int TYPE, int NB, int PT>
-cudaError_t launch_rb(hd_ctx *ctx, const GemvArgs &a, int ntiles, int ctas, int S) {
+cudaError_t launch_rb(hd_ctx *ctx, const GemvArgs &a, int ntiles, int ctas, int S, int groups) {
     const size_t smem = (size_t)8 * NB * 128 * sizeof(float);
     cudaError_t e = cudaFuncSetAttribute(k_qgemv_rb<TYPE, NB, PT>, cudaFuncAttributeMaxDynamicSharedMemorySize,
                                          (int)smem);
     if (e != cudaSuccess) return e;
-    return hd_launch(ctx, k_qgemv_rb<TYPE, NB, PT>, dim3(ctas), dim3(32 * NB), smem, a, ntiles, S, ctx->ws,
+    return hd_launch(ctx, k_qgemv_rb<TYPE, NB, PT>, dim3(ctas, groups), dim3(32 * NB), smem, a, ntiles, S, ctx->ws,
                      ctx->tickets);
 }
 
@@ -681,20 +689,25 @@ cudaError_t launch_rb(hd_ctx *ctx, const GemvArgs &a, int ntiles, int ctas, int 
 // (one per warp), so that the CTAs fill the SMs evenly; with at least one
 // tile per SM, one CTA per tile instead (no partial sums to combine).
 int run_gemv_rb(hd_ctx *ctx, const GemvArgs &a, int type, const char *name) {
-    const int nb = pad_batch(a.B);
+    const int nb = a.B <= 8 ? 8 : 16, groups = (a.B + 15) / 16;
     const int ntiles = (a.N + 127) / 128, units = a.w0.units;
     const int per_tile = ntiles >= ctx->sm_count ? 1 : 0;
     const int64_t nwu = (int64_t)ntiles * units;
     const int ctas = per_tile ? ntiles : (int)((nwu + 7) / 8);
     const int S = (8 + units - 1) / units + 1;  // tiles one CTA can touch
     if (!per_tile) {
-        int rc = hd_ensure_workspace(ctx, (size_t)ctas * S * nb * 128 * sizeof(float), (size_t)ntiles);
+        int rc = hd_ensure_workspace(ctx, (size_t)ctas * groups * S * nb * 128 * sizeof(float),
+                                     (size_t)ntiles * groups);
         if (rc) return rc;
     }
     cudaError_t e = cudaSuccess;
     HD_TYPE_SWITCH(type, T, {
-        if (per_tile) e = nb == 8 ? launch_rb<T, 8, 1>(ctx, a, ntiles, ctas, S) : launch_rb<T, 16, 1>(ctx, a, ntiles, ctas, S);
-        else e = nb == 8 ? launch_rb<T, 8, 0>(ctx, a, ntiles, ctas, S) : launch_rb<T, 16, 0>(ctx, a, ntiles, ctas, S);
+        if (per_tile)
+            e = nb == 8 ? launch_rb<T, 8, 1>(ctx, a, ntiles, ctas, S, groups)
+                        : launch_rb<T, 16, 1>(ctx, a, ntiles, ctas, S, groups);
+        else
+            e = nb == 8 ? launch_rb<T, 8, 0>(ctx, a, ntiles, ctas, S, groups)
+                        : launch_rb<T, 16, 0>(ctx, a, ntiles, ctas, S, groups);
     });
     if (e != cudaSuccess) return hd_fail(ctx, HD_E_CUDA, "%s: %s", name, cudaGetErrorString(e));
     return HD_OK;
@@ -777,4 +790,22 @@ extern "C" int hd_qgemv_host(hd_ctx *ctx, const hd_weight *w, const float *x_hos
     HD_CUDA_TRY(ctx, cudaMemcpyAsync(y_host, ctx->hbuf_y, yb, cudaMemcpyDeviceToHost, ctx->stream));
     HD_CUDA_TRY(ctx, cudaStreamSynchronize(ctx->stream));
     return HD_OK;
+}
+
+// fp32 Q-GEMM over T rows of x as groups of 16 rows of the batch kernel
+// (exact dequantized weights, fp32 accumulation; the decoder's fp32 steps).
+int hd_qgemm_rows_f32(hd_ctx *ctx, const hd_weight *w, const float *X, float *Y, int T) {
+    GemvArgs a;
+    a.w0 = a.w1 = wview(w);
+    a.x = X;
+    a.y = Y;
+    a.bias = nullptr;
+    a.residual = nullptr;
+    a.B = T;
+    a.N = (int)w->rows;
+    a.ldy = (int)w->rows;
+    a.K = (int)w->cols;
+    a.RC = a.G = 0;
+    a.pair = 0;
+    return run_gemv_rb(ctx, a, w->type, "hd_qgemm");
 }

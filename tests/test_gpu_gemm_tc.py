@@ -104,3 +104,25 @@ def test_qgemm_rejects_unaligned_output(ctx):
         ctx.qgemm(w, X, big[1:].view(T, N), precision=1)
     assert ei.value.code == hc.HD_E_ARG
     assert torch.isnan(big).all()
+
+
+@pytest.mark.parametrize("t,N,K,T", [(S.GGML_Q5_0, 4864, 896, 256), (S.GGML_Q4_K, 896, 4864, 37),
+                                     (S.GGML_Q6_K, 300, 768, 100), (S.GGML_Q8_0, 151936 // 8, 896, 20)])
+def test_qgemm_fp32_row_groups(ctx, t, N, K, T):
+    """fp32 Q-GEMM of up to 1024 rows runs as 16-row groups of the batch
+    Q-GEMV kernel: the oracle's product within 1e-5, bitwise-stable reruns."""
+    import torch
+    raw = S.gen_weight(t, N, K, 110 + T)
+    X = S.gen_activations(T, K, 111)
+    w = ctx.weight(t, raw, N, K)
+    Y = torch.empty(T, N, device="cuda")
+    Xd = torch.from_numpy(X).cuda()
+    ctx.qgemm(w, Xd, Y, precision=0)
+    ctx.check_device_errors()
+    ref = O.qgemv(t, raw, N, K, X, threads=8)
+    got = Y.cpu().numpy()
+    assert np.abs(got - ref).max() / np.abs(ref).max() <= 1e-5
+    Y2 = torch.empty(T, N, device="cuda")
+    ctx.qgemm(w, Xd, Y2, precision=0)
+    torch.cuda.synchronize()
+    assert torch.equal(Y, Y2)
