@@ -5,7 +5,7 @@
 
 #include "hd_internal.cuh"
 
-int hd_qgemm_tc(hd_ctx *ctx, const hd_weight *w, const float *X, float *Y, int T);
+int hd_qgemm_tc(hd_ctx *ctx, const hd_weight *w, const float *X, float *Y, int T, int exact);
 int hd_qgemm_rows_f32(hd_ctx *ctx, const hd_weight *w, const float *X, float *Y, int T);
 int hd_ensure_hbuf(hd_ctx *ctx, float **buf, size_t *have, size_t need);
 
@@ -145,14 +145,20 @@ extern "C" int hd_qgemm(hd_ctx *ctx, const hd_weight *w, const float *X, float *
                "hd_qgemm: X and Y must be 16-byte aligned");
     if (T == 0) return HD_OK;
     if (precision == HD_PREC_FP32) {
-        // up to 1024 rows (HACEDLE_ROWS_GEMV_MAX): groups of 16 rows on the
-        // batch Q-GEMV kernel, faster there; beyond, the 128 x 64 tiled kernel
+        // rows % 128 == 0 and more than 16 rows: the exact-product
+        // tensor-core mode (exact weights and x as fp16 hi + lo, 3 MMAs per
+        // product, fp32 accumulation).  Otherwise: up to 1024 rows, groups of
+        // 16 rows on the batch Q-GEMV kernel; beyond, the 128 x 64 tiled
+        // kernel.  HACEDLE_FP32_CUDA_CORES=1 keeps fp32 products on the CUDA
+        // cores.
+        if (w->rows % 128 == 0 && T > 16 && getenv("HACEDLE_FP32_CUDA_CORES") == nullptr)
+            return hd_qgemm_tc(ctx, w, X, Y, T, 1);
         const char *lim = getenv("HACEDLE_ROWS_GEMV_MAX");
         const int maxrows = lim ? atoi(lim) : 1024;
         if (T <= maxrows) return hd_qgemm_rows_f32(ctx, w, X, Y, T);
         return hd_qgemm_f32(ctx, w, X, Y, T);
     }
-    if (precision == HD_PREC_BF16_TC) return hd_qgemm_tc(ctx, w, X, Y, T);
+    if (precision == HD_PREC_BF16_TC) return hd_qgemm_tc(ctx, w, X, Y, T, 0);
     return hd_fail(ctx, HD_E_ARG, "hd_qgemm: unknown precision %d", precision);
 }
 

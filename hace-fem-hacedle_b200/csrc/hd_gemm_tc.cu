@@ -105,6 +105,11 @@ __host__ __device__ constexpr uint32_t idesc_bf16(int n) {
     return (1u << 4) | (1u << 7) | (1u << 10) | ((uint32_t)(n >> 3) << 17) | ((uint32_t)(128 >> 4) << 24);
 }
 
+// Same with fp16 A and B (formats 0): the exact-product mode.
+__host__ __device__ constexpr uint32_t idesc_f16(int n) {
+    return (1u << 4) | ((uint32_t)(n >> 3) << 17) | ((uint32_t)(128 >> 4) << 24);
+}
+
 __device__ __forceinline__ uint32_t pack_bf16(float a, float b) {
     __nv_bfloat162 h = __floats2bfloat162_rn(a, b);
     return *reinterpret_cast<uint32_t *>(&h);
@@ -551,24 +556,95 @@ __device__ __forceinline__ void tmem_st8(uint32_t taddr, const uint32_t (&o)[8])
     asm volatile("tcgen05.wait::st.sync.aligned;" ::: "memory");
 }
 
+// Exact-product mode: values 16*part .. 16*part+15 of unit u as exact fp32
+// (the fp32 path's dequantization), times 2^shift (exact), split into fp16
+// halves: v = hi + lo + r with |r| <= 2^-22 |v| (zeros when !valid).
+__device__ __forceinline__ uint32_t pack_h2(float a, float b) {
+    __half2 h = __floats2half2_rn(a, b);
+    return *reinterpret_cast<uint32_t *>(&h);
+}
+template <int TYPE>
+__device__ __forceinline__ void dq_words_exact(int u, int part, bool valid, const DqRaw &g, float scale,
+                                               uint32_t (&hi)[8], uint32_t (&lo)[8]) {
+    if (!valid) {
+#pragma unroll
+        for (int j = 0; j < 8; j++) hi[j] = lo[j] = 0u;
+        return;
+    }
+    float v[16];
+    const uint32_t wd[4] = {g.q0.x, g.q0.y, g.q0.z, g.q0.w};
+    if constexpr (TYPE == HD_TYPE_Q8_0) {
+        const float d = h2f((uint16_t)g.d);
+#pragma unroll
+        for (int i = 0; i < 4; i++) {
+            const uint32_t x = wd[i] ^ 0x80808080u;
+#pragma unroll
+            for (int c = 0; c < 4; c++) v[4 * i + c] = __fmul_rn(mag(x, c) - 8388736.0f, d);
+        }
+    } else if constexpr (TYPE == HD_TYPE_Q5_0) {
+        const float d = h2f((uint16_t)g.d);
+#pragma unroll
+        for (int i = 0; i < 4; i++) {
+            const uint32_t b = part ? (((wd[i] >> 4) & 0x0F0F0F0Fu) | ((g.qh << (4 - i)) & 0x10101010u))
+                                    : ((wd[i] & 0x0F0F0F0Fu) | ((g.qh >> i) & 0x10101010u));
+#pragma unroll
+            for (int c = 0; c < 4; c++) v[4 * i + c] = __fmul_rn(mag(b, c) - 8388624.0f, d);
+        }
+    } else if constexpr (TYPE == HD_TYPE_Q4_K) {
+        int s6, m6;
+        q4k_sm_regs(u & 7, g.m.y, g.m.z, g.m.w, s6, m6);
+        const float d1 = __fmul_rn(h2f((uint16_t)(g.m.x & 0xFFFF)), (float)s6);
+        const float m1 = __fmul_rn(h2f((uint16_t)(g.m.x >> 16)), (float)m6);
+#pragma unroll
+        for (int i = 0; i < 4; i++) {
+            const uint32_t b = (wd[i] >> (4 * part)) & 0x0F0F0F0Fu;
+#pragma unroll
+            for (int c = 0; c < 4; c++) v[4 * i + c] = __fsub_rn(__fmul_rn(mag(b, c) - 8388608.0f, d1), m1);
+        }
+    } else {
+        const uint32_t sw = (u & 4) ? ((u & 2) ? g.m.w : g.m.z) : ((u & 2) ? g.m.y : g.m.x);
+        const float dd =
+            __fmul_rn(h2f((uint16_t)g.d), (float)(int8_t)((sw >> (8 * (2 * (u & 1) + part))) & 0xFF));
+#pragma unroll
+        for (int i = 0; i < 4; i++) {
+            const int sh = 4 - 2 * i;
+            const uint32_t hsel = part ? g.hb.y : g.hb.x;
+            const uint32_t hx = sh >= 0 ? (hsel << sh) : (hsel >> -sh);
+            const uint32_t b = ((wd[i] >> (4 * part)) & 0x0F0F0F0Fu) | (hx & 0x30303030u);
+#pragma unroll
+            for (int c = 0; c < 4; c++) v[4 * i + c] = __fmul_rn(mag(b, c) - 8388640.0f, dd);
+        }
+    }
+#pragma unroll
+    for (int j = 0; j < 8; j++) {
+        const float a = v[2 * j] * scale, b = v[2 * j + 1] * scale;
+        const __half2 h = __floats2half2_rn(a, b);
+        hi[j] = *reinterpret_cast<const uint32_t *>(&h);
+        lo[j] = pack_h2(a - __low2float(h), b - __high2float(h));
+    }
+}
+
 constexpr int DQ_WARPS = 16, DQ_THREADS = DQ_WARPS * 32;
 constexpr int NXW = 3;                                  // activation copy warps
 constexpr int W_X = DQ_WARPS, W_MMA = W_X + NXW, W_EPI = W_MMA + 1;
 constexpr int TC3_THREADS = (W_EPI + 4) * 32;
 
-// Shared memory: XS activation stages and PD raw slots for the dequantizers
-// (the weight bytes of PD K-steps in flight).  Tensor memory (512 columns):
-// two fp32 accumulators of BT columns, then AS bf16 weight stages of 32
-// columns (128 rows x 64 K values, two per column) that the MMA reads as A.
-template <int TYPE, int BT>
+// Shared memory: XS activation stages (EX: an fp16 hi and an fp16 lo tile
+// each) and PD raw slots for the dequantizers (the weight bytes of PD
+// K-steps in flight).  Tensor memory (512 columns): two fp32 accumulators of
+// BT columns, then AS weight stages of 32 columns (128 rows x 64 K values,
+// two per column; EX: 64 columns, hi then lo) that the MMA reads as A.
+template <int TYPE, int BT, int EX>
 struct TC3 {
     static constexpr int XB = BT * BK * 2;
+    static constexpr int XT = EX ? 2 : 1;
     static constexpr int RB = RawSlot<TYPE>::BYTES;
-    static constexpr int AS = (512 - 2 * BT) / 32 > 4 ? 4 : (512 - 2 * BT) / 32;
+    static constexpr int ASC = EX ? 64 : 32;
+    static constexpr int AS = (512 - 2 * BT) / ASC > 4 ? 4 : (512 - 2 * BT) / ASC;
     static constexpr int A_COL = 2 * BT;
     static_assert(AS >= 2, "tensor memory plan");
-    static constexpr int XS = BT >= 192 ? 6 : 8;
-    static constexpr int R_OFF = XS * XB;
+    static constexpr int XS = EX ? (BT >= 128 ? 4 : 6) : (BT >= 192 ? 6 : 8);
+    static constexpr int R_OFF = XS * XT * XB;
     static constexpr int FREE = 227 * 1024 - 1024 - 512 - R_OFF;
     static constexpr int PD = FREE / RB > 6 ? 6 : FREE / RB;
     static_assert(PD >= 2, "shared memory plan");
@@ -600,11 +676,12 @@ struct StepCursor {
 // same time share an activation tile in L2) and, when the tiles alone would
 // leave SMs idle, one of two K halves (KS = 2: both halves add into Y, zeroed
 // beforehand; two addends onto zero commute, so the sum is order-independent).
-template <int TYPE, int BT>
+template <int TYPE, int BT, int EX>
 __global__ void __launch_bounds__(TC3_THREADS, 1)
-    k_qgemm_tc3(WView w, const __grid_constant__ CUtensorMap tmx, float *__restrict__ Y, int T, int N, int ntm,
-                int ntiles, int KS, int *flag) {
-    using C = TC3<TYPE, BT>;
+    k_qgemm_tc3(WView w, const __grid_constant__ CUtensorMap tmx, const __grid_constant__ CUtensorMap tmx_lo,
+                float *__restrict__ Y, int T, int N, int ntm, int ntiles, int KS, int wshift,
+                const int *__restrict__ rowshift, int *flag) {
+    using C = TC3<TYPE, BT, EX>;
     constexpr int XS = C::XS, AS = C::AS, PD = C::PD;
     extern __shared__ uint8_t smem_raw[];
     __shared__ __align__(8) uint64_t x_full[XS], x_empty[XS], a_full[AS], a_empty[AS];
@@ -631,6 +708,7 @@ __global__ void __launch_bounds__(TC3_THREADS, 1)
         mbar_init(smem_u32(&fin_bar), 1);
         asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
         asm volatile("prefetch.tensormap [%0];" ::"l"((uint64_t)&tmx) : "memory");
+        if (EX) asm volatile("prefetch.tensormap [%0];" ::"l"((uint64_t)&tmx_lo) : "memory");
     }
     if (warp == W_MMA) {
         asm volatile("tcgen05.alloc.cta_group::1.sync.aligned.shared::cta.b32 [%0], %1;" ::"r"(smem_u32(&tmem_base_sh)),
@@ -654,6 +732,7 @@ __global__ void __launch_bounds__(TC3_THREADS, 1)
         // whose slot is then refilled.
         const int e = threadIdx.x & 255, r = e & 127, h = e >> 7, part = threadIdx.x >> 8;
         uint8_t *slots = base + C::R_OFF;
+        const float wscale = __int_as_float((127 + wshift) << 23);  // 2^wshift, |wshift| <= 60
         StepCursor cl, cc;  // fetch cursor PD - 1 steps ahead of the compute cursor
         bool alive = true;
         cl.start(nitems, ntiles, ntm, kper, ksteps);
@@ -680,16 +759,19 @@ __global__ void __launch_bounds__(TC3_THREADS, 1)
             const int u = 2 * cc.ks + h;
             DqRaw rg;
             if (u < units) dq_read<TYPE>(slots + (g % PD) * C::RB, e, part, r & 1, rg);
-            uint32_t o[8];
-            dq_words<TYPE>(u, part, u < units, rg, o);
+            uint32_t o[8], ol[8];
+            if constexpr (EX) dq_words_exact<TYPE>(u, part, u < units, rg, wscale, o, ol);
+            else dq_words<TYPE>(u, part, u < units, rg, o);
             // After a failed wait the thread stops storing but keeps its place
             // in the loop, so that every thread takes the named barrier
             // equally often.
             alive = alive && mbar_wait(smem_u32(&a_empty[as]), ((g / AS) & 1) ^ 1, flag);
             if (alive) {
                 tc_fence_after();
-                tmem_st8(tmem + ((uint32_t)(32 * (warp & 3)) << 16) + (uint32_t)(C::A_COL + 32 * as + 16 * h + 8 * part),
-                         o);
+                const uint32_t ta = tmem + ((uint32_t)(32 * (warp & 3)) << 16) +
+                                    (uint32_t)(C::A_COL + C::ASC * as + 16 * h + 8 * part);
+                tmem_st8(ta, o);
+                if constexpr (EX) tmem_st8(ta + 32, ol);
                 tc_fence_before();
             }
             mbar_arrive(smem_u32(&a_full[as]));
@@ -711,8 +793,9 @@ __global__ void __launch_bounds__(TC3_THREADS, 1)
                     const int s = g % XS;
                     if (!mbar_wait(smem_u32(&x_empty[s]), ((g / XS) & 1) ^ 1, flag, 64)) { alive = false; break; }
                     const uint32_t bar = smem_u32(&x_full[s]);
-                    mbar_expect_tx(bar, C::XB);
-                    tma_2d(smem_u32(base + s * C::XB), &tmx, ks * BK, t0, bar);
+                    mbar_expect_tx(bar, C::XT * C::XB);
+                    tma_2d(smem_u32(base + s * C::XT * C::XB), &tmx, ks * BK, t0, bar);
+                    if (EX) tma_2d(smem_u32(base + (s * C::XT + 1) * C::XB), &tmx_lo, ks * BK, t0, bar);
                     last[s] = g;
                 }
             }
@@ -726,7 +809,7 @@ __global__ void __launch_bounds__(TC3_THREADS, 1)
     } else if (warp == W_MMA) {
         // ---- MMA issuer
         if (lane == 0) {
-            constexpr uint32_t idesc = idesc_bf16(BT);
+            constexpr uint32_t idesc = EX ? idesc_f16(BT) : idesc_bf16(BT);
             int g = 0, li = 0;
             bool alive = true;
             for (int item = blockIdx.x; item < nitems && alive; item += gridDim.x, li++) {
@@ -743,7 +826,8 @@ __global__ void __launch_bounds__(TC3_THREADS, 1)
                         break;
                     }
                     tc_fence_after();
-                    const uint32_t a0 = tmem + (uint32_t)(C::A_COL + 32 * as), b0 = smem_u32(base + xs * C::XB);
+                    const uint32_t a0 = tmem + (uint32_t)(C::A_COL + C::ASC * as);
+                    const uint32_t b0 = smem_u32(base + xs * C::XT * C::XB);
 #pragma unroll
                     for (int kk = 0; kk < BK / 16; kk++) {
                         const uint64_t bd = sw128_desc(b0 + kk * 32);
@@ -752,6 +836,14 @@ __global__ void __launch_bounds__(TC3_THREADS, 1)
                             "{\n .reg .pred p;\n setp.ne.b32 p, %4, 0;\n"
                             " tcgen05.mma.cta_group::1.kind::f16 [%0], [%1], %2, %3, p;\n}\n" ::"r"(d),
                             "r"(a0 + 8 * kk), "l"(bd), "r"(idesc), "r"(acc));
+                        if constexpr (EX) {
+                            // + w_hi x_lo + w_lo x_hi (w_lo x_lo is below 2^-22)
+                            const uint64_t bdl = sw128_desc(b0 + C::XB + kk * 32);
+                            asm volatile("tcgen05.mma.cta_group::1.kind::f16 [%0], [%1], %2, %3, 1;" ::"r"(d),
+                                         "r"(a0 + 8 * kk), "l"(bdl), "r"(idesc));
+                            asm volatile("tcgen05.mma.cta_group::1.kind::f16 [%0], [%1], %2, %3, 1;" ::"r"(d),
+                                         "r"(a0 + 32 + 8 * kk), "l"(bd), "r"(idesc));
+                        }
                     }
                     asm volatile("tcgen05.commit.cta_group::1.mbarrier::arrive::one.shared::cluster.b64 [%0];" ::"r"(
                                      smem_u32(&x_empty[xs]))
@@ -799,9 +891,12 @@ __global__ void __launch_bounds__(TC3_THREADS, 1)
                 for (int j = 0; j < 16; j++) {
                     const int t = t0 + c0 + j;
                     if (t < T) {
+                        float v = __uint_as_float(rr[j]);
+                        // EX: undo 2^(wshift + rowshift[t]) (exact power of two)
+                        if (EX) v *= __int_as_float((127 - wshift - __ldg(rowshift + t)) << 23);
                         float *dst = Y + (int64_t)t * N + n;
-                        if (KS == 1) *dst = __uint_as_float(rr[j]);
-                        else atomicAdd(dst, __uint_as_float(rr[j]));
+                        if (KS == 1) *dst = v;
+                        else atomicAdd(dst, v);
                     }
                 }
             }
@@ -816,6 +911,49 @@ __global__ void __launch_bounds__(TC3_THREADS, 1)
         tc_fence_after();
         asm volatile("tcgen05.dealloc.cta_group::1.sync.aligned.b32 %0, %1;" ::"r"(tmem), "r"(512));
     }
+}
+
+// Exact-product mode: row t of x times 2^rowshift[t] (largest magnitude near
+// 2^14), split into fp16 halves hi + lo (|x - hi - lo| <= 2^-22 |x|).  One
+// CTA per row; K % 8 == 0.
+__global__ void k_to_f16_split(const float *__restrict__ x, int K, __half *__restrict__ hi, __half *__restrict__ lo,
+                               int *__restrict__ rowshift) {
+    __shared__ float red[32];
+    pdl_wait();
+    pdl_trigger();
+    const int64_t t = blockIdx.x;
+    const float4 *xr = (const float4 *)(x + t * K);
+    float m = 0.f;
+    for (int k = threadIdx.x; k < K / 4; k += blockDim.x) {
+        const float4 v = xr[k];
+        m = fmaxf(m, fmaxf(fmaxf(fabsf(v.x), fabsf(v.y)), fmaxf(fabsf(v.z), fabsf(v.w))));
+    }
+    for (int o = 16; o > 0; o >>= 1) m = fmaxf(m, __shfl_xor_sync(0xffffffffu, m, o));
+    if ((threadIdx.x & 31) == 0) red[threadIdx.x >> 5] = m;
+    __syncthreads();
+    m = 0.f;
+    for (int i = 0; i < (int)(blockDim.x >> 5); i++) m = fmaxf(m, red[i]);
+    int sh = 0;
+    if (m > 0.f && m < INFINITY) {
+        int ex;
+        frexpf(16384.f / m, &ex);
+        sh = ex - 1;
+        sh = sh < -60 ? -60 : sh > 60 ? 60 : sh;
+    }
+    const float sc = __int_as_float((127 + sh) << 23);
+    for (int k = threadIdx.x; k < K / 4; k += blockDim.x) {
+        const float4 v = xr[k];
+        const float a0 = v.x * sc, a1 = v.y * sc, a2 = v.z * sc, a3 = v.w * sc;
+        const __half2 h01 = __floats2half2_rn(a0, a1), h23 = __floats2half2_rn(a2, a3);
+        const __half2 l01 = __floats2half2_rn(a0 - __low2float(h01), a1 - __high2float(h01));
+        const __half2 l23 = __floats2half2_rn(a2 - __low2float(h23), a3 - __high2float(h23));
+        __half2 *ph = (__half2 *)(hi + t * K) + 2 * k, *pl = (__half2 *)(lo + t * K) + 2 * k;
+        ph[0] = h01;
+        ph[1] = h23;
+        pl[0] = l01;
+        pl[1] = l23;
+    }
+    if (threadIdx.x == 0) rowshift[t] = sh;
 }
 
 __global__ void k_to_bf16(const float *__restrict__ x, __nv_bfloat16 *__restrict__ y, int64_t n) {
@@ -849,10 +987,12 @@ EncodeTiledFn encode_tiled() {
     return fn;
 }
 
-template <int TYPE, int BT>
-cudaError_t launch_tc3(hd_ctx *ctx, const hd_weight *w, const CUtensorMap &tmx, float *Y, int T, int ks) {
-    constexpr size_t smem = TC3<TYPE, BT>::SMEM;
-    cudaError_t e = cudaFuncSetAttribute(k_qgemm_tc3<TYPE, BT>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
+template <int TYPE, int BT, int EX>
+cudaError_t launch_tc3(hd_ctx *ctx, const hd_weight *w, const CUtensorMap &tmx, const CUtensorMap &tmx_lo, float *Y,
+                       int T, int ks, const int *rowshift) {
+    constexpr size_t smem = TC3<TYPE, BT, EX>::SMEM;
+    cudaError_t e =
+        cudaFuncSetAttribute(k_qgemm_tc3<TYPE, BT, EX>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
     if (e != cudaSuccess) return e;
     const int ntm = (int)(w->rows / 128), ntiles = ntm * ((T + BT - 1) / BT);
     if (ks == 2) {
@@ -861,62 +1001,87 @@ cudaError_t launch_tc3(hd_ctx *ctx, const hd_weight *w, const CUtensorMap &tmx, 
     }
     const int nitems = ntiles * ks;
     const int grid = nitems < ctx->sm_count ? nitems : ctx->sm_count;
-    return hd_launch(ctx, k_qgemm_tc3<TYPE, BT>, dim3(grid), dim3(TC3_THREADS), smem, wview(w), tmx, Y, T,
-                     (int)w->rows, ntm, ntiles, ks, ctx->flag);
+    return hd_launch(ctx, k_qgemm_tc3<TYPE, BT, EX>, dim3(grid), dim3(TC3_THREADS), smem, wview(w), tmx, tmx_lo, Y, T,
+                     (int)w->rows, ntm, ntiles, ks, w->f16_shift, rowshift, ctx->flag);
 }
 
 }  // namespace
 
 // rows % 128 == 0 uses the streamed v3 kernel, other shapes the v1 kernel.
-int hd_qgemm_tc(hd_ctx *ctx, const hd_weight *w, const float *X, float *Y, int T) {
+// exact != 0 (rows % 128 == 0 only): the fp32-accuracy mode -- exact weights
+// and x, each split into fp16 hi + lo, three MMAs per product.
+int hd_qgemm_tc(hd_ctx *ctx, const hd_weight *w, const float *X, float *Y, int T, int exact) {
     HD_REQUIRE(ctx, w->cols % 8 == 0, HD_E_SHAPE, "hd_qgemm: K must be a multiple of 8");
     const int64_t mt = (w->rows + 127) / 128;
     cudaError_t e = cudaSuccess;
-    if (w->rows % 128 == 0 && ((uintptr_t)Y & 15) == 0 && getenv("HACEDLE_TC_V1") == nullptr) {
-        // bf16 copy of the activations for the TMA
-        const size_t need = (size_t)T * w->cols * sizeof(__nv_bfloat16);
+    const bool v3 = w->rows % 128 == 0 && ((uintptr_t)Y & 15) == 0 && (exact || getenv("HACEDLE_TC_V1") == nullptr);
+    HD_REQUIRE(ctx, v3 || !exact, HD_E_UNSUPPORTED, "hd_qgemm: the exact tensor-core mode needs rows % 128 == 0");
+    if (v3) {
+        // activations for the TMA: bf16, or (exact) fp16 hi and lo planes and
+        // the per-row shifts
+        const size_t plane = ((size_t)T * w->cols * 2 + 255) & ~(size_t)255;
+        const size_t need = exact ? 2 * plane + (size_t)T * sizeof(int) : plane;
         int rc = hd_ensure_hbuf(ctx, &ctx->xbf, &ctx->xbf_bytes, (need + 3) / 4 * 4);
         if (rc) return rc;
+        uint8_t *xb = (uint8_t *)ctx->xbf;
+        int *rowshift = exact ? (int *)(xb + 2 * plane) : nullptr;
         const int64_t n = (int64_t)T * w->cols;
-        e = hd_launch(ctx, k_to_bf16, dim3((unsigned)((n / 4 + 255) / 256 + 1)), dim3(256), 0, X,
-                      (__nv_bfloat16 *)ctx->xbf, n);
-        if (e != cudaSuccess) return hd_fail(ctx, HD_E_CUDA, "hd_qgemm (bf16 convert): %s", cudaGetErrorString(e));
+        if (exact)
+            e = hd_launch(ctx, k_to_f16_split, dim3((unsigned)T), dim3(256), 0, X, (int)w->cols, (__half *)xb,
+                          (__half *)(xb + plane), rowshift);
+        else
+            e = hd_launch(ctx, k_to_bf16, dim3((unsigned)((n / 4 + 255) / 256 + 1)), dim3(256), 0, X,
+                          (__nv_bfloat16 *)xb, n);
+        if (e != cudaSuccess) return hd_fail(ctx, HD_E_CUDA, "hd_qgemm (activation convert): %s", cudaGetErrorString(e));
         // Token tile and K split by a cost model: rounds of items per SM x
-        // steps per item x cycles per step (the MMA's 2*BT plus ~200 cycles of
-        // per-step overhead); ties go to the smaller tile.
+        // steps per item x cycles per step (the MMA's 2*BT per product plus
+        // ~200 cycles of per-step overhead); ties go to the smaller tile.
         const int ksteps = (int)((w->units + 1) / 2);
         auto ksplit = [&](int cand) {
             return (2 * mt * ((T + cand - 1) / cand) <= ctx->sm_count && w->units >= 8) ? 2 : 1;
         };
+        const int top = exact ? 160 : 208;
         int bt = 64;
         double best = 1e30;
-        for (int cand : {64, 128, 208}) {
+        for (int cand : {64, 128, top}) {
             if (cand > 64 && T <= cand / 2) continue;
             const int64_t tiles = mt * ((T + cand - 1) / cand);
             const int ck = ksplit(cand);
             const double rounds = (double)((tiles * ck + ctx->sm_count - 1) / ctx->sm_count);
-            const double cost = rounds * ((ksteps + ck - 1) / ck) * (2.0 * cand + 200.0);
+            const double cost = rounds * ((ksteps + ck - 1) / ck) * ((exact ? 6.0 : 2.0) * cand + 200.0);
             if (cost < best - 1e-9) { best = cost; bt = cand; }
         }
         const char *bt_env = getenv("HACEDLE_TC_BT");
-        if (bt_env && (atoi(bt_env) == 64 || atoi(bt_env) == 128 || atoi(bt_env) == 208)) bt = atoi(bt_env);
+        if (bt_env && (atoi(bt_env) == 64 || atoi(bt_env) == 128 || atoi(bt_env) == top)) bt = atoi(bt_env);
         const int ks = ksplit(bt);
-        CUtensorMap tm;
+        EncodeTiledFn enc = encode_tiled();
+        if (!enc) return hd_fail(ctx, HD_E_CUDA, "hd_qgemm: cuTensorMapEncodeTiled is not available");
+        CUtensorMap tm, tm_lo;
         cuuint64_t dims[2] = {(cuuint64_t)w->cols, (cuuint64_t)T};
         cuuint64_t strides[1] = {(cuuint64_t)w->cols * 2};
         cuuint32_t box[2] = {(cuuint32_t)BK, (cuuint32_t)bt};
         cuuint32_t estr[2] = {1, 1};
-        EncodeTiledFn enc = encode_tiled();
-        if (!enc) return hd_fail(ctx, HD_E_CUDA, "hd_qgemm: cuTensorMapEncodeTiled is not available");
-        CUresult cr = enc(&tm, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 2, ctx->xbf, dims, strides, box,
-                                             estr, CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B,
-                                             CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+        const CUtensorMapDataType dt = exact ? CU_TENSOR_MAP_DATA_TYPE_FLOAT16 : CU_TENSOR_MAP_DATA_TYPE_BFLOAT16;
+        CUresult cr = enc(&tm, dt, 2, xb, dims, strides, box, estr, CU_TENSOR_MAP_INTERLEAVE_NONE,
+                          CU_TENSOR_MAP_SWIZZLE_128B, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
+                          CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+        if (cr == CUDA_SUCCESS)
+            cr = enc(&tm_lo, dt, 2, exact ? xb + plane : xb, dims, strides, box, estr, CU_TENSOR_MAP_INTERLEAVE_NONE,
+                     CU_TENSOR_MAP_SWIZZLE_128B, CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
         if (cr != CUDA_SUCCESS) return hd_fail(ctx, HD_E_CUDA, "hd_qgemm: cuTensorMapEncodeTiled failed (%d)", (int)cr);
-        HD_TYPE_SWITCH(w->type, TT, {
-            if (bt == 64) e = launch_tc3<TT, 64>(ctx, w, tm, Y, T, ks);
-            else if (bt == 128) e = launch_tc3<TT, 128>(ctx, w, tm, Y, T, ks);
-            else e = launch_tc3<TT, 208>(ctx, w, tm, Y, T, ks);
-        });
+        if (exact) {
+            HD_TYPE_SWITCH(w->type, TT, {
+                if (bt == 64) e = launch_tc3<TT, 64, 1>(ctx, w, tm, tm_lo, Y, T, ks, rowshift);
+                else if (bt == 128) e = launch_tc3<TT, 128, 1>(ctx, w, tm, tm_lo, Y, T, ks, rowshift);
+                else e = launch_tc3<TT, 160, 1>(ctx, w, tm, tm_lo, Y, T, ks, rowshift);
+            });
+        } else {
+            HD_TYPE_SWITCH(w->type, TT, {
+                if (bt == 64) e = launch_tc3<TT, 64, 0>(ctx, w, tm, tm_lo, Y, T, ks, rowshift);
+                else if (bt == 128) e = launch_tc3<TT, 128, 0>(ctx, w, tm, tm_lo, Y, T, ks, rowshift);
+                else e = launch_tc3<TT, 208, 0>(ctx, w, tm, tm_lo, Y, T, ks, rowshift);
+            });
+        }
         if (e != cudaSuccess) return hd_fail(ctx, HD_E_CUDA, "hd_qgemm (tcgen05 v3): %s", cudaGetErrorString(e));
         return HD_OK;
     }

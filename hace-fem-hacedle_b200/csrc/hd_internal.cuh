@@ -66,6 +66,10 @@ struct hd_weight {
     size_t alloc_bytes = 0;
     uint8_t *q = nullptr, *aux = nullptr, *meta = nullptr;
     uint16_t *dsb = nullptr;
+    // 2^f16_shift * |w| <= 2^15 for every dequantized value w (bound from the
+    // block scales at upload): the exact-product tensor-core GEMM splits
+    // scaled weights into fp16 halves without overflow
+    int f16_shift = 0;
 };
 
 // Plain view passed by value to kernels.

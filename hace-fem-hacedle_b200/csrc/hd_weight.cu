@@ -1,5 +1,8 @@
 // hd_weight.cu -- device weight handles: upload with re-layout, its inverse,
 // bit-exact dequantization (QuantTensorView::dequantize) and embedding rows.
+#include <cmath>
+#include <cstring>
+
 #include "hd_internal.cuh"
 
 namespace {
@@ -69,6 +72,34 @@ __global__ void k_relayout(const uint8_t *__restrict__ src, WView w, uint8_t *q,
 
 // Inverse of k_relayout.  Q8_0/Q5_0: one thread per (row, unit); Q4_K/Q6_K:
 // one thread per (row, super-block), since two units share GGUF bytes.
+// Upper bound of |w| over one unit of one row (exact decoded values never
+// exceed it), max-reduced as float bits (non-negative floats order as ints).
+template <int TYPE>
+__global__ void k_wbound(WView w, unsigned int *out) {
+    const int64_t i = (int64_t)blockIdx.x * blockDim.x + threadIdx.x;
+    float b = 0.f;
+    if (i < w.rows * (int64_t)w.units) {
+        const int u = (int)(i / w.rows);
+        const int64_t r = i % w.rows, ur = (int64_t)u * w.rows + r;
+        if constexpr (TYPE == HD_TYPE_Q8_0 || TYPE == HD_TYPE_Q5_0) {
+            b = fabsf(h2f(((const uint16_t *)w.meta)[ur])) * (TYPE == HD_TYPE_Q8_0 ? 128.f : 16.f);
+        } else if constexpr (TYPE == HD_TYPE_Q4_K) {
+            const uint8_t *m = w.meta + ((int64_t)(u >> 3) * w.rows + r) * 16;
+            int sc, mn;
+            q4k_sm(u & 7, m + 4, sc, mn);
+            b = fabsf(h2f(*(const uint16_t *)m)) * (float)sc * 15.f + fabsf(h2f(*(const uint16_t *)(m + 2))) * (float)mn;
+        } else {
+            const int64_t sr = (int64_t)(u >> 3) * w.rows + r;
+            const int8_t *sc = (const int8_t *)(w.meta + sr * 16) + 2 * (u & 7);
+            const float d = fabsf(h2f(w.dsb[sr]));
+            b = d * 32.f * fmaxf(fabsf((float)sc[0]), fabsf((float)sc[1]));
+        }
+    }
+    if (!(b == b)) b = INFINITY;
+    for (int o = 16; o > 0; o >>= 1) b = fmaxf(b, __shfl_xor_sync(0xffffffffu, b, o));
+    if ((threadIdx.x & 31) == 0 && b > 0.f) atomicMax(out, __float_as_uint(b));
+}
+
 template <int TYPE>
 __global__ void k_unlayout(WView w, uint8_t *__restrict__ dst) {
     pdl_wait();
@@ -239,12 +270,31 @@ int upload_common(hd_ctx *ctx, const uint8_t *src, bool src_on_device, size_t nb
     cudaError_t e = cudaSuccess;
     HD_TYPE_SWITCH(type, T, e = hd_launch(ctx, k_relayout<T>, grid, dim3(256), 0, dsrc, v, w->q, w->aux, w->meta,
                                           w->dsb));
+    // scale bound for the exact-product GEMM (f16_shift)
+    unsigned int *bound = nullptr, hb = 0;
+    if (e == cudaSuccess && cudaMalloc(&bound, sizeof(unsigned int)) != cudaSuccess) e = cudaErrorMemoryAllocation;
+    if (e == cudaSuccess) e = cudaMemsetAsync(bound, 0, sizeof(unsigned int), ctx->stream);
+    if (e == cudaSuccess)
+        HD_TYPE_SWITCH(type, T, e = hd_launch(ctx, k_wbound<T>, grid, dim3(256), 0, v, bound));
+    if (e == cudaSuccess) e = cudaMemcpyAsync(&hb, bound, sizeof(hb), cudaMemcpyDeviceToHost, ctx->stream);
     if (e == cudaSuccess) e = cudaStreamSynchronize(ctx->stream);
+    if (bound) cudaFree(bound);
     if (tmp) cudaFree(tmp);
     if (e != cudaSuccess) {
         cudaFree(w->base);
         delete w;
         return hd_fail(ctx, HD_E_CUDA, "hd_weight_upload: relayout: %s", cudaGetErrorString(e));
+    }
+    {
+        float bmax;
+        memcpy(&bmax, &hb, sizeof(bmax));
+        int sh = 0;
+        if (bmax > 0.f && bmax < INFINITY) {
+            int ex;
+            frexpf(32768.f / bmax, &ex);  // 2^(ex-1) <= 32768 / bmax < 2^ex
+            sh = ex - 1;
+        }
+        w->f16_shift = sh < -60 ? -60 : sh > 60 ? 60 : sh;
     }
     *out = w;
     return HD_OK;
