@@ -33,6 +33,44 @@ __global__ void k_kv_append(const float *__restrict__ k, const float *__restrict
     vc[dst] = v[i];
 }
 
+// Fused q/k/v rows [rows][ld] = q heads | k heads | v heads: NEOX RoPE on the
+// q and k heads in place (the arithmetic of k_rope_neox), and the rotated k
+// and v of row r appended to cache sequence r / T at position pos[r].
+__global__ void k_rope_kv_append(float *qkv, int64_t ld, const int32_t *__restrict__ pos,
+                                 const float *__restrict__ freq, int rows, int T, int n_heads, int n_kv, int hd,
+                                 float *kc, float *vc, int max_ctx) {
+    pdl_wait();
+    pdl_trigger();
+    const int half = hd >> 1, nr = n_heads + n_kv;
+    const int64_t nrot = (int64_t)rows * nr * half, nv = (int64_t)rows * n_kv * hd;
+    int64_t idx = (int64_t)blockIdx.x * blockDim.x + threadIdx.x;
+    if (idx < nrot) {
+        const int i = (int)(idx % half);
+        const int64_t rh = idx / half;
+        const int head = (int)(rh % nr), r = (int)(rh / nr);
+        float *v = qkv + (int64_t)r * ld + (int64_t)head * hd;
+        const int p = pos[r];
+        const float angle = __fdiv_rn((float)p, freq[i]);
+        const float c = cosf(angle), sn = sinf(angle);
+        const float x0 = v[i], x1 = v[i + half];
+        const float y0 = __fsub_rn(__fmul_rn(x0, c), __fmul_rn(x1, sn));
+        const float y1 = __fadd_rn(__fmul_rn(x0, sn), __fmul_rn(x1, c));
+        v[i] = y0;
+        v[i + half] = y1;
+        if (head >= n_heads && p >= 0 && p < max_ctx) {  // KvCache::append ignores pos >= max_seq_len
+            float *dst = kc + (((int64_t)(r / T) * max_ctx + p) * n_kv + (head - n_heads)) * hd;
+            dst[i] = y0;
+            dst[i + half] = y1;
+        }
+    } else if (idx < nrot + nv) {
+        const int64_t j = idx - nrot;
+        const int e = (int)(j % ((int64_t)n_kv * hd)), r = (int)(j / ((int64_t)n_kv * hd));
+        const int p = pos[r];
+        if (p >= 0 && p < max_ctx)
+            vc[((int64_t)(r / T) * max_ctx + p) * n_kv * hd + e] = qkv[(int64_t)r * ld + (int64_t)nr * hd + e];
+    }
+}
+
 // rows: query rows; row r reads cache sequence cseq(r) with length len(r):
 //   decode  (lens != null): cseq = r, len = lens[r]
 //   prefill (lens == null): rows are seqT consecutive tokens per sequence,
@@ -42,7 +80,7 @@ constexpr int ANT = 128;   // threads per CTA
 constexpr int MAXREP = 16;
 
 template <int HD>
-__global__ void __launch_bounds__(ANT) k_attention(const float *__restrict__ q, const float *__restrict__ kc,
+__global__ void __launch_bounds__(ANT) k_attention(const float *__restrict__ q, int64_t qld, const float *__restrict__ kc,
                                                    const float *__restrict__ vc, const int32_t *__restrict__ lens,
                                                    int pos0, int seqT, int n_heads, int n_kv, int max_ctx,
                                                    float scale, int P, int cpc, float *ws, int *tickets,
@@ -66,7 +104,7 @@ __global__ void __launch_bounds__(ANT) k_attention(const float *__restrict__ q, 
     float *Vs = sm + ((rep * KP + CH * KP + 3) & ~3);      // [CH][HD], 16-byte aligned for float4 stores
     float *S = Vs + CH * HD;                               // [rep][CH]
     float *mrun = S + rep * CH, *lrun = mrun + MAXREP, *alpha = lrun + MAXREP;
-    const float *qr = q + ((int64_t)r * n_heads + h0) * HD;
+    const float *qr = q + (int64_t)r * qld + (int64_t)h0 * HD;
     for (int i = tid; i < rep * HD; i += ANT) qs[(i / HD) * KP + i % HD] = qr[i];
     if (tid < rep) {
         mrun[tid] = -INFINITY;
@@ -188,7 +226,7 @@ size_t attn_smem(int rep) {
 }
 
 template <int HD>
-cudaError_t launch_attn(hd_ctx *ctx, int rows, int n_heads, int n_kv, int P, int cpc, const float *q,
+cudaError_t launch_attn(hd_ctx *ctx, int rows, int n_heads, int n_kv, int P, int cpc, const float *q, int64_t qld,
                         const float *kc, const float *vc, const int32_t *lens, int pos0, int seqT, int max_ctx,
                         float *out) {
     const int rep = n_heads / n_kv;
@@ -198,14 +236,14 @@ cudaError_t launch_attn(hd_ctx *ctx, int rows, int n_heads, int n_kv, int P, int
         if (e != cudaSuccess) return e;
     }
     const float scale = sqrtf((float)HD);
-    return hd_launch(ctx, k_attention<HD>, dim3(rows, n_kv, P), dim3(ANT), smem, q, kc, vc, lens, pos0, seqT,
+    return hd_launch(ctx, k_attention<HD>, dim3(rows, n_kv, P), dim3(ANT), smem, q, qld, kc, vc, lens, pos0, seqT,
                      n_heads, n_kv, max_ctx, scale, P, cpc, (float *)ctx->ws, ctx->tickets, out);
 }
 
 }  // namespace
 
-int hd_attention_run(hd_ctx *ctx, const float *q, const float *kc, const float *vc, const int32_t *lens, int rows,
-                     int pos0, int seqT, int n_heads, int n_kv, int hd, int max_ctx, int maxlen, float *out,
+int hd_attention_run(hd_ctx *ctx, const float *q, int64_t qld, const float *kc, const float *vc, const int32_t *lens,
+                     int rows, int pos0, int seqT, int n_heads, int n_kv, int hd, int max_ctx, int maxlen, float *out,
                      const char *name) {
     if (!ctx || !q || !kc || !vc || !out) return hd_fail(ctx, HD_E_ARG, "%s: null argument", name);
     HD_REQUIRE(ctx, n_heads > 0 && n_kv > 0 && n_heads % n_kv == 0 && n_heads / n_kv <= MAXREP, HD_E_SHAPE,
@@ -231,10 +269,21 @@ int hd_attention_run(hd_ctx *ctx, const float *q, const float *kc, const float *
         if (rc) return rc;
     }
     cudaError_t e;
-    if (hd == 64) e = launch_attn<64>(ctx, rows, n_heads, n_kv, P, cpc, q, kc, vc, lens, pos0, seqT, max_ctx, out);
-    else if (hd == 128) e = launch_attn<128>(ctx, rows, n_heads, n_kv, P, cpc, q, kc, vc, lens, pos0, seqT, max_ctx, out);
-    else e = launch_attn<32>(ctx, rows, n_heads, n_kv, P, cpc, q, kc, vc, lens, pos0, seqT, max_ctx, out);
+    if (qld == 0) qld = (int64_t)n_heads * hd;
+    if (hd == 64) e = launch_attn<64>(ctx, rows, n_heads, n_kv, P, cpc, q, qld, kc, vc, lens, pos0, seqT, max_ctx, out);
+    else if (hd == 128)
+        e = launch_attn<128>(ctx, rows, n_heads, n_kv, P, cpc, q, qld, kc, vc, lens, pos0, seqT, max_ctx, out);
+    else e = launch_attn<32>(ctx, rows, n_heads, n_kv, P, cpc, q, qld, kc, vc, lens, pos0, seqT, max_ctx, out);
     if (e != cudaSuccess) return hd_fail(ctx, HD_E_CUDA, "%s: %s", name, cudaGetErrorString(e));
+    return HD_OK;
+}
+
+int hd_rope_kv_append(hd_ctx *ctx, float *qkv, int64_t ld, const int32_t *pos, int rows, int T, int n_heads, int n_kv,
+                      int hd, float *kc, float *vc, int max_ctx) {
+    const int64_t n = (int64_t)rows * ((int64_t)(n_heads + n_kv) * (hd / 2) + (int64_t)n_kv * hd);
+    if (n == 0) return HD_OK;
+    HD_CUDA_TRY(ctx, hd_launch(ctx, k_rope_kv_append, dim3((unsigned)((n + 255) / 256)), dim3(256), 0, qkv, ld, pos,
+                               (const float *)ctx->rope_freq, rows, T, n_heads, n_kv, hd, kc, vc, max_ctx));
     return HD_OK;
 }
 
@@ -254,13 +303,13 @@ extern "C" int hd_attention_decode(hd_ctx *ctx, const float *q, const float *kc,
                                    const int32_t *len, int seqs, int n_heads, int n_kv, int head_dim, int max_ctx,
                                    float *out) {
     if (!len) return hd_fail(ctx, HD_E_ARG, "hd_attention_decode: null lengths");
-    return hd_attention_run(ctx, q, kc, vc, len, seqs, 0, 1, n_heads, n_kv, head_dim, max_ctx, max_ctx, out,
+    return hd_attention_run(ctx, q, 0, kc, vc, len, seqs, 0, 1, n_heads, n_kv, head_dim, max_ctx, max_ctx, out,
                             "hd_attention_decode");
 }
 
 extern "C" int hd_attention_prefill(hd_ctx *ctx, const float *q, const float *kc, const float *vc, int T, int pos0,
                                     int n_heads, int n_kv, int head_dim, int max_ctx, float *out) {
     if (T < 0 || pos0 < 0) return hd_fail(ctx, HD_E_ARG, "hd_attention_prefill: negative size");
-    return hd_attention_run(ctx, q, kc, vc, nullptr, T, pos0, T > 0 ? T : 1, n_heads, n_kv, head_dim, max_ctx,
+    return hd_attention_run(ctx, q, 0, kc, vc, nullptr, T, pos0, T > 0 ? T : 1, n_heads, n_kv, head_dim, max_ctx,
                             pos0 + T, out, "hd_attention_prefill");
 }

@@ -15,6 +15,8 @@
 // residual and SwiGLU epilogues; above that they are Q-GEMMs.
 //
 // KV cache: [layer][seq][max_ctx][n_kv][head_dim] f32.
+#include <cstdlib>
+#include <cstring>
 #include <vector>
 
 #include "hd_internal.cuh"
@@ -25,6 +27,10 @@ struct hd_decoder {
     struct Layer {
         const hd_weight *wq, *wk, *wv, *wo, *wg, *wu, *wd;
         float *bq, *bk, *bv, *attn_norm, *ffn_norm;
+        // q, k and v stacked by rows into one weight (owned) and one bias,
+        // when their types and widths agree: one projection per layer
+        hd_weight *wqkv = nullptr;
+        float *bqkv = nullptr;
     };
     std::vector<Layer> L;
     float *out_norm = nullptr;
@@ -32,7 +38,7 @@ struct hd_decoder {
     float *kc = nullptr, *vc = nullptr;
     // decode state, sized for max_seqs
     float *h = nullptr, *xn = nullptr, *q = nullptr, *k = nullptr, *v = nullptr, *att = nullptr, *a = nullptr,
-          *g = nullptr, *tmp = nullptr, *logits = nullptr;
+          *g = nullptr, *tmp = nullptr, *logits = nullptr, *qkv = nullptr;
     int32_t *tok = nullptr, *pos = nullptr, *lens = nullptr, *amax = nullptr, *step = nullptr, *hist = nullptr;
     size_t hist_cap = 0;
     std::vector<void *> allocs;
@@ -145,20 +151,37 @@ int layer_forward(hd_decoder *d, int li, int rows, const int32_t *pos, const int
     const int hd = c.head_dim, nkv = c.n_kv * hd;
     const size_t lay = (size_t)li * c.max_seqs * c.max_ctx * nkv;
     int rc = hd_rmsnorm(ctx, d->h, l.attn_norm, nullptr, d->xn, rows, c.hidden, c.eps);
-    if (!rc) rc = linear(d, l.wq, d->xn, d->q, rows, l.bq, nullptr, prec);
-    if (!rc) rc = linear(d, l.wk, d->xn, d->k, rows, l.bk, nullptr, prec);
-    if (!rc) rc = linear(d, l.wv, d->xn, d->v, rows, l.bv, nullptr, prec);
-    if (!rc) rc = hd_rope_neox(ctx, d->q, pos, rows, c.n_heads, hd, c.theta);
-    if (!rc) rc = hd_rope_neox(ctx, d->k, pos, rows, c.n_kv, hd, c.theta);
-    if (rc) return rc;
-    if (lens) {
-        rc = hd_kv_append(ctx, d->k, d->v, d->kc + lay, d->vc + lay, pos, S, 1, c.n_kv, hd, c.max_ctx);
-        if (!rc) rc = hd_attention_run(ctx, d->q, d->kc + lay, d->vc + lay, lens, S, 0, 1, c.n_heads, c.n_kv, hd,
-                                       c.max_ctx, c.max_ctx, d->att, "decoder attention");
+    if (l.wqkv) {
+        // one q|k|v projection, RoPE + cache append in one kernel, attention
+        // reading q from the fused rows
+        const int64_t ld = l.wqkv->rows;
+        if (!rc) rc = linear(d, l.wqkv, d->xn, d->qkv, rows, l.bqkv, nullptr, prec);
+        if (!rc)
+            rc = hd_rope_kv_append(ctx, d->qkv, ld, pos, rows, lens ? 1 : T, c.n_heads, c.n_kv, hd, d->kc + lay,
+                                   d->vc + lay, c.max_ctx);
+        if (rc) return rc;
+        if (lens)
+            rc = hd_attention_run(ctx, d->qkv, ld, d->kc + lay, d->vc + lay, lens, S, 0, 1, c.n_heads, c.n_kv, hd,
+                                  c.max_ctx, c.max_ctx, d->att, "decoder attention");
+        else
+            rc = hd_attention_run(ctx, d->qkv, ld, d->kc + lay, d->vc + lay, nullptr, rows, 0, T, c.n_heads, c.n_kv,
+                                  hd, c.max_ctx, T, d->att, "decoder prefill attention");
     } else {
-        rc = hd_kv_append(ctx, d->k, d->v, d->kc + lay, d->vc + lay, pos0_zero, S, T, c.n_kv, hd, c.max_ctx);
-        if (!rc) rc = hd_attention_run(ctx, d->q, d->kc + lay, d->vc + lay, nullptr, rows, 0, T, c.n_heads, c.n_kv,
-                                       hd, c.max_ctx, T, d->att, "decoder prefill attention");
+        if (!rc) rc = linear(d, l.wq, d->xn, d->q, rows, l.bq, nullptr, prec);
+        if (!rc) rc = linear(d, l.wk, d->xn, d->k, rows, l.bk, nullptr, prec);
+        if (!rc) rc = linear(d, l.wv, d->xn, d->v, rows, l.bv, nullptr, prec);
+        if (!rc) rc = hd_rope_neox(ctx, d->q, pos, rows, c.n_heads, hd, c.theta);
+        if (!rc) rc = hd_rope_neox(ctx, d->k, pos, rows, c.n_kv, hd, c.theta);
+        if (rc) return rc;
+        if (lens) {
+            rc = hd_kv_append(ctx, d->k, d->v, d->kc + lay, d->vc + lay, pos, S, 1, c.n_kv, hd, c.max_ctx);
+            if (!rc) rc = hd_attention_run(ctx, d->q, 0, d->kc + lay, d->vc + lay, lens, S, 0, 1, c.n_heads, c.n_kv,
+                                           hd, c.max_ctx, c.max_ctx, d->att, "decoder attention");
+        } else {
+            rc = hd_kv_append(ctx, d->k, d->v, d->kc + lay, d->vc + lay, pos0_zero, S, T, c.n_kv, hd, c.max_ctx);
+            if (!rc) rc = hd_attention_run(ctx, d->q, 0, d->kc + lay, d->vc + lay, nullptr, rows, 0, T, c.n_heads,
+                                           c.n_kv, hd, c.max_ctx, T, d->att, "decoder prefill attention");
+        }
     }
     if (!rc) rc = linear(d, l.wo, d->att, d->h, rows, nullptr, d->h, prec);
     if (!rc) rc = hd_rmsnorm(ctx, d->h, l.ffn_norm, nullptr, d->xn, rows, c.hidden, c.eps);
@@ -188,8 +211,39 @@ int decode_step(hd_decoder *d, int S, int n_gen, int prec) {
 }
 
 void free_all(hd_decoder *d) {
+    for (hd_decoder::Layer &l : d->L)
+        if (l.wqkv) {
+            hd_weight_free(d->ctx, l.wqkv);
+            l.wqkv = nullptr;
+        }
     for (void *p : d->allocs) cudaFree(p);
     d->allocs.clear();
+}
+
+// Stacks q, k and v by rows: the GGUF bytes of a weight are its rows in
+// order, so the stacked weight is the three byte strings one after another.
+int build_qkv(hd_decoder *d, hd_decoder::Layer &D, const hd_layer_weights &l) {
+    hd_ctx *ctx = d->ctx;
+    const hd_weight *ws[3] = {l.wq, l.wk, l.wv};
+    for (const hd_weight *w : ws)
+        if (w->type != l.wq->type || w->cols != l.wq->cols) return HD_OK;  // keep separate projections
+    size_t total = 0;
+    for (const hd_weight *w : ws) total += w->gguf_bytes;
+    std::vector<uint8_t> bytes(total);
+    size_t off = 0;
+    for (const hd_weight *w : ws) {
+        int rc = hd_weight_download(ctx, w, bytes.data() + off, w->gguf_bytes);
+        if (rc) return rc;
+        off += w->gguf_bytes;
+    }
+    const int64_t rows = l.wq->rows + l.wk->rows + l.wv->rows;
+    int rc = hd_weight_upload(ctx, bytes.data(), total, l.wq->type, rows, l.wq->cols, &D.wqkv);
+    if (rc) return rc;
+    std::vector<float> b((size_t)rows);
+    memcpy(b.data(), l.bq, sizeof(float) * l.wq->rows);
+    memcpy(b.data() + l.wq->rows, l.bk, sizeof(float) * l.wk->rows);
+    memcpy(b.data() + l.wq->rows + l.wk->rows, l.bv, sizeof(float) * l.wv->rows);
+    return upload_vec(d, &D.bqkv, b.data(), (size_t)rows);
 }
 
 }  // namespace
@@ -235,6 +289,7 @@ extern "C" int hd_decoder_create(hd_ctx *ctx, const hd_decoder_config *cfg, cons
         if (!rc) rc = upload_vec(d, &D.bv, l.bv, nkv);
         if (!rc) rc = upload_vec(d, &D.attn_norm, l.attn_norm, c.hidden);
         if (!rc) rc = upload_vec(d, &D.ffn_norm, l.ffn_norm, c.hidden);
+        if (!rc && getenv("HACEDLE_DECODER_UNFUSED") == nullptr) rc = build_qkv(d, D, l);
     }
     if (!rc) rc = upload_vec(d, &d->out_norm, out_norm_host, c.hidden);
     size_t kvn = (size_t)c.n_layers * c.max_seqs * c.max_ctx * nkv;
@@ -281,6 +336,7 @@ extern "C" int hd_decoder_generate(hd_decoder *d, const int32_t *prompts, int S,
     int rc = dalloc(d, &d->h, (size_t)Rm * c.hidden);
     if (!rc) rc = dalloc(d, &d->xn, (size_t)Rm * c.hidden);
     if (!rc) rc = dalloc(d, &d->q, (size_t)Rm * nq);
+    if (!rc) rc = dalloc(d, &d->qkv, (size_t)Rm * (nq + 2 * nkv));
     if (!rc) rc = dalloc(d, &d->k, (size_t)Rm * nkv);
     if (!rc) rc = dalloc(d, &d->v, (size_t)Rm * nkv);
     if (!rc) rc = dalloc(d, &d->att, (size_t)Rm * nq);

@@ -105,9 +105,13 @@ bool hd_type_supported(int t);
 int hd_ensure_hbuf(hd_ctx *ctx, float **buf, size_t *have, size_t need);
 int hd_qgemm_f32(hd_ctx *ctx, const hd_weight *w, const float *X, float *Y, int T);
 // Attention over `rows` query rows (see k_attention in hd_attention.cu).
-int hd_attention_run(hd_ctx *ctx, const float *q, const float *kc, const float *vc, const int32_t *lens, int rows,
-                     int pos0, int seqT, int n_heads, int n_kv, int hd, int max_ctx, int maxlen, float *out,
+int hd_attention_run(hd_ctx *ctx, const float *q, int64_t qld, const float *kc, const float *vc, const int32_t *lens,
+                     int rows, int pos0, int seqT, int n_heads, int n_kv, int hd, int max_ctx, int maxlen, float *out,
                      const char *name);
+// Fused q|k|v rows (row stride ld): RoPE on q and k heads in place, rotated k
+// and v appended to cache sequence r / T at position pos[r].
+int hd_rope_kv_append(hd_ctx *ctx, float *qkv, int64_t ld, const int32_t *pos, int rows, int T, int n_heads, int n_kv,
+                      int hd, float *kc, float *vc, int max_ctx);
 
 // Launch with programmatic stream serialization, so the next kernel's
 // pre-dependency prologue (weight prefetch) overlaps this one's tail.
