@@ -150,12 +150,16 @@ int layer_forward(hd_decoder *d, int li, int rows, const int32_t *pos, const int
     const hd_decoder::Layer &l = d->L[li];
     const int hd = c.head_dim, nkv = c.n_kv * hd;
     const size_t lay = (size_t)li * c.max_seqs * c.max_ctx * nkv;
-    int rc = hd_rmsnorm(ctx, d->h, l.attn_norm, nullptr, d->xn, rows, c.hidden, c.eps);
+    // up to 16 rows the RMSNorm runs inside the projection that consumes it
+    const bool gemv = rows <= 16 && l.wqkv;
+    int rc = gemv ? HD_OK : hd_rmsnorm(ctx, d->h, l.attn_norm, nullptr, d->xn, rows, c.hidden, c.eps);
     if (l.wqkv) {
         // one q|k|v projection, RoPE + cache append in one kernel, attention
         // reading q from the fused rows
         const int64_t ld = l.wqkv->rows;
-        if (!rc) rc = linear(d, l.wqkv, d->xn, d->qkv, rows, l.bqkv, nullptr, prec);
+        if (!rc)
+            rc = gemv ? hd_qgemv_norm(ctx, l.wqkv, nullptr, d->h, l.attn_norm, c.eps, d->qkv, rows, l.bqkv, nullptr)
+                      : linear(d, l.wqkv, d->xn, d->qkv, rows, l.bqkv, nullptr, prec);
         if (!rc)
             rc = hd_rope_kv_append(ctx, d->qkv, ld, pos, rows, lens ? 1 : T, c.n_heads, c.n_kv, hd, d->kc + lay,
                                    d->vc + lay, c.max_ctx);
@@ -184,8 +188,12 @@ int layer_forward(hd_decoder *d, int li, int rows, const int32_t *pos, const int
         }
     }
     if (!rc) rc = linear(d, l.wo, d->att, d->h, rows, nullptr, d->h, prec);
-    if (!rc) rc = hd_rmsnorm(ctx, d->h, l.ffn_norm, nullptr, d->xn, rows, c.hidden, c.eps);
-    if (!rc) rc = ffn_gate_up(d, l, d->xn, d->a, rows, prec);
+    if (gemv) {
+        if (!rc) rc = hd_qgemv_norm(ctx, l.wg, l.wu, d->h, l.ffn_norm, c.eps, d->a, rows, nullptr, nullptr);
+    } else {
+        if (!rc) rc = hd_rmsnorm(ctx, d->h, l.ffn_norm, nullptr, d->xn, rows, c.hidden, c.eps);
+        if (!rc) rc = ffn_gate_up(d, l, d->xn, d->a, rows, prec);
+    }
     if (!rc) rc = linear(d, l.wd, d->a, d->h, rows, nullptr, d->h, prec);
     return rc;
 }
@@ -193,8 +201,13 @@ int layer_forward(hd_decoder *d, int li, int rows, const int32_t *pos, const int
 // Final norm, LM head and argmax for S rows of `hid`.
 int head(hd_decoder *d, const float *hid, int S, int prec) {
     hd_ctx *ctx = d->ctx;
-    int rc = hd_rmsnorm(ctx, hid, d->out_norm, nullptr, d->xn, S, d->c.hidden, d->c.eps);
-    if (!rc) rc = linear(d, d->embed, d->xn, d->logits, S, nullptr, nullptr, prec);
+    int rc;
+    if (S <= 16 && getenv("HACEDLE_DECODER_UNFUSED") == nullptr) {
+        rc = hd_qgemv_norm(ctx, d->embed, nullptr, hid, d->out_norm, d->c.eps, d->logits, S, nullptr, nullptr);
+    } else {
+        rc = hd_rmsnorm(ctx, hid, d->out_norm, nullptr, d->xn, S, d->c.hidden, d->c.eps);
+        if (!rc) rc = linear(d, d->embed, d->xn, d->logits, S, nullptr, nullptr, prec);
+    }
     if (!rc) rc = hd_argmax_rows(ctx, d->logits, S, d->c.vocab, d->amax);
     return rc;
 }

@@ -44,7 +44,43 @@ struct GemvArgs {
     int B, N, ldy, K;
     int RC, G;             // rows per CTA, unit groups per CTA
     int pair;              // 1: SwiGLU of (w0, w1)
+    const float *nw;       // [K] RMSNorm weight: x is normalized first (null: x as is)
+    float eps;
 };
+
+// RMSNorm scales of B rows of x [B][K] (1 / sqrt(mean(x^2) + eps)) into
+// rs[b], by the whole CTA in a fixed order: per-thread strided sums, warp
+// shuffles, warp partials added in warp order.  nred: NWARPS_MAX x NB floats.
+// The CTA is whole warps (the launchers round block sizes up to 32).
+template <int NB>
+__device__ __forceinline__ void norm_scales(const float *__restrict__ x, int K, int B, float eps, float *nred,
+                                            float *rs) {
+    float ss[NB];
+#pragma unroll
+    for (int b = 0; b < NB; b++) ss[b] = 0.f;
+    for (int k = threadIdx.x; k < K; k += blockDim.x) {
+#pragma unroll
+        for (int b = 0; b < NB; b++)
+            if (b < B) {
+                const float v = x[(int64_t)b * K + k];
+                ss[b] = fmaf(v, v, ss[b]);
+            }
+    }
+#pragma unroll
+    for (int b = 0; b < NB; b++)
+        for (int o = 16; o > 0; o >>= 1) ss[b] += __shfl_xor_sync(0xffffffffu, ss[b], o);
+    const int warp = threadIdx.x >> 5, nw = blockDim.x >> 5;
+    if ((threadIdx.x & 31) == 0)
+#pragma unroll
+        for (int b = 0; b < NB; b++) nred[warp * NB + b] = ss[b];
+    __syncthreads();
+    if ((int)threadIdx.x < B) {
+        float t = 0.f;
+        for (int w = 0; w < nw; w++) t += nred[w * NB + threadIdx.x];
+        rs[threadIdx.x] = 1.0f / sqrtf(t / (float)K + eps);
+    }
+    __syncthreads();
+}
 template <int TYPE>
 struct URegs;
 template <>
@@ -111,7 +147,7 @@ __device__ __forceinline__ float dot4(float a0, float a1, float a2, float a3, co
 }
 
 // acc[b] += unit(u) . x[b][unit]; xs points at this unit's 32 floats of batch
-// row 0, batch rows `xstride4` float4s apart.
+// row 0, batch row b at float4 offset xoff[b].
 // The float 2 + byte/64, exact for byte < 128: byte c of v goes to bits
 // 16..23 under the exponent byte 0x40 (one byte_perm, no subtraction).  The
 // constant 2 is removed per unit with the sum of x (see unit_fma).
@@ -120,7 +156,8 @@ __device__ __forceinline__ float f2q(uint32_t v, int c) {
 }
 
 // acc[b] += unit(u) . x[b][unit].  xs points at this unit's 32 floats of batch
-// row 0 (float4), batch rows `xstride4` float4s apart; xh holds the sums of
+// row 0 (float4), batch row b at float4 offset xoff[b] (padded rows read row
+// 0, so nothing past the B rows of x is touched); xh holds the sums of
 // x over the unit's two 16-value halves, batch rows `xh_stride` apart.
 //
 // Q5_0, Q4_K and Q6_K form S = sum_j f_j x_j with f_j = 2 + q_j/64, so
@@ -129,7 +166,7 @@ __device__ __forceinline__ float f2q(uint32_t v, int c) {
 // Q6_K  dl (64 S_lo - 160 X_lo) + dh (64 S_hi - 160 X_hi).  Q8_0 (signed
 // bytes) uses 2^23 + byte and one subtraction per value.
 template <int TYPE, int NB>
-__device__ __forceinline__ void unit_fma(const URegs<TYPE> &g, int u, const float4 *xs, int xstride4,
+__device__ __forceinline__ void unit_fma(const URegs<TYPE> &g, int u, const float4 *xs, const int (&xoff)[NB],
                                          const float *xh, int xh_stride, float (&acc)[NB]) {
     if constexpr (TYPE == HD_TYPE_Q8_0) {
         float s[NB];
@@ -141,7 +178,7 @@ __device__ __forceinline__ void unit_fma(const URegs<TYPE> &g, int u, const floa
             const float o = 8388736.0f;  // 2^23 + 128
             float f0 = mag(v, 0) - o, f1 = mag(v, 1) - o, f2 = mag(v, 2) - o, f3 = mag(v, 3) - o;
 #pragma unroll
-            for (int b = 0; b < NB; b++) s[b] = dot4(f0, f1, f2, f3, xs[b * xstride4 + wd], s[b]);
+            for (int b = 0; b < NB; b++) s[b] = dot4(f0, f1, f2, f3, xs[xoff[b] + wd], s[b]);
         }
         float d = h2f((uint16_t)g.d);
 #pragma unroll
@@ -159,8 +196,8 @@ __device__ __forceinline__ void unit_fma(const URegs<TYPE> &g, int u, const floa
             float h0 = f2q(hi, 0), h1 = f2q(hi, 1), h2 = f2q(hi, 2), h3 = f2q(hi, 3);
 #pragma unroll
             for (int b = 0; b < NB; b++) {
-                sl[b] = dot4(l0, l1, l2, l3, xs[b * xstride4 + wd], sl[b]);
-                sh[b] = dot4(h0, h1, h2, h3, xs[b * xstride4 + 4 + wd], sh[b]);
+                sl[b] = dot4(l0, l1, l2, l3, xs[xoff[b] + wd], sl[b]);
+                sh[b] = dot4(h0, h1, h2, h3, xs[xoff[b] + 4 + wd], sh[b]);
             }
         }
         int s0 = 2 * (u & 7);
@@ -192,8 +229,8 @@ __device__ __forceinline__ void unit_fma(const URegs<TYPE> &g, int u, const floa
             float h0 = f2q(hi, 0), h1 = f2q(hi, 1), h2 = f2q(hi, 2), h3 = f2q(hi, 3);
 #pragma unroll
             for (int b = 0; b < NB; b++) {
-                float t = dot4(l0, l1, l2, l3, xs[b * xstride4 + wd], s[b]);
-                s[b] = dot4(h0, h1, h2, h3, xs[b * xstride4 + 4 + wd], t);
+                float t = dot4(l0, l1, l2, l3, xs[xoff[b] + wd], s[b]);
+                s[b] = dot4(h0, h1, h2, h3, xs[xoff[b] + 4 + wd], t);
             }
         }
         if constexpr (TYPE == HD_TYPE_Q5_0) {
@@ -257,12 +294,27 @@ __global__ void __launch_bounds__(GemvShape<NB, P>::MAXT) k_qgemv(GemvArgs a) {
     float *xh = sm;
     float *red = sm + (TYPE == HD_TYPE_Q8_0 ? 0 : NB * nu * 2);   // [NT][P+1][NB]
     float *red2 = red + NT * (P + 1) * NB;                            // [RC*NB*(P+1)][nch]
+    // With a norm weight: x normalized into shared memory [B][K] first.
+    const float *xsrc = a.x;
+    if (a.nw) {
+        __shared__ float nred[32 * NB], rs[NB];
+        const int nch0 = (G + 15) / 16;
+        float *xsm = red2 + RC * NB * (P + 1) * (nch0 > 1 ? nch0 : 0);
+        xsm = (float *)(((uintptr_t)xsm + 15) & ~(uintptr_t)15);  // float4 reads
+        norm_scales<NB>(a.x, a.K, a.B, a.eps, nred, rs);
+        for (int i = t; i < a.B * a.K; i += NT) {
+            const int b = i / a.K, k = i - b * a.K;
+            xsm[i] = __fmul_rn(__fmul_rn(a.x[i], a.nw[k]), rs[b]);
+        }
+        __syncthreads();
+        xsrc = xsm;
+    }
     if constexpr (TYPE != HD_TYPE_Q8_0) {
         for (int i = t; i < NB * nu * 2; i += NT) {
             const int b = i / (nu * 2), ul = (i >> 1) % nu, hf = i & 1;
             float sx = 0.f;
             if (b < a.B) {
-                const float4 *p4 = (const float4 *)(a.x + (int64_t)b * a.K + (int64_t)(u0 + ul) * 32 + hf * 16);
+                const float4 *p4 = (const float4 *)(xsrc + (int64_t)b * a.K + (int64_t)(u0 + ul) * 32 + hf * 16);
 #pragma unroll
                 for (int j = 0; j < 4; j++) {
                     const float4 v = p4[j];
@@ -280,7 +332,9 @@ __global__ void __launch_bounds__(GemvShape<NB, P>::MAXT) k_qgemv(GemvArgs a) {
 #pragma unroll
         for (int b = 0; b < NB; b++) acc[p][b] = 0.f;
 
-    const int xs4 = a.K / 4;
+    int xoff[NB];
+#pragma unroll
+    for (int b = 0; b < NB; b++) xoff[b] = b < a.B ? b * (a.K / 4) : 0;
     for (int base = u0 + g; base < u1; base += UCT * G) {
         if (base != u0 + g) {
 #pragma unroll
@@ -297,10 +351,10 @@ __global__ void __launch_bounds__(GemvShape<NB, P>::MAXT) k_qgemv(GemvArgs a) {
         for (int c = 0; c < UCT; c++) {
             const int u = base + c * G;
             if (ok && u < u1) {
-                const float4 *xp = (const float4 *)(a.x + (int64_t)u * 32);
+                const float4 *xp = (const float4 *)(xsrc + (int64_t)u * 32);
 #pragma unroll
                 for (int p = 0; p <= P; p++)
-                    unit_fma<TYPE, NB>(cur[c][p], u, xp, xs4, xh + (u - u0) * 2, nu * 2, acc[p]);
+                    unit_fma<TYPE, NB>(cur[c][p], u, xp, xoff, xh + (u - u0) * 2, nu * 2, acc[p]);
             }
         }
     }
@@ -435,6 +489,7 @@ __global__ void __launch_bounds__(32 * NB, 1)
     const float *Rs = a.residual ? a.residual + (int64_t)grp * 16 * a.ldy : nullptr;
     int *tk = tickets + grp * ntiles;
     const int64_t cta = (int64_t)grp * gridDim.x + blockIdx.x;
+    __shared__ float nred[32 * NB], rs[NB];
     const int units = a.w0.units;
     const int nwu = ntiles * units, g0 = blockIdx.x * 8;
     // Flattened: warp w takes pair g0 + w (one unit).  Per tile (tall
@@ -462,6 +517,7 @@ __global__ void __launch_bounds__(32 * NB, 1)
 #pragma unroll
         for (int b = 0; b < 8; b++) acc[rr][b] = 0.f;
     const int bbase = 8 * bg, nbw = B - bbase < 8 ? B - bbase : 8;  // this warp's batch rows
+    if (a.nw) norm_scales<NB>(X, a.K, B, a.eps, nred, rs);
     // flattened: one pass (straight-line code); per tile: the warp's units
     for (int u = ufirst; u < units; u = per_tile ? u + ustep : units) {
         if (per_tile && u != ufirst) {
@@ -473,8 +529,16 @@ __global__ void __launch_bounds__(32 * NB, 1)
         }
         float4 *xs = (float4 *)sm + (warp * NB + bbase) * 8;
         __syncwarp();
-        for (int i = lane; i < nbw * 8; i += 32)
-            xs[i] = __ldg((const float4 *)(X + (int64_t)(bbase + (i >> 3)) * a.K + (int64_t)u * 32) + (i & 7));
+        for (int i = lane; i < nbw * 8; i += 32) {
+            float4 v = __ldg((const float4 *)(X + (int64_t)(bbase + (i >> 3)) * a.K + (int64_t)u * 32) + (i & 7));
+            if (a.nw) {  // RMSNorm on the fly: (x * w) * r
+                const float4 wn = __ldg((const float4 *)(a.nw + (int64_t)u * 32) + (i & 7));
+                const float r = rs[bbase + (i >> 3)];
+                v = make_float4(__fmul_rn(__fmul_rn(v.x, wn.x), r), __fmul_rn(__fmul_rn(v.y, wn.y), r),
+                                __fmul_rn(__fmul_rn(v.z, wn.z), r), __fmul_rn(__fmul_rn(v.w, wn.w), r));
+            }
+            xs[i] = v;
+        }
         __syncwarp();
         URowScale scl[4];
 #pragma unroll
@@ -641,7 +705,7 @@ Plan plan_gemv(int N, int units, int B, bool pair, int sms) {
     if (RC > N) RC = N;
     p.RC = RC;
     p.G = G;
-    p.nt = RC * G;
+    p.nt = (RC * G + 31) / 32 * 32;  // whole warps (threads past RC*G own no unit group)
     p.tiles = (N + RC - 1) / RC;
     const int P1 = pair ? 2 : 1, nch = (G + 15) / 16;
     p.smem = ((size_t)p.nb * units * 2 + (size_t)p.nt * P1 * p.nb + (size_t)RC * p.nb * P1 * (nch > 1 ? nch : 0)) *
@@ -714,7 +778,8 @@ int run_gemv_rb(hd_ctx *ctx, const GemvArgs &a, int type, const char *name) {
 }
 
 int run_gemv(hd_ctx *ctx, const hd_weight *w, const hd_weight *w_up, const float *x, float *y, int B,
-             const float *bias, const float *residual, const char *name) {
+             const float *bias, const float *residual, const char *name, const float *nw = nullptr,
+             float eps = 0.f) {
     if (!ctx || !w || !x || !y) return hd_fail(ctx, HD_E_ARG, "%s: null argument", name);
     HD_REQUIRE(ctx, B >= 1 && B <= 16, HD_E_ARG, "%s: batch %d outside 1..16", name, B);
     HD_REQUIRE(ctx, ((uintptr_t)x & 15) == 0, HD_E_ARG, "%s: x must be 16-byte aligned", name);
@@ -726,8 +791,8 @@ int run_gemv(hd_ctx *ctx, const hd_weight *w, const hd_weight *w_up, const float
         // pair would hold 2 x 16 accumulators per thread at this batch).
         size_t one = (size_t)B * w->rows;
         int rc = hd_ensure_hbuf(ctx, &ctx->scratch, &ctx->scratch_bytes, 2 * one * sizeof(float));
-        if (!rc) rc = run_gemv(ctx, w, nullptr, x, ctx->scratch, B, nullptr, nullptr, name);
-        if (!rc) rc = run_gemv(ctx, w_up, nullptr, x, ctx->scratch + one, B, nullptr, nullptr, name);
+        if (!rc) rc = run_gemv(ctx, w, nullptr, x, ctx->scratch, B, nullptr, nullptr, name, nw, eps);
+        if (!rc) rc = run_gemv(ctx, w_up, nullptr, x, ctx->scratch + one, B, nullptr, nullptr, name, nw, eps);
         if (!rc) rc = hd_swiglu(ctx, ctx->scratch, ctx->scratch + one, y, (int64_t)one);
         return rc;
     }
@@ -743,8 +808,11 @@ int run_gemv(hd_ctx *ctx, const hd_weight *w, const hd_weight *w_up, const float
     a.ldy = (int)w->rows;
     a.K = (int)w->cols;
     a.pair = w_up ? 1 : 0;
+    a.nw = nw;
+    a.eps = eps;
     if (!w_up && pad_batch(B) >= 8 && getenv("HACEDLE_GEMV_RB") == nullptr) return run_gemv_rb(ctx, a, w->type, name);
     Plan p = plan_gemv((int)w->rows, w->units, B, w_up != nullptr, ctx->sm_count);
+    if (nw) p.smem += (size_t)B * w->cols * sizeof(float) + 16;  // the normalized x, 16-byte aligned
     a.RC = p.RC;
     a.G = p.G;
     cudaError_t e = cudaSuccess;
@@ -807,5 +875,24 @@ int hd_qgemm_rows_f32(hd_ctx *ctx, const hd_weight *w, const float *X, float *Y,
     a.K = (int)w->cols;
     a.RC = a.G = 0;
     a.pair = 0;
+    a.nw = nullptr;
+    a.eps = 0.f;
     return run_gemv_rb(ctx, a, w->type, "hd_qgemm");
+}
+
+// y = W rmsnorm(x) (+bias, +residual) or SwiGLU(W_gate x', W_up x') for
+// B <= 16 rows: the RMSNorm ((x * w) * r, as hd_rmsnorm) is computed by each
+// CTA in its prologue instead of a separate kernel (the decoder's steps).
+int hd_qgemv_norm(hd_ctx *ctx, const hd_weight *w, const hd_weight *w_up, const float *x, const float *norm_w,
+                  float eps, float *y, int B, const float *bias, const float *residual) {
+    if (!norm_w) return hd_fail(ctx, HD_E_ARG, "hd_qgemv_rmsnorm: null norm weight");
+    if (w_up && (bias || residual))
+        return hd_fail(ctx, HD_E_ARG, "hd_qgemv_rmsnorm: the SwiGLU pair takes no bias or residual");
+    return run_gemv(ctx, w, w_up, x, y, B, bias, residual, "hd_qgemv_rmsnorm", norm_w, eps);
+}
+
+extern "C" int hd_qgemv_rmsnorm(hd_ctx *ctx, const hd_weight *w, const hd_weight *w_up, const float *x_dev,
+                                const float *norm_w_dev, float eps, float *y_dev, int B, const float *bias_dev,
+                                const float *residual_dev) {
+    return hd_qgemv_norm(ctx, w, w_up, x_dev, norm_w_dev, eps, y_dev, B, bias_dev, residual_dev);
 }

@@ -108,6 +108,10 @@ int hd_qgemm_f32(hd_ctx *ctx, const hd_weight *w, const float *X, float *Y, int 
 int hd_attention_run(hd_ctx *ctx, const float *q, int64_t qld, const float *kc, const float *vc, const int32_t *lens,
                      int rows, int pos0, int seqT, int n_heads, int n_kv, int hd, int max_ctx, int maxlen, float *out,
                      const char *name);
+// Q-GEMV (B <= 16) of rmsnorm(x) with the norm in each CTA's prologue;
+// w_up != null: SwiGLU pair.
+int hd_qgemv_norm(hd_ctx *ctx, const hd_weight *w, const hd_weight *w_up, const float *x, const float *norm_w,
+                  float eps, float *y, int B, const float *bias, const float *residual);
 // Fused q|k|v rows (row stride ld): RoPE on q and k heads in place, rotated k
 // and v appended to cache sequence r / T at position pos[r].
 int hd_rope_kv_append(hd_ctx *ctx, float *qkv, int64_t ld, const int32_t *pos, int rows, int T, int n_heads, int n_kv,

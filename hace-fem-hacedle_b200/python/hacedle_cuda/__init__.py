@@ -27,7 +27,7 @@ EXPORTS = [
     "hd_ctx_create", "hd_ctx_destroy", "hd_ctx_set_stream", "hd_ctx_synchronize", "hd_ctx_reserve_workspace",
     "hd_last_error", "hd_ctx_launch_count", "hd_version", "hd_ctx_check_device_errors",
     "hd_weight_upload", "hd_weight_upload_device", "hd_weight_free", "hd_weight_info", "hd_weight_download",
-    "hd_dequantize", "hd_qgemv", "hd_qgemv_swiglu", "hd_qgemv_host", "hd_qgemm", "hd_qgemm_host", "hd_matmul_f32",
+    "hd_dequantize", "hd_qgemv", "hd_qgemv_swiglu", "hd_qgemv_rmsnorm", "hd_qgemv_host", "hd_qgemm", "hd_qgemm_host", "hd_matmul_f32",
     "hd_rmsnorm", "hd_rmsnorm_graph", "hd_rope_neox", "hd_rope_interleaved", "hd_softmax_rows", "hd_swiglu",
     "hd_add", "hd_argmax_rows", "hd_argmax_rows_noalloc", "hd_embed", "hd_kv_append", "hd_attention_decode", "hd_attention_prefill",
     "hd_dot_i8", "hd_fused_qdot_qadd_qacc_i8", "hd_gather_columns", "hd_decoder_create", "hd_decoder_free", "hd_decoder_generate",
@@ -62,6 +62,7 @@ def lib() -> C.CDLL:
         "hd_weight_info": [V, C.POINTER(I), C.POINTER(I64), C.POINTER(I64), C.POINTER(SZ)],
         "hd_weight_download": [V, V, V, SZ], "hd_dequantize": [V, V, V, SZ],
         "hd_qgemv": [V, V, V, V, I, V, V], "hd_qgemv_swiglu": [V, V, V, V, V, I], "hd_qgemv_host": [V, V, V, V, I],
+        "hd_qgemv_rmsnorm": [V, V, V, V, V, F, V, I, V, V],
         "hd_qgemm": [V, V, V, V, I, I], "hd_qgemm_host": [V, V, V, V, I, I], "hd_matmul_f32": [V, V, V, V, I64, I64, I64],
         "hd_rmsnorm": [V, V, V, V, V, I64, I, F], "hd_rmsnorm_graph": [V, V, V, V, I64, I, F],
         "hd_rope_neox": [V, V, V, I, I, I, F], "hd_rope_interleaved": [V, V, V, V, V, I64, I],
@@ -111,9 +112,10 @@ class Weight:
         return out
 
     def free(self):
-        if self.h:
+        # after the context is closed its device memory is gone with it
+        if self.h and getattr(self.ctx, "h", None):
             lib().hd_weight_free(self.ctx.h, self.h)
-            self.h = None
+        self.h = None
 
     def __del__(self):
         try:
@@ -177,6 +179,12 @@ class Context:
     def qgemv_swiglu(self, wg: Weight, wu: Weight, x, y):
         B = x.shape[0] if x.dim() == 2 else 1
         self._check(lib().hd_qgemv_swiglu(self.h, wg.h, wu.h, _ptr(x), _ptr(y), B))
+
+    def qgemv_norm(self, w: Weight, x, norm_w, y, eps: float = 1e-6, w_up: Weight | None = None, bias=None,
+                   residual=None):
+        B = x.shape[0] if x.dim() == 2 else 1
+        self._check(lib().hd_qgemv_rmsnorm(self.h, w.h, w_up.h if w_up else None, _ptr(x), _ptr(norm_w), eps,
+                                           _ptr(y), B, _ptr(bias), _ptr(residual)))
 
     def qgemv_host(self, w: Weight, x: np.ndarray) -> np.ndarray:
         x = np.ascontiguousarray(x, np.float32).reshape(-1, w.cols)
@@ -320,9 +328,9 @@ class Decoder:
         return out, dm.value, pm.value
 
     def free(self):
-        if getattr(self, "h", None):
+        if getattr(self, "h", None) and getattr(self.ctx, "h", None):
             lib().hd_decoder_free(self.h)
-            self.h = None
+        self.h = None
         for w in self.weights:
             w.free()
         self.weights = []

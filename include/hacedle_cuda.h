@@ -113,6 +113,15 @@ int hd_qgemv(hd_ctx *ctx, const hd_weight *w, const float *x_dev, float *y_dev, 
  * (src/ops/silu.rs:5-13 applied as Qwen2's silu(gate)*up). */
 int hd_qgemv_swiglu(hd_ctx *ctx, const hd_weight *w_gate, const hd_weight *w_up,
                     const float *x_dev, float *y_dev, int B);
+/* RMSNorm fused into the projection that consumes it: y = W rmsnorm(x)
+ * (+bias, +residual), or with w_up != NULL the SwiGLU pair of rmsnorm(x).
+ * Replaces the pair rms_norm (core/tensor_ops/rms_norm.rs:4-13, the block's
+ * attn/ffn norms at core/ops/block.rs:96-103, 203-209) + matmul_vec_matrix;
+ * the norm is (x * norm_w) * r with r = 1/sqrt(mean(x^2) + eps), as
+ * hd_rmsnorm.  norm_w_dev [cols]; B <= 16; other arguments as hd_qgemv. */
+int hd_qgemv_rmsnorm(hd_ctx *ctx, const hd_weight *w, const hd_weight *w_up, const float *x_dev,
+                     const float *norm_w_dev, float eps, float *y_dev, int B, const float *bias_dev,
+                     const float *residual_dev);
 /* The reference operator with host slices in and out (matmul_vec_matrix's
  * &[f32] -> Vec<f32> contract): copies x in, runs hd_qgemv, copies y out. */
 int hd_qgemv_host(hd_ctx *ctx, const hd_weight *w, const float *x_host, float *y_host, int B);

@@ -206,3 +206,40 @@ def test_gemv_batched_register_blocked(ctx, t, N, K, B, bias, residual):
     ctx.qgemv(w, x, y2)
     torch.cuda.synchronize()
     assert torch.equal(y1, y2)
+
+
+@pytest.mark.parametrize("t,N,K,B", [(S.GGML_Q5_0, 1152, 896, 1), (S.GGML_Q5_0, 896, 896, 3), (S.GGML_Q8_0, 896, 896, 4),
+                                     (S.GGML_Q6_K, 512, 768, 9), (S.GGML_Q4_K, 384, 512, 16)])
+def test_gemv_fused_rmsnorm(ctx, t, N, K, B):
+    """hd_qgemv_rmsnorm (the norm in each CTA's prologue) against the oracle's
+    RMSNorm followed by its GEMV, with bias and in-place residual."""
+    torch = _torch()
+    raw = S.gen_weight(t, N, K, 400 + B)
+    X = S.gen_activations(B, K, 401)
+    nw = (1.0 + 0.02 * S.rng(402).standard_normal(K)).astype(np.float32)
+    bh = (0.02 * S.rng(403).standard_normal(N)).astype(np.float32)
+    rh = S.rng(404).standard_normal((B, N), dtype=np.float32)
+    xn = O.rmsnorm(X, nw, 1e-6).reshape(B, K)
+    ref = rh + (O.qgemv(t, raw, N, K, xn, threads=8) + bh[None, :])
+    w = ctx.weight(t, raw, N, K)
+    y = torch.from_numpy(rh.copy()).cuda()
+    ctx.qgemv_norm(w, torch.from_numpy(X).cuda(), torch.from_numpy(nw).cuda(), y, bias=torch.from_numpy(bh).cuda(),
+                   residual=y)
+    torch.cuda.synchronize()
+    assert _rel_err(y.cpu().numpy(), ref) <= REL_TOL
+
+
+@pytest.mark.parametrize("B", [1, 4, 12])
+def test_gemv_fused_rmsnorm_swiglu_pair(ctx, B):
+    torch = _torch()
+    N, K = 4864, 896
+    rg, ru = S.gen_weight(S.GGML_Q5_0, N, K, 410), S.gen_weight(S.GGML_Q5_0, N, K, 411)
+    X = S.gen_activations(B, K, 412)
+    nw = (1.0 + 0.02 * S.rng(413).standard_normal(K)).astype(np.float32)
+    xn = O.rmsnorm(X, nw, 1e-6).reshape(B, K)
+    ref = O.swiglu(O.qgemv(S.GGML_Q5_0, rg, N, K, xn, threads=8), O.qgemv(S.GGML_Q5_0, ru, N, K, xn, threads=8))
+    wg, wu = ctx.weight(S.GGML_Q5_0, rg, N, K), ctx.weight(S.GGML_Q5_0, ru, N, K)
+    y = torch.empty(B, N, device="cuda")
+    ctx.qgemv_norm(wg, torch.from_numpy(X).cuda(), torch.from_numpy(nw).cuda(), y, w_up=wu)
+    torch.cuda.synchronize()
+    assert _rel_err(y.cpu().numpy(), ref.reshape(B, N)) <= 2 * REL_TOL

@@ -126,3 +126,24 @@ def test_qgemm_fp32_row_groups(ctx, t, N, K, T):
     ctx.qgemm(w, Xd, Y2, precision=0)
     torch.cuda.synchronize()
     assert torch.equal(Y, Y2)
+
+
+@pytest.mark.parametrize("t,N,K", [(S.GGML_Q5_0, 256, 896), (S.GGML_Q4_K, 128, 1024), (S.GGML_Q6_K, 384, 512),
+                                   (S.GGML_Q8_0, 128, 256)])
+def test_qgemm_fp32_tensor_core_row_scaling(ctx, t, N, K):
+    """fp32 precision on the tensor cores splits x and the weights into fp16
+    halves after power-of-two scaling per activation row: rows whose
+    magnitudes differ by 10 orders each keep 1e-5 of their own maximum."""
+    import torch
+    T = 48
+    raw = S.gen_weight(t, N, K, 130 + t)
+    X = S.gen_activations(T, K, 131)
+    X *= np.float32(10.0) ** np.linspace(-6, 4, T, dtype=np.float32)[:, None]
+    w = ctx.weight(t, raw, N, K)
+    Y = torch.empty(T, N, device="cuda")
+    ctx.qgemm(w, torch.from_numpy(X).cuda(), Y, precision=0)
+    ctx.check_device_errors()
+    ref = O.qgemv(t, raw, N, K, X, threads=8)
+    got = Y.cpu().numpy()
+    err = np.abs(got - ref).max(axis=1) / np.abs(ref).max(axis=1)
+    assert err.max() <= 1e-5, err.max()
