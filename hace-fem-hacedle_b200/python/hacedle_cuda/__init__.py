@@ -186,11 +186,16 @@ class Context:
         self._check(lib().hd_qgemv_rmsnorm(self.h, w.h, w_up.h if w_up else None, _ptr(x), _ptr(norm_w), eps,
                                            _ptr(y), B, _ptr(bias), _ptr(residual)))
 
-    def qgemv_host(self, w: Weight, x: np.ndarray) -> np.ndarray:
+    def qgemv_host(self, w: Weight, x: np.ndarray, out: np.ndarray | None = None) -> np.ndarray:
+        """Host x [B][cols] -> host y [B][rows]; `out` (float32, C-contiguous,
+        e.g. a pinned buffer) receives y when given."""
         x = np.ascontiguousarray(x, np.float32).reshape(-1, w.cols)
-        y = np.zeros((x.shape[0], w.rows), np.float32)
-        self._check(lib().hd_qgemv_host(self.h, w.h, x.ctypes.data, y.ctypes.data, x.shape[0]))
-        return y
+        if out is None:
+            out = np.zeros((x.shape[0], w.rows), np.float32)
+        elif out.dtype != np.float32 or not out.flags.c_contiguous or out.size != x.shape[0] * w.rows:
+            raise ValueError("out must be a C-contiguous float32 array of B x rows")
+        self._check(lib().hd_qgemv_host(self.h, w.h, x.ctypes.data, out.ctypes.data, x.shape[0]))
+        return out
 
     def qgemm(self, w: Weight, X, Y, precision: int = PREC_FP32):
         self._check(lib().hd_qgemm(self.h, w.h, _ptr(X), _ptr(Y), X.shape[0], precision))
