@@ -6,6 +6,7 @@
 #include "hd_internal.cuh"
 
 int hd_qgemm_tc(hd_ctx *ctx, const hd_weight *w, const float *X, float *Y, int T, int exact);
+int hd_tc4_min_t();
 int hd_qgemm_rows_f32(hd_ctx *ctx, const hd_weight *w, const float *X, float *Y, int T);
 int hd_ensure_hbuf(hd_ctx *ctx, float **buf, size_t *have, size_t need);
 
@@ -145,13 +146,16 @@ extern "C" int hd_qgemm(hd_ctx *ctx, const hd_weight *w, const float *X, float *
                "hd_qgemm: X and Y must be 16-byte aligned");
     if (T == 0) return HD_OK;
     if (precision == HD_PREC_FP32) {
-        // rows % 128 == 0 and more than 16 rows: the exact-product
-        // tensor-core mode (exact weights and x as fp16 hi + lo, 3 MMAs per
-        // product, fp32 accumulation).  Otherwise: up to 1024 rows, groups of
+        // More than 16 rows and a weight the exact-product tensor-core mode
+        // takes (rows % 128 == 0 for the streamed kernel, any rows for the
+        // two-pass kernel): exact weights and x as fp16 hi + lo, 3 MMAs per
+        // product, fp32 accumulation.  Otherwise: up to 1024 rows, groups of
         // 16 rows on the batch Q-GEMV kernel; beyond, the 128 x 64 tiled
         // kernel.  HACEDLE_FP32_CUDA_CORES=1 keeps fp32 products on the CUDA
         // cores.
-        if (w->rows % 128 == 0 && T > 16 && getenv("HACEDLE_FP32_CUDA_CORES") == nullptr)
+        const int min_t = hd_tc4_min_t();
+        if (T > 16 && (w->rows % 128 == 0 || (min_t > 0 && T >= min_t)) &&
+            getenv("HACEDLE_FP32_CUDA_CORES") == nullptr)
             return hd_qgemm_tc(ctx, w, X, Y, T, 1);
         const char *lim = getenv("HACEDLE_ROWS_GEMV_MAX");
         const int maxrows = lim ? atoi(lim) : 1024;

@@ -914,14 +914,11 @@ __global__ void __launch_bounds__(TC3_THREADS, 1)
 }
 
 // Exact-product mode: row t of x times 2^rowshift[t] (largest magnitude near
-// 2^14), split into fp16 halves hi + lo (|x - hi - lo| <= 2^-22 |x|).  One
-// CTA per row; K % 8 == 0.
-__global__ void k_to_f16_split(const float *__restrict__ x, int K, __half *__restrict__ hi, __half *__restrict__ lo,
-                               int *__restrict__ rowshift) {
-    __shared__ float red[32];
-    pdl_wait();
-    pdl_trigger();
-    const int64_t t = blockIdx.x;
+// 2^14), split into fp16 halves hi + lo (|x - hi - lo| <= 2^-22 |x|), by the
+// whole CTA; K % 8 == 0.
+__device__ __forceinline__ void f16_split_row(const float *__restrict__ x, int K, __half *__restrict__ hi,
+                                              __half *__restrict__ lo, int *__restrict__ rowshift, int64_t t,
+                                              float *red) {
     const float4 *xr = (const float4 *)(x + t * K);
     float m = 0.f;
     for (int k = threadIdx.x; k < K / 4; k += blockDim.x) {
@@ -956,6 +953,15 @@ __global__ void k_to_f16_split(const float *__restrict__ x, int K, __half *__res
     if (threadIdx.x == 0) rowshift[t] = sh;
 }
 
+// One CTA per row.
+__global__ void k_to_f16_split(const float *__restrict__ x, int K, __half *__restrict__ hi, __half *__restrict__ lo,
+                               int *__restrict__ rowshift) {
+    __shared__ float red[32];
+    pdl_wait();
+    pdl_trigger();
+    f16_split_row(x, K, hi, lo, rowshift, blockIdx.x, red);
+}
+
 __global__ void k_to_bf16(const float *__restrict__ x, __nv_bfloat16 *__restrict__ y, int64_t n) {
     pdl_wait();
     pdl_trigger();
@@ -987,6 +993,392 @@ EncodeTiledFn encode_tiled() {
     return fn;
 }
 
+// ------------------------------------------------------------------- v4
+// Two passes, for prompts long enough that one dequantization of the weight
+// is cheap next to the products (the weight is re-read by every token tile):
+//   k_prep writes the weight once as 16-bit rows [N][K] (bf16, or in the
+//     exact-product mode fp16 hi and lo planes of 2^wshift * w), into a
+//     workspace that stays in L2 for the layer sizes of a 0.5B-7B model, and
+//     in the same launch converts the activations as for v3;
+//   k_gemm_tc4 is then a persistent tcgen05 GEMM whose operands both arrive by
+//     TMA (SWIZZLE_128B K-major) into a ring of STG stages of 128 weight rows
+//     and BT tokens x 64 K values each.
+// Without dequantizer warps on the critical path a K-step costs what its
+// shared-memory traffic costs (each stage is written once by TMA and read
+// once by the MMA), against 2*BT cycles of MMA.  BT (a multiple of 16, at most
+// 256) is a runtime argument, chosen by the host against wave quantization.
+// Warps: 0-3 TMA producers (warp j issues the steps g with g % 4 == j, since
+// one warp's bulk copies are processed one after another; with fewer than 4
+// stages, as many warps as stages), 4 TMEM + MMA,
+// 5-8 epilogue (as in v3: straight from TMEM registers to Y, 128 contiguous
+// bytes per store instruction).  Any row count: rows past N arrive as zeros
+// from the TMA and are not stored.
+
+// Both operand preparations in one launch (256 threads per CTA).  CTAs
+// [0, nw) dequantize blocks of 32 weight rows x 8 units: thread (row r, unit
+// u) makes one coalesced load of its unit from the unit-major layout (a warp
+// reads 32 consecutive rows), decodes 32 values and stages the 16-bit values
+// in shared memory, after which every warp store writes 512 contiguous bytes
+// of one row.  The exact mode stores fp16 hi and lo planes of 2^wshift * w
+// from the exact (oracle-order) dequantization.  The remaining CTAs convert
+// the activations: bf16, 8 values per thread; exact mode, one CTA per row
+// (f16_split_row).
+constexpr int PREP_RS = 32 * 16 + 16;  // staged row stride in bytes (conflict-free)
+
+template <int TYPE, int EX>
+__global__ void __launch_bounds__(256) k_prep(WView w, uint16_t *__restrict__ whi, uint16_t *__restrict__ wlo,
+                                              int wshift, int nrb, int nw, const float *__restrict__ X, int T,
+                                              uint16_t *__restrict__ xhi, uint16_t *__restrict__ xlo,
+                                              int *__restrict__ rowshift) {
+    __shared__ __align__(16) uint8_t tile[EX ? 2 : 1][32 * PREP_RS];
+    __shared__ float red[32];
+    pdl_wait();
+    pdl_trigger();
+    const int64_t K = (int64_t)w.units * 32;
+    if ((int)blockIdx.x < nw) {
+        const int rb = blockIdx.x % nrb, ub = blockIdx.x / nrb;
+        const int r = threadIdx.x & 31, wp = threadIdx.x >> 5;
+        const int64_t row = (int64_t)rb * 32 + r;
+        const int u = ub * 8 + wp;
+        if (row < w.rows && u < w.units) {
+            float v[32];
+            if constexpr (EX) decode_unit_exact<TYPE>(w, row, u, v);
+            else unit_values<TYPE>(w, row, u, true, v);
+            uint8_t *dh = tile[0] + r * PREP_RS + wp * 64;
+            if constexpr (EX) {
+                uint8_t *dl = tile[EX ? 1 : 0] + r * PREP_RS + wp * 64;
+                const float sc = __int_as_float((127 + wshift) << 23);  // 2^wshift, |wshift| <= 60
+#pragma unroll
+                for (int c = 0; c < 4; c++) {
+                    uint32_t h[4], l[4];
+#pragma unroll
+                    for (int j = 0; j < 4; j++) {
+                        const float a = v[8 * c + 2 * j] * sc, b = v[8 * c + 2 * j + 1] * sc;
+                        const __half2 hh = __floats2half2_rn(a, b);
+                        const __half2 ll = __floats2half2_rn(a - __low2float(hh), b - __high2float(hh));
+                        h[j] = *reinterpret_cast<const uint32_t *>(&hh);
+                        l[j] = *reinterpret_cast<const uint32_t *>(&ll);
+                    }
+                    *(uint4 *)(dh + 16 * c) = make_uint4(h[0], h[1], h[2], h[3]);
+                    *(uint4 *)(dl + 16 * c) = make_uint4(l[0], l[1], l[2], l[3]);
+                }
+            } else {
+#pragma unroll
+                for (int c = 0; c < 4; c++)
+                    *(uint4 *)(dh + 16 * c) =
+                        make_uint4(pack_bf16(v[8 * c], v[8 * c + 1]), pack_bf16(v[8 * c + 2], v[8 * c + 3]),
+                                   pack_bf16(v[8 * c + 4], v[8 * c + 5]), pack_bf16(v[8 * c + 6], v[8 * c + 7]));
+            }
+        }
+        __syncthreads();
+        // lane l writes bytes 16l.. of the block's 512-byte row segment
+        const int l = threadIdx.x & 31;
+        if (ub * 8 + (l >> 2) < w.units) {
+            for (int rr = wp; rr < 32; rr += 8) {
+                const int64_t grow = (int64_t)rb * 32 + rr;
+                if (grow >= w.rows) break;
+                const int64_t o = (grow * K + (int64_t)ub * 256) * 2 + 16 * l;
+                *(uint4 *)((uint8_t *)whi + o) = *(const uint4 *)(tile[0] + rr * PREP_RS + 16 * l);
+                if constexpr (EX) *(uint4 *)((uint8_t *)wlo + o) = *(const uint4 *)(tile[EX ? 1 : 0] + rr * PREP_RS + 16 * l);
+            }
+        }
+        return;
+    }
+    const int xb = blockIdx.x - nw;
+    if constexpr (EX) {
+        f16_split_row(X, (int)K, (__half *)xhi, (__half *)xlo, rowshift, xb, red);
+    } else {
+        const int64_t i = ((int64_t)xb * 256 + threadIdx.x) * 8;
+        if (i < (int64_t)T * K) {
+            const float4 a = *(const float4 *)(X + i), b = *(const float4 *)(X + i + 4);
+            *(uint4 *)(xhi + i) = make_uint4(pack_bf16(a.x, a.y), pack_bf16(a.z, a.w), pack_bf16(b.x, b.y),
+                                             pack_bf16(b.z, b.w));
+        }
+    }
+}
+
+constexpr int TC4_PW = 4;                       // TMA producer warps
+constexpr int TC4_MMA = TC4_PW, TC4_EPI = TC4_PW + 1;
+constexpr int TC4_THREADS = (TC4_EPI + 4) * 32;
+constexpr int TC4_MAX_STG = 10;
+constexpr int TC4_SMEM_MAX = 227 * 1024;
+constexpr int TC4_ECH = 16;                              // token columns per output chunk
+constexpr int TC4_EPI_BYTES = 2 * TC4_ECH * 128 * 4;     // two fp32 chunks [16 tokens][128 rows]
+
+// Shared memory: STG stages [A hi 16 KB][A lo 16 KB, EX][B hi BT*128][B lo
+// BT*128, EX], then the two output chunks of the epilogue.
+__host__ __device__ inline int tc4_stage_bytes(int bt, int ex) { return (ex ? 2 : 1) * (128 + bt) * BK * 2; }
+__host__ __device__ inline int tc4_stages(int bt, int ex) {
+    const int n = (TC4_SMEM_MAX - 2048 - TC4_EPI_BYTES) / tc4_stage_bytes(bt, ex);
+    return n > TC4_MAX_STG ? TC4_MAX_STG : n;
+}
+
+// Bounded wait by a whole warp, with a warp-uniform result.
+__device__ __forceinline__ bool mbar_wait_warp(uint32_t bar, uint32_t parity, int *flag, unsigned sleep_ns = 0) {
+    return __all_sync(0xffffffffu, mbar_wait(bar, parity, flag, sleep_ns));
+}
+
+// The 128 epilogue threads: named barrier 1, and a vote that makes a flag
+// uniform over them (so that all take the same barriers).
+__device__ __forceinline__ void epi_sync() { asm volatile("bar.sync 1, 128;" ::: "memory"); }
+__device__ __forceinline__ bool epi_all(bool v) {
+    uint32_t r;
+    asm volatile(
+        "{\n .reg .pred p, q;\n setp.ne.u32 p, %1, 0;\n bar.red.and.pred q, 1, 128, p;\n selp.u32 %0, 1, 0, q;\n}\n"
+        : "=r"(r)
+        : "r"((uint32_t)v)
+        : "memory");
+    return r != 0;
+}
+__device__ __forceinline__ void tma_store_2d(const CUtensorMap *tm, uint32_t src, int x, int y) {
+    asm volatile("cp.async.bulk.tensor.2d.global.shared::cta.bulk_group [%0, {%2, %3}], [%1];" ::"l"((uint64_t)tm),
+                 "r"(src), "r"(x), "r"(y)
+                 : "memory");
+}
+__device__ __forceinline__ void bulk_commit() { asm volatile("cp.async.bulk.commit_group;" ::: "memory"); }
+__device__ __forceinline__ void bulk_wait_read1() { asm volatile("cp.async.bulk.wait_group.read 1;" ::: "memory"); }
+__device__ __forceinline__ void bulk_wait_all() { asm volatile("cp.async.bulk.wait_group 0;" ::: "memory"); }
+
+template <int EX>
+__global__ void __launch_bounds__(TC4_THREADS, 1)
+    k_gemm_tc4(const __grid_constant__ CUtensorMap tmw, const __grid_constant__ CUtensorMap tmw_lo,
+               const __grid_constant__ CUtensorMap tmx, const __grid_constant__ CUtensorMap tmx_lo,
+               const __grid_constant__ CUtensorMap tmy, float *__restrict__ Y, int T, int N, int BT, int ntm,
+               int ntiles, int ksteps, int wshift, const int *__restrict__ rowshift, int ytma, int *flag) {
+    extern __shared__ uint8_t smem_raw[];
+    __shared__ __align__(8) uint64_t full[TC4_MAX_STG], empty[TC4_MAX_STG];
+    __shared__ __align__(8) uint64_t acc_full[2], acc_empty[2], fin_bar;
+    __shared__ uint32_t tmem_base_sh;
+
+    const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+    const int SB = tc4_stage_bytes(BT, EX), STG = tc4_stages(BT, EX);
+    const int AB = 128 * BK * 2, BB = BT * BK * 2;
+    const int A_LO = AB, B_HI = (EX ? 2 : 1) * AB, B_LO = B_HI + BB;
+    uint8_t *base = (uint8_t *)(((uintptr_t)smem_raw + 1023) & ~(uintptr_t)1023);
+
+    if (threadIdx.x == 0) {
+        for (int s = 0; s < STG; s++) {
+            mbar_init(smem_u32(&full[s]), 1);
+            mbar_init(smem_u32(&empty[s]), 1);
+        }
+        for (int i = 0; i < 2; i++) {
+            mbar_init(smem_u32(&acc_full[i]), 1);
+            mbar_init(smem_u32(&acc_empty[i]), 128);
+        }
+        mbar_init(smem_u32(&fin_bar), 1);
+        asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
+        asm volatile("prefetch.tensormap [%0];" ::"l"((uint64_t)&tmw) : "memory");
+        asm volatile("prefetch.tensormap [%0];" ::"l"((uint64_t)&tmx) : "memory");
+        if (ytma) asm volatile("prefetch.tensormap [%0];" ::"l"((uint64_t)&tmy) : "memory");
+        if (EX) {
+            asm volatile("prefetch.tensormap [%0];" ::"l"((uint64_t)&tmw_lo) : "memory");
+            asm volatile("prefetch.tensormap [%0];" ::"l"((uint64_t)&tmx_lo) : "memory");
+        }
+    }
+    if (warp == TC4_MMA) {
+        asm volatile("tcgen05.alloc.cta_group::1.sync.aligned.shared::cta.b32 [%0], %1;" ::"r"(smem_u32(&tmem_base_sh)),
+                     "r"(512));
+        asm volatile("tcgen05.relinquish_alloc_permit.cta_group::1.sync.aligned;");
+    }
+    tc_fence_before();
+    __syncthreads();
+    tc_fence_after();
+    const uint32_t tmem = tmem_base_sh;
+    pdl_wait();
+    pdl_trigger();
+
+    // The producer and MMA loops run on whole warps (one lane issues), so that
+    // no lane waits at a reconvergence point while another spins.
+    if (warp < TC4_PW) {
+        // ---- TMA producers: warp j < npw issues the steps g with g % npw == j.
+        // npw <= STG keeps every parity wait on empty[s] at most one phase
+        // ahead: before its step g a warp has seen step g - npw - STG consumed
+        // (its previous wait), so the phase of step g - 2 STG is complete.
+        const int npw = STG < TC4_PW ? STG : TC4_PW;
+        if (warp < npw) {
+            int g = 0, s = 0, turn = 0, last[TC4_MAX_STG];
+            uint32_t ph = 0;  // phase parity of stage s at step g
+            for (int i = 0; i < STG; i++) last[i] = -1;
+            bool alive = true;
+            for (int item = blockIdx.x; item < ntiles && alive; item += gridDim.x) {
+                const int row0 = (item % ntm) * 128, t0 = (item / ntm) * BT;
+                for (int ks = 0; ks < ksteps; ks++) {
+                    if (turn == warp) {
+                        if (!mbar_wait_warp(smem_u32(&empty[s]), ph ^ 1, flag, 64)) { alive = false; break; }
+                        if (lane == 0) {
+                            const uint32_t bar = smem_u32(&full[s]), st = smem_u32(base + s * SB);
+                            mbar_expect_tx(bar, SB);
+                            tma_2d(st, &tmw, ks * BK, row0, bar);
+                            tma_2d(st + B_HI, &tmx, ks * BK, t0, bar);
+                            if (EX) {
+                                tma_2d(st + A_LO, &tmw_lo, ks * BK, row0, bar);
+                                tma_2d(st + B_LO, &tmx_lo, ks * BK, t0, bar);
+                            }
+                        }
+                        __syncwarp();
+                        last[s] = g;
+                    }
+                    g++;
+                    if (++s == STG) { s = 0; ph ^= 1; }
+                    if (++turn == npw) turn = 0;
+                }
+            }
+            // On an early exit, this warp's copies still in flight land before
+            // the CTA does (on a normal exit the MMA has consumed them all).
+            if (!alive)
+                for (int i = 0; i < STG; i++)
+                    if (last[i] >= 0) mbar_wait_quiet(smem_u32(&full[i]), (last[i] / STG) & 1);
+        }
+    } else if (warp == TC4_MMA) {
+        // ---- MMA issuer
+        const uint32_t idesc = EX ? idesc_f16(BT) : idesc_bf16(BT);
+        int s = 0, li = 0;
+        uint32_t ph = 0;
+        bool alive = true;
+        for (int item = blockIdx.x; item < ntiles && alive; item += gridDim.x, li++) {
+            const int buf = li & 1;
+            if (!mbar_wait_warp(smem_u32(&acc_empty[buf]), ((li >> 1) & 1) ^ 1, flag)) break;
+            tc_fence_after();
+            const uint32_t d = tmem + (uint32_t)(buf * BT);
+            // With four or more stages, two K-steps per round: their waits,
+            // MMAs and commits back to back, so that the fixed per-round cost
+            // of the issuing thread (barrier waits, commits) is paid once per
+            // 8 MMAs.  The MMAs read shared memory that TMA wrote; the
+            // mbarrier completion orders those writes, no tcgen05 fence is
+            // needed here.
+            for (int ks = 0; ks < ksteps;) {
+                const bool two = STG >= 4 && ks + 1 < ksteps;
+                const int s1 = s + 1 == STG ? 0 : s + 1;
+                const uint32_t ph1 = s + 1 == STG ? ph ^ 1 : ph;
+                bool ok = mbar_wait(smem_u32(&full[s]), ph, flag);
+                if (two) ok = ok && mbar_wait(smem_u32(&full[s1]), ph1, flag);
+                if (!__all_sync(0xffffffffu, ok)) { alive = false; break; }
+                if (lane == 0) {
+#pragma unroll
+                    for (int h = 0; h < 2; h++) {
+                        if (h == 1 && !two) break;
+                        const uint32_t a0 = smem_u32(base + (h ? s1 : s) * SB), b0 = a0 + B_HI;
+#pragma unroll
+                        for (int kk = 0; kk < BK / 16; kk++) {
+                            const uint64_t ad = sw128_desc(a0 + kk * 32), bd = sw128_desc(b0 + kk * 32);
+                            const uint32_t acc = (ks > 0 || h > 0 || kk > 0) ? 1u : 0u;
+                            asm volatile(
+                                "{\n .reg .pred p;\n setp.ne.b32 p, %4, 0;\n"
+                                " tcgen05.mma.cta_group::1.kind::f16 [%0], %1, %2, %3, p;\n}\n" ::"r"(d),
+                                "l"(ad), "l"(bd), "r"(idesc), "r"(acc));
+                            if (EX) {
+                                // + w_hi x_lo + w_lo x_hi (w_lo x_lo is below 2^-22)
+                                const uint64_t bdl = sw128_desc(a0 + B_LO + kk * 32);
+                                const uint64_t adl = sw128_desc(a0 + A_LO + kk * 32);
+                                asm volatile("tcgen05.mma.cta_group::1.kind::f16 [%0], %1, %2, %3, 1;" ::"r"(d),
+                                             "l"(ad), "l"(bdl), "r"(idesc));
+                                asm volatile("tcgen05.mma.cta_group::1.kind::f16 [%0], %1, %2, %3, 1;" ::"r"(d),
+                                             "l"(adl), "l"(bd), "r"(idesc));
+                            }
+                        }
+                    }
+                    asm volatile("tcgen05.commit.cta_group::1.mbarrier::arrive::one.shared::cluster.b64 [%0];" ::"r"(
+                                     smem_u32(&empty[s]))
+                                 : "memory");
+                    if (two)
+                        asm volatile(
+                            "tcgen05.commit.cta_group::1.mbarrier::arrive::one.shared::cluster.b64 [%0];" ::"r"(
+                                smem_u32(&empty[s1]))
+                            : "memory");
+                }
+                __syncwarp();
+                if (two) {
+                    s = s1 + 1 == STG ? 0 : s1 + 1;
+                    ph = s1 + 1 == STG ? ph1 ^ 1 : ph1;
+                } else {
+                    s = s1;
+                    ph = ph1;
+                }
+                ks += two ? 2 : 1;
+            }
+            if (alive && lane == 0)
+                asm volatile("tcgen05.commit.cta_group::1.mbarrier::arrive::one.shared::cluster.b64 [%0];" ::"r"(
+                                 smem_u32(&acc_full[buf]))
+                             : "memory");
+            __syncwarp();
+        }
+        // Completion of this commit covers every MMA issued above; it is
+        // awaited also after a timeout, before TMEM is freed.
+        if (lane == 0)
+            asm volatile("tcgen05.commit.cta_group::1.mbarrier::arrive::one.shared::cluster.b64 [%0];" ::"r"(
+                             smem_u32(&fin_bar))
+                         : "memory");
+        __syncwarp();
+        mbar_wait_quiet(smem_u32(&fin_bar), 0);
+    } else {
+        // ---- epilogue: warp quarter q reads TMEM lanes 32q.. (weight rows),
+        // 16 token columns at a time.  With ytma the chunk goes through shared
+        // memory ([16 tokens][128 rows], two buffers) and leaves by one TMA
+        // store, which clips rows past N and tokens past T; otherwise each
+        // store instruction writes 32 consecutive weight rows of one token.
+        const int q = warp & 3, et = threadIdx.x - TC4_EPI * 32;
+        float *ebuf = (float *)(base + STG * SB);
+        int li = 0, ch = 0;
+        for (int item = blockIdx.x; item < ntiles; item += gridDim.x, li++) {
+            const int buf = li & 1;
+            const int row0 = (item % ntm) * 128;
+            const int64_t n = (int64_t)row0 + 32 * q + lane;
+            const int t0 = (item / ntm) * BT;
+            const bool ok = epi_all(mbar_wait(smem_u32(&acc_full[buf]), (li >> 1) & 1, flag, 128));
+            tc_fence_after();
+            for (int c0 = 0; ok && c0 < BT && t0 + c0 < T; c0 += TC4_ECH, ch++) {
+                uint32_t rr[16];
+                const uint32_t taddr = tmem + ((uint32_t)(32 * q) << 16) + (uint32_t)(buf * BT + c0);
+                asm volatile(
+                    "tcgen05.ld.sync.aligned.32x32b.x16.b32 {%0,%1,%2,%3,%4,%5,%6,%7,%8,%9,%10,%11,%12,%13,%14,%15}, "
+                    "[%16];"
+                    : "=r"(rr[0]), "=r"(rr[1]), "=r"(rr[2]), "=r"(rr[3]), "=r"(rr[4]), "=r"(rr[5]), "=r"(rr[6]),
+                      "=r"(rr[7]), "=r"(rr[8]), "=r"(rr[9]), "=r"(rr[10]), "=r"(rr[11]), "=r"(rr[12]), "=r"(rr[13]),
+                      "=r"(rr[14]), "=r"(rr[15])
+                    : "r"(taddr));
+                asm volatile("tcgen05.wait::ld.sync.aligned;" ::: "memory");
+                float v[16];
+#pragma unroll
+                for (int j = 0; j < 16; j++) {
+                    v[j] = __uint_as_float(rr[j]);
+                    // EX: undo 2^(wshift + rowshift[t]) (exact power of two)
+                    if (EX) {
+                        const int t = min(t0 + c0 + j, T - 1);
+                        v[j] *= __int_as_float((127 - wshift - __ldg(rowshift + t)) << 23);
+                    }
+                }
+                if (ytma) {
+                    float *sb = ebuf + (ch & 1) * (TC4_ECH * 128);
+                    if (et == 0) bulk_wait_read1();  // the store issued from this buffer two chunks ago has read it
+                    epi_sync();
+#pragma unroll
+                    for (int j = 0; j < 16; j++) sb[j * 128 + 32 * q + lane] = v[j];
+                    fence_async_smem();
+                    epi_sync();
+                    if (et == 0) {
+                        tma_store_2d(&tmy, smem_u32(sb), row0, t0 + c0);
+                        bulk_commit();
+                    }
+                } else if (n < N) {
+#pragma unroll
+                    for (int j = 0; j < 16; j++)
+                        if (t0 + c0 + j < T) Y[(int64_t)(t0 + c0 + j) * N + n] = v[j];
+                }
+            }
+            tc_fence_before();
+            mbar_arrive(smem_u32(&acc_empty[buf]));
+            if (!ok) break;
+        }
+        if (et == 0) bulk_wait_all();
+    }
+    tc_fence_before();
+    __syncthreads();
+    if (warp == TC4_MMA) {
+        tc_fence_after();
+        asm volatile("tcgen05.dealloc.cta_group::1.sync.aligned.b32 %0, %1;" ::"r"(tmem), "r"(512));
+    }
+}
+
 template <int TYPE, int BT, int EX>
 cudaError_t launch_tc3(hd_ctx *ctx, const hd_weight *w, const CUtensorMap &tmx, const CUtensorMap &tmx_lo, float *Y,
                        int T, int ks, const int *rowshift) {
@@ -1005,14 +1397,132 @@ cudaError_t launch_tc3(hd_ctx *ctx, const hd_weight *w, const CUtensorMap &tmx, 
                      (int)w->rows, ntm, ntiles, ks, w->f16_shift, rowshift, ctx->flag);
 }
 
+// Token tile of the two-pass GEMM: the multiple of 16 (64..256; exact mode
+// up to 160, three stages of hi and lo tiles) minimising rounds of tiles per
+// SM x cycles per K-step, a step costing the larger of its MMA time (2*BT per
+// product) and its shared-memory traffic at ~128 B per cycle (stage written
+// once, read once; exact mode: hi tiles read twice).
+int tc4_pick_bt(int64_t mt, int T, int sms, int ex) {
+    int best_bt = 64;
+    double best = 1e30;
+    for (int bt = 64; bt <= (ex ? 160 : 256); bt += 16) {
+        if (bt > 64 && T <= bt - 16) break;
+        if (tc4_stages(bt, ex) < 3) continue;
+        const int64_t tiles = mt * ((T + bt - 1) / bt);
+        const double rounds = (double)((tiles + sms - 1) / sms);
+        const double sb = tc4_stage_bytes(bt, ex);
+        const double mma = (ex ? 3.0 : 1.0) * 2.0 * bt, smem = (ex ? 2.5 : 2.0) * sb / 128.0;
+        const double cost = rounds * ((mma > smem ? mma : smem) + 64.0);
+        if (cost < best - 1e-9) { best = cost; best_bt = bt; }
+    }
+    return best_bt;
+}
+
+// The two-pass path (see k_gemm_tc4).  Activations as for v3; the weight is
+// dequantized into ctx->wbf first.
+int qgemm_tc4(hd_ctx *ctx, const hd_weight *w, const float *X, float *Y, int T, int exact) {
+    const int64_t N = w->rows, K = w->cols;
+    const size_t plane = ((size_t)T * K * 2 + 255) & ~(size_t)255;
+    const size_t need = exact ? 2 * plane + (size_t)T * sizeof(int) : plane;
+    int rc = hd_ensure_hbuf(ctx, &ctx->xbf, &ctx->xbf_bytes, (need + 3) / 4 * 4);
+    if (rc) return rc;
+    const size_t wplane = ((size_t)N * K * 2 + 255) & ~(size_t)255;
+    rc = hd_ensure_hbuf(ctx, &ctx->wbf, &ctx->wbf_bytes, (exact ? 2 : 1) * wplane);
+    if (rc) return rc;
+    uint8_t *xb = (uint8_t *)ctx->xbf, *wb = (uint8_t *)ctx->wbf;
+    int *rowshift = exact ? (int *)(xb + 2 * plane) : nullptr;
+    const WView v = wview(w);
+    const int nrb = (int)((N + 31) / 32), nw = nrb * ((w->units + 7) / 8);
+    const int nx = exact ? T : (int)(((int64_t)T * K / 8 + 255) / 256);
+    cudaError_t e = cudaSuccess;
+    HD_TYPE_SWITCH(w->type, TT, {
+        if (exact)
+            e = hd_launch(ctx, k_prep<TT, 1>, dim3((unsigned)(nw + nx)), dim3(256), 0, v, (uint16_t *)wb,
+                          (uint16_t *)(wb + wplane), w->f16_shift, nrb, nw, X, T, (uint16_t *)xb,
+                          (uint16_t *)(xb + plane), rowshift);
+        else
+            e = hd_launch(ctx, k_prep<TT, 0>, dim3((unsigned)(nw + nx)), dim3(256), 0, v, (uint16_t *)wb,
+                          (uint16_t *)nullptr, 0, nrb, nw, X, T, (uint16_t *)xb, (uint16_t *)nullptr, (int *)nullptr);
+    });
+    if (e != cudaSuccess) return hd_fail(ctx, HD_E_CUDA, "hd_qgemm (operand preparation): %s", cudaGetErrorString(e));
+
+    const int64_t mt = (N + 127) / 128;
+    int bt = tc4_pick_bt(mt, T, ctx->sm_count, exact);
+    if (const char *env = getenv("HACEDLE_TC_BT")) {
+        const int b = atoi(env);
+        if (b >= 16 && b <= (exact ? 160 : 256) && b % 16 == 0) bt = b;
+    }
+    EncodeTiledFn enc = encode_tiled();
+    if (!enc) return hd_fail(ctx, HD_E_CUDA, "hd_qgemm: cuTensorMapEncodeTiled is not available");
+    const CUtensorMapDataType dt = exact ? CU_TENSOR_MAP_DATA_TYPE_FLOAT16 : CU_TENSOR_MAP_DATA_TYPE_BFLOAT16;
+    CUtensorMap tw, twl, tx, txl;
+    auto make = [&](CUtensorMap *m, void *ptr, int64_t rows, int box_rows) {
+        cuuint64_t dims[2] = {(cuuint64_t)K, (cuuint64_t)rows};
+        cuuint64_t strides[1] = {(cuuint64_t)K * 2};
+        cuuint32_t box[2] = {(cuuint32_t)BK, (cuuint32_t)box_rows};
+        cuuint32_t estr[2] = {1, 1};
+        return enc(m, dt, 2, ptr, dims, strides, box, estr, CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B,
+                   CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+    };
+    CUresult cr = make(&tw, wb, N, 128);
+    if (cr == CUDA_SUCCESS) cr = make(&twl, exact ? wb + wplane : wb, N, 128);
+    if (cr == CUDA_SUCCESS) cr = make(&tx, xb, T, bt);
+    if (cr == CUDA_SUCCESS) cr = make(&txl, exact ? xb + plane : xb, T, bt);
+    // Output chunks by TMA store when the rows of Y are 16-byte multiples.
+    CUtensorMap ty;
+    int ytma = 0;
+    if (cr == CUDA_SUCCESS && N % 4 == 0 && getenv("HACEDLE_TC4_DIRECT_STORE") == nullptr) {
+        cuuint64_t dims[2] = {(cuuint64_t)N, (cuuint64_t)T};
+        cuuint64_t strides[1] = {(cuuint64_t)N * 4};
+        cuuint32_t box[2] = {128, (cuuint32_t)TC4_ECH};
+        cuuint32_t estr[2] = {1, 1};
+        cr = enc(&ty, CU_TENSOR_MAP_DATA_TYPE_FLOAT32, 2, Y, dims, strides, box, estr, CU_TENSOR_MAP_INTERLEAVE_NONE,
+                 CU_TENSOR_MAP_SWIZZLE_NONE, CU_TENSOR_MAP_L2_PROMOTION_NONE, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+        ytma = 1;
+    } else {
+        ty = tx;
+    }
+    if (cr != CUDA_SUCCESS) return hd_fail(ctx, HD_E_CUDA, "hd_qgemm: cuTensorMapEncodeTiled failed (%d)", (int)cr);
+
+    const size_t smem = (size_t)tc4_stages(bt, exact) * tc4_stage_bytes(bt, exact) + TC4_EPI_BYTES + 1024;
+    const int ntm = (int)mt, ntiles = ntm * ((T + bt - 1) / bt);
+    const int grid = ntiles < ctx->sm_count ? ntiles : ctx->sm_count;
+    const int ksteps = (int)((w->units + 1) / 2);
+    if (exact) {
+        e = cudaFuncSetAttribute(k_gemm_tc4<1>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
+        if (e == cudaSuccess)
+            e = hd_launch(ctx, k_gemm_tc4<1>, dim3(grid), dim3(TC4_THREADS), smem, tw, twl, tx, txl, ty, Y, T, (int)N,
+                          bt, ntm, ntiles, ksteps, w->f16_shift, (const int *)rowshift, ytma, ctx->flag);
+    } else {
+        e = cudaFuncSetAttribute(k_gemm_tc4<0>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
+        if (e == cudaSuccess)
+            e = hd_launch(ctx, k_gemm_tc4<0>, dim3(grid), dim3(TC4_THREADS), smem, tw, twl, tx, txl, ty, Y, T, (int)N,
+                          bt, ntm, ntiles, ksteps, 0, (const int *)nullptr, ytma, ctx->flag);
+    }
+    if (e != cudaSuccess) return hd_fail(ctx, HD_E_CUDA, "hd_qgemm (tcgen05 two-pass): %s", cudaGetErrorString(e));
+    return HD_OK;
+}
+
 }  // namespace
 
-// rows % 128 == 0 uses the streamed v3 kernel, other shapes the v1 kernel.
+// Fewest tokens for the two-pass path: 128 (HACEDLE_TC4_MIN_T overrides the
+// threshold; 0 disables the path).
+int hd_tc4_min_t() {
+    const char *env = getenv("HACEDLE_TC4_MIN_T");
+    return env ? atoi(env) : 128;
+}
+
+// From hd_tc4_min_t() tokens the two-pass kernel; below, rows % 128 == 0 uses
+// the streamed v3 kernel, other shapes the v1 kernel.
 // exact != 0 (rows % 128 == 0 only): the fp32-accuracy mode -- exact weights
 // and x, each split into fp16 hi + lo, three MMAs per product.
 int hd_qgemm_tc(hd_ctx *ctx, const hd_weight *w, const float *X, float *Y, int T, int exact) {
     HD_REQUIRE(ctx, w->cols % 8 == 0, HD_E_SHAPE, "hd_qgemm: K must be a multiple of 8");
     const int64_t mt = (w->rows + 127) / 128;
+    {
+        const int min_t = hd_tc4_min_t();
+        if (min_t > 0 && T >= min_t) return qgemm_tc4(ctx, w, X, Y, T, exact);
+    }
     cudaError_t e = cudaSuccess;
     const bool v3 = w->rows % 128 == 0 && ((uintptr_t)Y & 15) == 0 && (exact || getenv("HACEDLE_TC_V1") == nullptr);
     HD_REQUIRE(ctx, v3 || !exact, HD_E_UNSUPPORTED, "hd_qgemm: the exact tensor-core mode needs rows % 128 == 0");

@@ -54,6 +54,8 @@ struct hd_ctx {
     size_t scratch_bytes = 0;
     float *xbf = nullptr;            // bf16 copy of GEMM activations (TMA source)
     size_t xbf_bytes = 0;
+    float *wbf = nullptr;            // dequantized weight rows of the two-pass GEMM (TMA source)
+    size_t wbf_bytes = 0;
 };
 
 struct hd_weight {

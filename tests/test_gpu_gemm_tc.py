@@ -70,12 +70,15 @@ def test_qgemm_tc_prefill_2048(ctx):
                                      (S.GGML_Q6_K, 128, 768, 33), (S.GGML_Q8_0, 256, 160, 300),
                                      (S.GGML_Q5_0, 128, 896, 64)])
 @pytest.mark.parametrize("bt", ["", "64", "128", "208"])
-def test_qgemm_tc_streamed_ragged_tiles(ctx, monkeypatch, t, N, K, T, bt):
+@pytest.mark.parametrize("path", ["streamed", "two_pass"])
+def test_qgemm_tc_streamed_ragged_tiles(ctx, monkeypatch, t, N, K, T, bt, path):
     """Streamed kernel (rows % 128 == 0): odd unit counts (a half-empty last K
-    step), token tails, the two-way K split of small grids, every token tile."""
+    step), token tails, the two-way K split of small grids, every token tile;
+    the same cases through the two-pass kernel (dequantize, then TMA GEMM)."""
     import torch
     if bt:
         monkeypatch.setenv("HACEDLE_TC_BT", bt)
+    monkeypatch.setenv("HACEDLE_TC4_MIN_T", "0" if path == "streamed" else "1")
     raw = S.gen_weight(t, N, K, 80 + N)
     X = S.gen_activations(T, K, 81)
     w = ctx.weight(t, raw, N, K)
@@ -130,11 +133,13 @@ def test_qgemm_fp32_row_groups(ctx, t, N, K, T):
 
 @pytest.mark.parametrize("t,N,K", [(S.GGML_Q5_0, 256, 896), (S.GGML_Q4_K, 128, 1024), (S.GGML_Q6_K, 384, 512),
                                    (S.GGML_Q8_0, 128, 256)])
-def test_qgemm_fp32_tensor_core_row_scaling(ctx, t, N, K):
+@pytest.mark.parametrize("path", ["streamed", "two_pass"])
+def test_qgemm_fp32_tensor_core_row_scaling(ctx, monkeypatch, t, N, K, path):
     """fp32 precision on the tensor cores splits x and the weights into fp16
     halves after power-of-two scaling per activation row: rows whose
     magnitudes differ by 10 orders each keep 1e-5 of their own maximum."""
     import torch
+    monkeypatch.setenv("HACEDLE_TC4_MIN_T", "0" if path == "streamed" else "1")
     T = 48
     raw = S.gen_weight(t, N, K, 130 + t)
     X = S.gen_activations(T, K, 131)
@@ -147,3 +152,50 @@ def test_qgemm_fp32_tensor_core_row_scaling(ctx, t, N, K):
     got = Y.cpu().numpy()
     err = np.abs(got - ref).max(axis=1) / np.abs(ref).max(axis=1)
     assert err.max() <= 1e-5, err.max()
+
+
+@pytest.mark.parametrize("t,N,K,T", [(S.GGML_Q5_0, 100, 96, 1), (S.GGML_Q5_0, 200, 160, 70),
+                                     (S.GGML_Q4_K, 130, 512, 33), (S.GGML_Q6_K, 257, 256, 257),
+                                     (S.GGML_Q8_0, 64, 64, 300), (S.GGML_Q4_K, 1000, 768, 129)])
+@pytest.mark.parametrize("bt", ["", "16", "112", "256"])
+def test_qgemm_two_pass_any_rows(ctx, monkeypatch, t, N, K, T, bt):
+    """Two-pass kernel on row counts that are not multiples of 128 (rows past
+    N arrive as TMA zero fill and are not stored), odd unit counts, token tails
+    and token tiles from 16 to 256; NaN-filled outputs must be fully written."""
+    import torch
+    monkeypatch.setenv("HACEDLE_TC4_MIN_T", "1")
+    if bt:
+        monkeypatch.setenv("HACEDLE_TC_BT", bt)
+    raw = S.gen_weight(t, N, K, 140 + N)
+    X = S.gen_activations(T, K, 141)
+    w = ctx.weight(t, raw, N, K)
+    Y = torch.full((T, N), float("nan"), device="cuda")
+    ctx.qgemm(w, torch.from_numpy(X).cuda(), Y, precision=1)
+    ctx.check_device_errors()
+    ref = X @ O.dequantize(t, raw, N * K).reshape(N, K).T
+    got = Y.cpu().numpy()
+    assert np.isfinite(got).all()
+    assert np.abs(got - ref).max() / np.abs(ref).max() <= TOL
+
+
+@pytest.mark.parametrize("t,N,K,T", [(S.GGML_Q5_0, 200, 160, 70), (S.GGML_Q6_K, 257, 256, 257),
+                                     (S.GGML_Q4_K, 1000, 768, 129), (S.GGML_Q8_0, 4864, 896, 300)])
+def test_qgemm_fp32_two_pass_any_rows(ctx, monkeypatch, t, N, K, T):
+    """Exact-product mode of the two-pass kernel, any row count: the oracle's
+    fp32 product within 1e-5 of its maximum, bitwise-stable reruns."""
+    import torch
+    monkeypatch.setenv("HACEDLE_TC4_MIN_T", "1")
+    raw = S.gen_weight(t, N, K, 150 + N)
+    X = S.gen_activations(T, K, 151)
+    w = ctx.weight(t, raw, N, K)
+    Xd = torch.from_numpy(X).cuda()
+    Y = torch.full((T, N), float("nan"), device="cuda")
+    ctx.qgemm(w, Xd, Y, precision=0)
+    ctx.check_device_errors()
+    ref = O.qgemv(t, raw, N, K, X, threads=8)
+    got = Y.cpu().numpy()
+    assert np.abs(got - ref).max() / np.abs(ref).max() <= 1e-5
+    Y2 = torch.empty(T, N, device="cuda")
+    ctx.qgemm(w, Xd, Y2, precision=0)
+    torch.cuda.synchronize()
+    assert torch.equal(Y, Y2)
