@@ -1520,8 +1520,14 @@ int hd_qgemm_tc(hd_ctx *ctx, const hd_weight *w, const float *X, float *Y, int T
     HD_REQUIRE(ctx, w->cols % 8 == 0, HD_E_SHAPE, "hd_qgemm: K must be a multiple of 8");
     const int64_t mt = (w->rows + 127) / 128;
     {
+        // The exact-product mode stays on the streamed kernel where that one
+        // runs (rows % 128 == 0): its accumulation order reproduces the fp32
+        // oracle's greedy tokens on the 0.5B-shaped decoder, the two-pass
+        // order (one K chain per tile) flips a near tie after 15 tokens.
+        // HACEDLE_TC4_EXACT=1 sends it to the two-pass kernel as well.
         const int min_t = hd_tc4_min_t();
-        if (min_t > 0 && T >= min_t) return qgemm_tc4(ctx, w, X, Y, T, exact);
+        const bool ex_v4 = w->rows % 128 != 0 || getenv("HACEDLE_TC4_EXACT") != nullptr;
+        if (min_t > 0 && T >= min_t && (!exact || ex_v4)) return qgemm_tc4(ctx, w, X, Y, T, exact);
     }
     cudaError_t e = cudaSuccess;
     const bool v3 = w->rows % 128 == 0 && ((uintptr_t)Y & 15) == 0 && (exact || getenv("HACEDLE_TC_V1") == nullptr);

@@ -140,6 +140,8 @@ def test_qgemm_fp32_tensor_core_row_scaling(ctx, monkeypatch, t, N, K, path):
     magnitudes differ by 10 orders each keep 1e-5 of their own maximum."""
     import torch
     monkeypatch.setenv("HACEDLE_TC4_MIN_T", "0" if path == "streamed" else "1")
+    if path == "two_pass":
+        monkeypatch.setenv("HACEDLE_TC4_EXACT", "1")
     T = 48
     raw = S.gen_weight(t, N, K, 130 + t)
     X = S.gen_activations(T, K, 131)
@@ -185,6 +187,7 @@ def test_qgemm_fp32_two_pass_any_rows(ctx, monkeypatch, t, N, K, T):
     fp32 product within 1e-5 of its maximum, bitwise-stable reruns."""
     import torch
     monkeypatch.setenv("HACEDLE_TC4_MIN_T", "1")
+    monkeypatch.setenv("HACEDLE_TC4_EXACT", "1")
     raw = S.gen_weight(t, N, K, 150 + N)
     X = S.gen_activations(T, K, 151)
     w = ctx.weight(t, raw, N, K)
