@@ -116,16 +116,34 @@ __global__ void __launch_bounds__(ANT) k_attention(const float *__restrict__ q, 
     for (int k = 0; k < OPT; k++) o[k] = 0.f;
     const int64_t cbase = (int64_t)cseq * max_ctx;
     const int c1 = min(nchunks, (p + 1) * cpc);
+    // A chunk's K and V rows: CH * HD / 4 float4 each, NLD per thread per
+    // batch.  All loads of a batch are issued before any is stored, so the
+    // chunk costs one memory latency per batch rather than one per float4.
+    constexpr int NF4 = CH * (HD / 4) / ANT, NB = HD > 64 ? 4 : 8, NLD = NF4 < NB ? NF4 : NB;
     for (int c = p * cpc; c < c1; c++) {
         const int j0 = c * CH, nj = min(CH, L - j0);
         __syncthreads();
-        for (int i = tid; i < nj * (HD / 4); i += ANT) {
-            const int j = i / (HD / 4), d4 = i % (HD / 4);
-            const int64_t g = ((cbase + j0 + j) * n_kv + kvh) * HD + 4 * d4;
-            const float4 kv = *(const float4 *)(kc + g), vv = *(const float4 *)(vc + g);
-            float *kd = Ks + j * KP + 4 * d4;
-            kd[0] = kv.x; kd[1] = kv.y; kd[2] = kv.z; kd[3] = kv.w;
-            *(float4 *)(Vs + j * HD + 4 * d4) = vv;
+#pragma unroll
+        for (int b0 = 0; b0 < NF4; b0 += NLD) {
+            float4 kr[NLD], vr[NLD];
+#pragma unroll
+            for (int u = 0; u < NLD; u++) {
+                const int i = tid + (b0 + u) * ANT, j = i / (HD / 4), d4 = i % (HD / 4);
+                if (j < nj) {
+                    const int64_t g = ((cbase + j0 + j) * n_kv + kvh) * HD + 4 * d4;
+                    kr[u] = __ldg((const float4 *)(kc + g));
+                    vr[u] = __ldg((const float4 *)(vc + g));
+                }
+            }
+#pragma unroll
+            for (int u = 0; u < NLD; u++) {
+                const int i = tid + (b0 + u) * ANT, j = i / (HD / 4), d4 = i % (HD / 4);
+                if (j < nj) {
+                    float *kd = Ks + j * KP + 4 * d4;
+                    kd[0] = kr[u].x; kd[1] = kr[u].y; kd[2] = kr[u].z; kd[3] = kr[u].w;
+                    *(float4 *)(Vs + j * HD + 4 * d4) = vr[u];
+                }
+            }
         }
         __syncthreads();
         for (int i = tid; i < rep * nj; i += ANT) {
@@ -207,8 +225,10 @@ __global__ void __launch_bounds__(ANT) k_attention(const float *__restrict__ q, 
     for (int i = tid; i < npairs; i += ANT) {
         const int h = i / HD, d = i % HD;
         float M = -INFINITY;
+#pragma unroll 8
         for (int pp = 0; pp < Pr; pp++) M = fmaxf(M, __ldcg(part + (int64_t)pp * rep * W + h * W + HD));
         float O = 0.f, Ls = 0.f;
+#pragma unroll 8
         for (int pp = 0; pp < Pr; pp++) {
             const float *pt = part + (int64_t)pp * rep * W + h * W;
             const float e = expf(__ldcg(pt + HD) - M);
