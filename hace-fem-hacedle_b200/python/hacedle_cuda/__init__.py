@@ -31,6 +31,9 @@ EXPORTS = [
     "hd_rmsnorm", "hd_rmsnorm_graph", "hd_rope_neox", "hd_rope_interleaved", "hd_softmax_rows", "hd_swiglu",
     "hd_add", "hd_argmax_rows", "hd_argmax_rows_noalloc", "hd_embed", "hd_kv_append", "hd_attention_decode", "hd_attention_prefill",
     "hd_dot_i8", "hd_fused_qdot_qadd_qacc_i8", "hd_gather_columns", "hd_decoder_create", "hd_decoder_free", "hd_decoder_generate",
+    "hd_gguf_open", "hd_gguf_open_memory", "hd_gguf_close", "hd_gguf_error", "hd_gguf_counts", "hd_gguf_tensor",
+    "hd_gguf_find_tensor", "hd_gguf_kv", "hd_gguf_find_key", "hd_gguf_kv_int", "hd_gguf_kv_float", "hd_gguf_kv_string",
+    "hd_gguf_kv_array", "hd_gguf_upload",
 ]
 
 
@@ -76,12 +79,19 @@ def lib() -> C.CDLL:
         "hd_dot_i8": [V, V, V, I64, I, V], "hd_fused_qdot_qadd_qacc_i8": [V, V, V, I64, I, V, V, V],
         "hd_decoder_create": [V, V, V, V, V, C.POINTER(V)], "hd_decoder_free": [V],
         "hd_decoder_generate": [V, V, I, I, I, I, V, V, V],
+        "hd_gguf_open": [C.c_char_p, C.POINTER(V)], "hd_gguf_open_memory": [V, SZ, C.POINTER(V)], "hd_gguf_close": [V],
+        "hd_gguf_error": [], "hd_gguf_counts": [V, V, V, V, V], "hd_gguf_tensor": [V, I64, V],
+        "hd_gguf_find_tensor": [V, C.c_char_p, V], "hd_gguf_kv": [V, I64, V, V, V, V],
+        "hd_gguf_find_key": [V, C.c_char_p, V], "hd_gguf_kv_int": [V, I64, V], "hd_gguf_kv_float": [V, I64, V],
+        "hd_gguf_kv_string": [V, I64, C.c_uint64, V, V], "hd_gguf_kv_array": [V, I64, V, V],
+        "hd_gguf_upload": [V, V, C.c_char_p, C.POINTER(V)],
     }
     for name, args in sig.items():
         fn = getattr(L, name)
         fn.argtypes = args
         fn.restype = I
     L.hd_last_error.restype = C.c_char_p
+    L.hd_gguf_error.restype = C.c_char_p
     L.hd_version.restype = C.c_char_p
     L.hd_ctx_launch_count.restype = C.c_uint64
     _lib = L
@@ -105,6 +115,13 @@ class Weight:
         h = V()
         ctx._check(lib().hd_weight_upload(ctx.h, raw.ctypes.data, raw.size, ggml_type, rows, cols, C.byref(h)))
         self.h = h
+
+    @classmethod
+    def from_handle(cls, ctx: "Context", h, ggml_type: int, rows: int, cols: int, nbytes: int) -> "Weight":
+        """Wrap a handle the library made (hd_gguf_upload)."""
+        w = cls.__new__(cls)
+        w.ctx, w.type, w.rows, w.cols, w.nbytes, w.h = ctx, ggml_type, rows, cols, nbytes, h
+        return w
 
     def download(self) -> np.ndarray:
         out = np.zeros(self.nbytes, np.uint8)

@@ -254,6 +254,57 @@ int hd_decoder_generate(hd_decoder *dec, const int32_t *prompts_host, int seqs, 
                         int n_gen, int prefill_precision, int32_t *out_host, float *decode_ms_out,
                         float *prefill_ms_out);
 
+/* ------------------------------------------------------------ GGUF reader */
+/* Replaces GgufLoader::load_std, GgufTensorIndex::parse and tensor_bytes
+ * (src/x/loader/gguf/loader.rs:64-141, tensor_index.rs:24-170, header.rs:54-84)
+ * with a reader of the published GGUF v2/v3 layout (gguf 0.19.0 GGUFWriter):
+ * u32 value types (STRING = 8, ARRAY = 9, UINT64 = 10 ...), tensor infos as
+ * {name, n_dims, dims, ggml_type, offset}, data aligned to general.alignment,
+ * tensor sizes from the ggml block tables.  Host only (no context, no GPU),
+ * except hd_gguf_upload.  A malformed or truncated file fails with HD_E_ARG
+ * (HD_E_UNSUPPORTED for other versions or array element types); the message
+ * of the last failed hd_gguf_* call on this thread is hd_gguf_error(). */
+typedef struct hd_gguf hd_gguf;
+typedef struct {
+    const char *name;       /* owned by the handle                            */
+    int32_t ggml_type;
+    int32_t n_dims;         /* 1..4                                           */
+    int64_t dims[4];        /* ggml order: dims[0] is the contiguous axis (a
+                               [rows x cols] weight has dims {cols, rows}); 1 past n_dims */
+    uint64_t offset;        /* absolute file offset of the tensor's data      */
+    uint64_t nbytes;        /* 0 when the type's block size is not known here */
+    const uint8_t *data;    /* host pointer into the handle's bytes           */
+} hd_gguf_tensor_info;
+
+/* Maps the file read-only (the handle keeps the mapping until hd_gguf_close). */
+int hd_gguf_open(const char *path, hd_gguf **out);
+/* Parses a copy of `nbytes` bytes already in host memory. */
+int hd_gguf_open_memory(const uint8_t *bytes, size_t nbytes, hd_gguf **out);
+int hd_gguf_close(hd_gguf *g);
+const char *hd_gguf_error(void);
+int hd_gguf_counts(const hd_gguf *g, uint32_t *version, int64_t *n_tensors, int64_t *n_kv,
+                   uint64_t *alignment);
+/* Tensor i in file order; GgufLoader::get_tensor (loader.rs:112-114) by name. */
+int hd_gguf_tensor(const hd_gguf *g, int64_t i, hd_gguf_tensor_info *out);
+int hd_gguf_find_tensor(const hd_gguf *g, const char *name, int64_t *index);
+/* Metadata entry i: key, value type (GGUFValueType), and for arrays the
+ * element type and length (-1 and 0 otherwise). */
+int hd_gguf_kv(const hd_gguf *g, int64_t i, const char **key, int32_t *type, int32_t *arr_type,
+               uint64_t *arr_len);
+int hd_gguf_find_key(const hd_gguf *g, const char *key, int64_t *index);
+/* Scalar integers and bools as int64; floats (and integers) as double. */
+int hd_gguf_kv_int(const hd_gguf *g, int64_t i, int64_t *out);
+int hd_gguf_kv_float(const hd_gguf *g, int64_t i, double *out);
+/* A string value (j = 0) or element j of a string array: pointer and length
+ * (not NUL-terminated). */
+int hd_gguf_kv_string(const hd_gguf *g, int64_t i, uint64_t j, const char **s, uint64_t *len);
+/* A numeric array: pointer to its little-endian elements and their count (a
+ * numeric scalar reads as an array of one, e.g. a u64 above INT64_MAX). */
+int hd_gguf_kv_array(const hd_gguf *g, int64_t i, const void **data, uint64_t *n);
+/* hd_weight_upload of the named 2-D Q8_0 / Q5_0 / Q4_K / Q6_K tensor
+ * (rows = dims[1], cols = dims[0]). */
+int hd_gguf_upload(hd_ctx *ctx, const hd_gguf *g, const char *name, hd_weight **out);
+
 #ifdef __cplusplus
 }
 #endif
