@@ -70,6 +70,7 @@ extern "C" int hd_ctx_destroy(hd_ctx *ctx) {
     cudaFree(ctx->scratch);
     cudaFree(ctx->xbf);
     cudaFree(ctx->wbf);
+    cudaFree(ctx->samp);
     if (ctx->own_stream) cudaStreamDestroy(ctx->own_stream);
     delete ctx;
     return HD_OK;

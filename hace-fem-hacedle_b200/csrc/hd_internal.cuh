@@ -56,6 +56,8 @@ struct hd_ctx {
     size_t xbf_bytes = 0;
     float *wbf = nullptr;            // dequantized weight rows of the two-pass GEMM (TMA source)
     size_t wbf_bytes = 0;
+    float *samp = nullptr;           // logits processor: sorted rows, segment offsets, sort scratch
+    size_t samp_bytes = 0;
 };
 
 struct hd_weight {

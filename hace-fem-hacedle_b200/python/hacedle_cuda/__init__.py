@@ -33,7 +33,7 @@ EXPORTS = [
     "hd_dot_i8", "hd_fused_qdot_qadd_qacc_i8", "hd_gather_columns", "hd_decoder_create", "hd_decoder_free", "hd_decoder_generate",
     "hd_gguf_open", "hd_gguf_open_memory", "hd_gguf_close", "hd_gguf_error", "hd_gguf_counts", "hd_gguf_tensor",
     "hd_gguf_find_tensor", "hd_gguf_kv", "hd_gguf_find_key", "hd_gguf_kv_int", "hd_gguf_kv_float", "hd_gguf_kv_string",
-    "hd_gguf_kv_array", "hd_gguf_upload",
+    "hd_gguf_kv_array", "hd_gguf_upload", "hd_logits_process", "hd_sample_rows",
 ]
 
 
@@ -85,6 +85,7 @@ def lib() -> C.CDLL:
         "hd_gguf_find_key": [V, C.c_char_p, V], "hd_gguf_kv_int": [V, I64, V], "hd_gguf_kv_float": [V, I64, V],
         "hd_gguf_kv_string": [V, I64, C.c_uint64, V, V], "hd_gguf_kv_array": [V, I64, V, V],
         "hd_gguf_upload": [V, V, C.c_char_p, C.POINTER(V)],
+        "hd_logits_process": [V, V, I64, I64, F, F, I64], "hd_sample_rows": [V, V, I64, I64, C.c_uint64, C.c_uint64, V],
     }
     for name, args in sig.items():
         fn = getattr(L, name)
@@ -186,6 +187,16 @@ class Context:
         return Weight(self, ggml_type, raw, rows, cols)
 
     # ---- kernels (device tensors) ----
+    def logits_process(self, logits, temperature: float, top_p: float, top_k: int):
+        """LogitsProcessor::process in place on a [rows, n] device tensor."""
+        rows, n = (1, logits.numel()) if logits.dim() == 1 else logits.shape
+        self._check(lib().hd_logits_process(self.h, _ptr(logits), rows, n, temperature, top_p, top_k))
+
+    def sample(self, logits, idx, seed: int, offset: int = 0):
+        """One index per row of [rows, n] logits into int32 idx[rows]."""
+        rows, n = (1, logits.numel()) if logits.dim() == 1 else logits.shape
+        self._check(lib().hd_sample_rows(self.h, _ptr(logits), rows, n, seed, offset, _ptr(idx)))
+
     def dequantize(self, w: Weight, out):
         self._check(lib().hd_dequantize(self.h, w.h, _ptr(out), out.numel()))
 

@@ -254,6 +254,21 @@ int hd_decoder_generate(hd_decoder *dec, const int32_t *prompts_host, int seqs, 
                         int n_gen, int prefill_precision, int32_t *out_host, float *decode_ms_out,
                         float *prefill_ms_out);
 
+/* ---------------------------------------------------------------- sampler */
+/* LogitsProcessor::process (src/x/provider/candle/lmhead.rs:42-111) in place on
+ * rows x n logits, with the reference's definitions: l /= max(temperature,
+ * 0.001); top-p threshold = the logit at which the descending-order f32 sum of
+ * min(exp(l), 1) first reaches top_p (0.0 if it never does); top-k threshold =
+ * the (top_k+1)-th largest logit after top-p (none when top_k is 0 or >= n);
+ * logits below either threshold become -inf.  rows * n < 2^31. */
+int hd_logits_process(hd_ctx *ctx, float *logits_dev, int64_t rows, int64_t n, float temperature,
+                      float top_p, int64_t top_k);
+/* One index per row drawn from softmax(logits) (-inf entries never drawn;
+ * -1 for a row with no finite logit).  Row r uses the Philox4x32-10 block at
+ * counter offset + r under key `seed`, so draws are reproducible. */
+int hd_sample_rows(hd_ctx *ctx, const float *logits_dev, int64_t rows, int64_t n, uint64_t seed,
+                   uint64_t offset, int32_t *idx_dev);
+
 /* ------------------------------------------------------------ GGUF reader */
 /* Replaces GgufLoader::load_std, GgufTensorIndex::parse and tensor_bytes
  * (src/x/loader/gguf/loader.rs:64-141, tensor_index.rs:24-170, header.rs:54-84)

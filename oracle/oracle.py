@@ -291,3 +291,98 @@ def dequant_model(model: dict):
         layers.append(d)
     t, raw, n, kk = model["embed"]
     return layers, model["out_norm"], dequantize(t, raw, n * kk).reshape(n, kk)
+
+
+# ---------------------------------------------------------------- sampler
+def logits_process(logits, temperature: float, top_p: float, top_k: int) -> np.ndarray:
+    """LogitsProcessor::process (src/x/provider/candle/lmhead.rs:42-111) on each
+    row of [rows, n] f32 logits, in the reference's order and arithmetic:
+    apply_temperature (:55-60) l / max(t, 0.001); apply_top_p (:63-84) the
+    descending-order sequential f32 sum of min(exp(l), 1) (f32 exp: numpy's,
+    the reference's is the platform libm's) until it reaches top_p, whose logit
+    is the threshold (0.0 if never reached); apply_top_k (:87-101) the
+    (top_k+1)-th largest logit after top-p; logits below a threshold -> -inf."""
+    x = np.array(logits, dtype=np.float32, copy=True)
+    rows = x.reshape(1, -1) if x.ndim == 1 else x
+    t = np.float32(max(np.float32(temperature), np.float32(0.001)))
+    rows /= t
+    for r in rows:
+        s = np.sort(r)[::-1]
+        with np.errstate(over="ignore"):                # exp overflows to inf, then min(., 1) = 1
+            c = np.minimum(np.exp(s), np.float32(1.0)).astype(np.float32)
+        cum = np.cumsum(c, dtype=np.float32)          # sequential f32 adds
+        hit = np.nonzero(cum >= np.float32(top_p))[0]
+        tp = s[hit[0]] if hit.size else np.float32(0.0)
+        r[r < tp] = -np.inf
+        if 0 < top_k < r.size:
+            tk = np.sort(r)[::-1][top_k]
+            r[r < tk] = -np.inf
+    return x
+
+
+_PHILOX_M = (0xD2511F53, 0xCD9E8D57)
+_PHILOX_W = (0x9E3779B9, 0xBB67AE85)
+
+
+def philox4x32_10(ctr, key) -> tuple:
+    """Philox4x32-10 (Salmon, Moraes, Dror, Shaw, SC'11; the Random123 round:
+    (hi(M1 c2) ^ c1 ^ k0, lo(M1 c2), hi(M0 c0) ^ c3 ^ k1, lo(M0 c0)), key
+    bumped by the Weyl constants after each of 10 rounds)."""
+    c = [int(v) & 0xFFFFFFFF for v in ctr]
+    k = [int(v) & 0xFFFFFFFF for v in key]
+    for _ in range(10):
+        p0, p1 = _PHILOX_M[0] * c[0], _PHILOX_M[1] * c[2]
+        c = [((p1 >> 32) ^ c[1] ^ k[0]) & 0xFFFFFFFF, p1 & 0xFFFFFFFF,
+             ((p0 >> 32) ^ c[3] ^ k[1]) & 0xFFFFFFFF, p0 & 0xFFFFFFFF]
+        k = [(k[0] + _PHILOX_W[0]) & 0xFFFFFFFF, (k[1] + _PHILOX_W[1]) & 0xFFFFFFFF]
+    return tuple(c)
+
+
+def sample_uniform(seed: int, ctr: int) -> np.float32:
+    w = philox4x32_10((ctr & 0xFFFFFFFF, ctr >> 32, 0, 0), (seed & 0xFFFFFFFF, seed >> 32))[0]
+    return np.float32(w >> 8) * np.float32(1.0 / 16777216.0)
+
+
+def sample_rows(logits, seed: int, offset: int = 0, nt: int = 256):
+    """The draw of hd_sample_rows in the same f32 operation order: chunk sums
+    of exp(l - max) over nt contiguous chunks, their sequential exclusive
+    prefix, target = u * total, the walk of the chunk that holds it.  Returns
+    (indices, margins): margin = distance of the target to the nearest edge
+    of the drawn entry's interval, relative to the total (where the platform
+    exp's last-bit differences could move a draw)."""
+    x = np.asarray(logits, np.float32)
+    x = x.reshape(1, -1) if x.ndim == 1 else x
+    n = x.shape[1]
+    C_ = -(-n // nt)
+    idx, margin = [], []
+    for r, row in enumerate(x):
+        m = row.max()
+        if not np.isfinite(m):
+            idx.append(-1)
+            margin.append(np.inf)
+            continue
+        e = np.exp((row - m).astype(np.float32)).astype(np.float32)
+        sums = np.zeros(nt, np.float32)
+        for t in range(nt):
+            ch = e[t * C_:min(n, (t + 1) * C_)]
+            sums[t] = np.cumsum(ch, dtype=np.float32)[-1] if ch.size else np.float32(0)
+        pre = np.concatenate([[np.float32(0)], np.cumsum(sums, dtype=np.float32)]).astype(np.float32)
+        total = pre[-1]
+        target = np.float32(sample_uniform(seed, offset + r) * total)
+        if target >= total:
+            t = max(j for j in range(nt) if sums[j] > 0)
+        else:
+            t = next(j for j in range(nt) if pre[j] <= target < pre[j + 1])
+        ch = e[t * C_:min(n, (t + 1) * C_)]
+        acc = np.cumsum(np.concatenate([[pre[t]], ch]).astype(np.float32), dtype=np.float32)[1:]
+        pick, lo = -1, pre[t]
+        for i in range(ch.size):
+            if ch[i] > 0:
+                pick = t * C_ + i
+            if acc[i] > target and ch[i] > 0:
+                break
+            lo = acc[i]
+        hi = acc[pick - t * C_] if pick >= 0 else lo
+        idx.append(pick)
+        margin.append(float(min(target - lo, hi - target)) / float(total))
+    return np.array(idx, np.int32), np.array(margin)
