@@ -72,7 +72,7 @@ __global__ void k_rope_kv_append(float *qkv, int64_t ld, const int32_t *__restri
 }
 
 // rows: query rows; row r reads cache sequence cseq(r) with length len(r):
-//   decode  (lens != null): cseq = r, len = lens[r]
+//   decode  (lens != null): cseq = slots ? slots[r] : r, len = lens[r]
 //   prefill (lens == null): rows are seqT consecutive tokens per sequence,
 //                           cseq = r / seqT, len = pos0 + r % seqT + 1
 constexpr int CH = 64;     // positions per chunk
@@ -84,7 +84,7 @@ __global__ void __launch_bounds__(ANT) k_attention(const float *__restrict__ q, 
                                                    const float *__restrict__ vc, const int32_t *__restrict__ lens,
                                                    int pos0, int seqT, int n_heads, int n_kv, int max_ctx,
                                                    float scale, int P, int cpc, float *ws, int *tickets,
-                                                   float *__restrict__ out) {
+                                                   const int32_t *__restrict__ slots, float *__restrict__ out) {
     extern __shared__ float sm[];
     constexpr int KP = HD + 1;                      // padded K row
     constexpr int OPT = (MAXREP * HD + ANT - 1) / ANT;
@@ -92,7 +92,7 @@ __global__ void __launch_bounds__(ANT) k_attention(const float *__restrict__ q, 
     pdl_trigger();
     const int r = blockIdx.x, kvh = blockIdx.y, p = blockIdx.z;
     const int rep = n_heads / n_kv, h0 = kvh * rep;
-    const int cseq = lens ? r : r / seqT;
+    const int cseq = lens ? (slots ? slots[r] : r) : r / seqT;
     int L = lens ? lens[r] : pos0 + r % seqT + 1;
     L = L < 0 ? 0 : L > max_ctx ? max_ctx : L;
     const int nchunks = (L + CH - 1) / CH;
@@ -248,7 +248,7 @@ size_t attn_smem(int rep) {
 template <int HD>
 cudaError_t launch_attn(hd_ctx *ctx, int rows, int n_heads, int n_kv, int P, int cpc, const float *q, int64_t qld,
                         const float *kc, const float *vc, const int32_t *lens, int pos0, int seqT, int max_ctx,
-                        float *out) {
+                        const int32_t *slots, float *out) {
     const int rep = n_heads / n_kv;
     const size_t smem = attn_smem<HD>(rep);
     if (smem > 48 * 1024) {
@@ -257,14 +257,14 @@ cudaError_t launch_attn(hd_ctx *ctx, int rows, int n_heads, int n_kv, int P, int
     }
     const float scale = sqrtf((float)HD);
     return hd_launch(ctx, k_attention<HD>, dim3(rows, n_kv, P), dim3(ANT), smem, q, qld, kc, vc, lens, pos0, seqT,
-                     n_heads, n_kv, max_ctx, scale, P, cpc, (float *)ctx->ws, ctx->tickets, out);
+                     n_heads, n_kv, max_ctx, scale, P, cpc, (float *)ctx->ws, ctx->tickets, slots, out);
 }
 
 }  // namespace
 
 int hd_attention_run(hd_ctx *ctx, const float *q, int64_t qld, const float *kc, const float *vc, const int32_t *lens,
                      int rows, int pos0, int seqT, int n_heads, int n_kv, int hd, int max_ctx, int maxlen, float *out,
-                     const char *name) {
+                     const char *name, const int32_t *slots) {
     if (!ctx || !q || !kc || !vc || !out) return hd_fail(ctx, HD_E_ARG, "%s: null argument", name);
     HD_REQUIRE(ctx, n_heads > 0 && n_kv > 0 && n_heads % n_kv == 0 && n_heads / n_kv <= MAXREP, HD_E_SHAPE,
                "%s: n_heads %d must be a multiple of n_kv %d, at most %d per kv head", name, n_heads, n_kv, MAXREP);
@@ -290,10 +290,10 @@ int hd_attention_run(hd_ctx *ctx, const float *q, int64_t qld, const float *kc, 
     }
     cudaError_t e;
     if (qld == 0) qld = (int64_t)n_heads * hd;
-    if (hd == 64) e = launch_attn<64>(ctx, rows, n_heads, n_kv, P, cpc, q, qld, kc, vc, lens, pos0, seqT, max_ctx, out);
+    if (hd == 64) e = launch_attn<64>(ctx, rows, n_heads, n_kv, P, cpc, q, qld, kc, vc, lens, pos0, seqT, max_ctx, slots, out);
     else if (hd == 128)
-        e = launch_attn<128>(ctx, rows, n_heads, n_kv, P, cpc, q, qld, kc, vc, lens, pos0, seqT, max_ctx, out);
-    else e = launch_attn<32>(ctx, rows, n_heads, n_kv, P, cpc, q, qld, kc, vc, lens, pos0, seqT, max_ctx, out);
+        e = launch_attn<128>(ctx, rows, n_heads, n_kv, P, cpc, q, qld, kc, vc, lens, pos0, seqT, max_ctx, slots, out);
+    else e = launch_attn<32>(ctx, rows, n_heads, n_kv, P, cpc, q, qld, kc, vc, lens, pos0, seqT, max_ctx, slots, out);
     if (e != cudaSuccess) return hd_fail(ctx, HD_E_CUDA, "%s: %s", name, cudaGetErrorString(e));
     return HD_OK;
 }

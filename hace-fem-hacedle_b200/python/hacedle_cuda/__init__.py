@@ -34,6 +34,9 @@ EXPORTS = [
     "hd_gguf_open", "hd_gguf_open_memory", "hd_gguf_close", "hd_gguf_error", "hd_gguf_counts", "hd_gguf_tensor",
     "hd_gguf_find_tensor", "hd_gguf_kv", "hd_gguf_find_key", "hd_gguf_kv_int", "hd_gguf_kv_float", "hd_gguf_kv_string",
     "hd_gguf_kv_array", "hd_gguf_upload", "hd_logits_process", "hd_sample_rows",
+    "hd_kv_arena_create", "hd_kv_arena_free", "hd_kv_layer", "hd_kv_allocate", "hd_kv_release", "hd_kv_session",
+    "hd_kv_advance", "hd_kv_soul_sessions", "hd_kv_snapshot", "hd_kv_restore", "hd_kv_snapshot_free",
+    "hd_kv_append_slots", "hd_attention_decode_slots",
 ]
 
 
@@ -86,6 +89,13 @@ def lib() -> C.CDLL:
         "hd_gguf_kv_string": [V, I64, C.c_uint64, V, V], "hd_gguf_kv_array": [V, I64, V, V],
         "hd_gguf_upload": [V, V, C.c_char_p, C.POINTER(V)],
         "hd_logits_process": [V, V, I64, I64, F, F, I64], "hd_sample_rows": [V, V, I64, I64, C.c_uint64, C.c_uint64, V],
+        "hd_kv_arena_create": [V, I, I, I, I, I, C.POINTER(V)], "hd_kv_arena_free": [V], "hd_kv_layer": [V, I, V, V],
+        "hd_kv_allocate": [V, C.c_char_p, C.c_char_p, V], "hd_kv_release": [V, C.c_char_p],
+        "hd_kv_session": [V, C.c_char_p, V, V], "hd_kv_advance": [V, C.c_char_p, I],
+        "hd_kv_soul_sessions": [V, C.c_char_p, V], "hd_kv_snapshot": [V, C.c_char_p, V],
+        "hd_kv_restore": [V, V, C.c_char_p], "hd_kv_snapshot_free": [V, V],
+        "hd_kv_append_slots": [V, V, V, V, V, V, V, I, I, I, I],
+        "hd_attention_decode_slots": [V, V, V, V, V, V, I, I, I, I, I, V],
     }
     for name, args in sig.items():
         fn = getattr(L, name)
@@ -315,6 +325,86 @@ class _DecCfg(C.Structure):
 class _LayerW(C.Structure):
     _fields_ = [(n, C.c_void_p) for n in ("wq", "wk", "wv", "wo", "wg", "wu", "wd", "bq", "bk", "bv", "attn_norm",
                                            "ffn_norm")]
+
+
+class KvSnapshot(C.Structure):
+    """hd_kv_snapshot_t (KvSnapshot)."""
+    _fields_ = [("snapshot_id", C.c_uint64), ("token_position", C.c_int32), ("slot", C.c_int32),
+                ("kv_offset", C.c_uint64), ("timestamp", C.c_uint64)]
+
+
+class KvArena:
+    """hd_kv_arena: the device KV-cache manager (KvCacheManager over a pool of
+    `slots` KV slots, K and V [layers][slots][max_ctx][n_kv][head_dim] f32)."""
+
+    def __init__(self, ctx: "Context", layers: int, n_kv: int, head_dim: int, max_ctx: int, slots: int):
+        self.ctx, self.layers, self.n_kv, self.head_dim, self.max_ctx, self.slots = \
+            ctx, layers, n_kv, head_dim, max_ctx, slots
+        h = V()
+        ctx._check(lib().hd_kv_arena_create(ctx.h, layers, n_kv, head_dim, max_ctx, slots, C.byref(h)))
+        self.h = h
+
+    def layer(self, li: int):
+        """(k, v) device addresses of layer li's [slots][max_ctx][n_kv][head_dim] blocks."""
+        k, v = V(), V()
+        self.ctx._check(lib().hd_kv_layer(self.h, li, C.byref(k), C.byref(v)))
+        return k.value, v.value
+
+    def allocate(self, session: str, soul: str) -> int:
+        s = C.c_int()
+        self.ctx._check(lib().hd_kv_allocate(self.h, session.encode(), soul.encode(), C.byref(s)))
+        return s.value
+
+    def release(self, session: str):
+        self.ctx._check(lib().hd_kv_release(self.h, session.encode()))
+
+    def session(self, session: str):
+        """(slot, position)."""
+        s, p = C.c_int(), C.c_int()
+        self.ctx._check(lib().hd_kv_session(self.h, session.encode(), C.byref(s), C.byref(p)))
+        return s.value, p.value
+
+    def advance(self, session: str, count: int):
+        self.ctx._check(lib().hd_kv_advance(self.h, session.encode(), count))
+
+    def soul_sessions(self, soul: str) -> int:
+        n = C.c_int()
+        self.ctx._check(lib().hd_kv_soul_sessions(self.h, soul.encode(), C.byref(n)))
+        return n.value
+
+    def snapshot(self, session: str) -> KvSnapshot:
+        s = KvSnapshot()
+        self.ctx._check(lib().hd_kv_snapshot(self.h, session.encode(), C.byref(s)))
+        return s
+
+    def restore(self, snap: KvSnapshot, session: str):
+        self.ctx._check(lib().hd_kv_restore(self.h, C.byref(snap), session.encode()))
+
+    def snapshot_free(self, snap: KvSnapshot):
+        self.ctx._check(lib().hd_kv_snapshot_free(self.h, C.byref(snap)))
+
+    def append(self, li: int, k, v, slots, pos):
+        """Rows of k, v [rows, n_kv * head_dim] into layer li at (slots[r], pos[r])."""
+        kc, vc = self.layer(li)
+        self.ctx._check(lib().hd_kv_append_slots(self.ctx.h, _ptr(k), _ptr(v), kc, vc, _ptr(slots), _ptr(pos),
+                                                 k.shape[0], self.n_kv, self.head_dim, self.max_ctx))
+
+    def attention(self, li: int, q, slots, lens, n_heads: int, out):
+        kc, vc = self.layer(li)
+        self.ctx._check(lib().hd_attention_decode_slots(self.ctx.h, _ptr(q), kc, vc, _ptr(slots), _ptr(lens),
+                                                        q.shape[0], n_heads, self.n_kv, self.head_dim, self.max_ctx,
+                                                        _ptr(out)))
+
+    def free(self):
+        if getattr(self, "h", None) and getattr(self.ctx, "h", None):
+            lib().hd_kv_arena_free(self.h)
+        self.h = None
+
+    def __del__(self):
+        try:
+            self.free()
+        except Exception:
+            pass
 
 
 class Decoder:

@@ -269,6 +269,55 @@ int hd_logits_process(hd_ctx *ctx, float *logits_dev, int64_t rows, int64_t n, f
 int hd_sample_rows(hd_ctx *ctx, const float *logits_dev, int64_t rows, int64_t n, uint64_t seed,
                    uint64_t offset, int32_t *idx_dev);
 
+/* -------------------------------------------------------- KV-cache arena */
+/* The device KV-cache manager (runtime/kv_cache.rs: KvArena :8-34, SessionKv
+ * :37-56, SoulKv / SoulMemoryRegistry :58-118, KvCacheManager :121-127).
+ * The arena is `slots` KV slots in HBM, K and V each
+ * [layers][slots][max_ctx][n_kv][head_dim] f32 (hd_kv_layer gives one
+ * layer's [slots][max_ctx][n_kv][head_dim] block).  Sessions (by id, under a
+ * soul id) and snapshots each hold one slot.  KvError: SessionNotFound /
+ * SoulNotFound -> HD_E_ARG, ContextFull -> HD_E_SHAPE, AllocationFailed ->
+ * HD_E_OOM (message names the case).  An arena is used from its context's
+ * thread, like the context. */
+typedef struct hd_kv_arena hd_kv_arena;
+typedef struct {            /* KvSnapshot (kv_cache.rs:83-88)                   */
+    uint64_t snapshot_id;
+    int32_t token_position; /* positions copied                                 */
+    int32_t slot;           /* the slot holding the copy                        */
+    uint64_t kv_offset;     /* byte offset of that slot within a layer's block  */
+    uint64_t timestamp;     /* logical clock of the arena (one tick per snapshot) */
+} hd_kv_snapshot_t;
+
+int hd_kv_arena_create(hd_ctx *ctx, int layers, int n_kv, int head_dim, int max_ctx, int slots,
+                       hd_kv_arena **out);
+int hd_kv_arena_free(hd_kv_arena *arena);
+int hd_kv_layer(hd_kv_arena *arena, int layer, float **k_dev, float **v_dev);
+/* KvCacheManager::allocate / SoulKv::get_or_create_session: the session's
+ * slot (an existing session keeps its slot and position). */
+int hd_kv_allocate(hd_kv_arena *arena, const char *session_id, const char *soul_id, int *slot);
+int hd_kv_release(hd_kv_arena *arena, const char *session_id);
+int hd_kv_session(hd_kv_arena *arena, const char *session_id, int *slot, int *position);
+/* KvCacheManager::append: the session's position advances by `count`
+ * (ContextFull beyond max_ctx, position unchanged). */
+int hd_kv_advance(hd_kv_arena *arena, const char *session_id, int count);
+int hd_kv_soul_sessions(hd_kv_arena *arena, const char *soul_id, int *count);
+/* KvCacheManager::snapshot / restore: copy the session's cached positions
+ * (every layer, K and V) into a free slot / back into `session_id` (created
+ * under the snapshot's soul if new: a branch), whose position becomes the
+ * snapshot's.  Snapshots stay valid until hd_kv_snapshot_free. */
+int hd_kv_snapshot(hd_kv_arena *arena, const char *session_id, hd_kv_snapshot_t *out);
+int hd_kv_restore(hd_kv_arena *arena, const hd_kv_snapshot_t *snap, const char *session_id);
+int hd_kv_snapshot_free(hd_kv_arena *arena, const hd_kv_snapshot_t *snap);
+/* Slot-indexed device ops on one layer's block: row r's k/v appended to slot
+ * slots[r] at pos[r]; decode attention of row r over slot slots[r]'s first
+ * len[r] positions (otherwise as hd_attention_decode). */
+int hd_kv_append_slots(hd_ctx *ctx, const float *k_dev, const float *v_dev, float *kc_dev, float *vc_dev,
+                       const int32_t *slots_dev, const int32_t *pos_dev, int rows, int n_kv, int head_dim,
+                       int max_ctx);
+int hd_attention_decode_slots(hd_ctx *ctx, const float *q_dev, const float *kc_dev, const float *vc_dev,
+                              const int32_t *slots_dev, const int32_t *len_dev, int rows, int n_heads, int n_kv,
+                              int head_dim, int max_ctx, float *out_dev);
+
 /* ------------------------------------------------------------ GGUF reader */
 /* Replaces GgufLoader::load_std, GgufTensorIndex::parse and tensor_bytes
  * (src/x/loader/gguf/loader.rs:64-141, tensor_index.rs:24-170, header.rs:54-84)
