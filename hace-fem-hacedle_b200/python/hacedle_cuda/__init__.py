@@ -36,7 +36,7 @@ EXPORTS = [
     "hd_gguf_kv_array", "hd_gguf_upload", "hd_logits_process", "hd_sample_rows",
     "hd_kv_arena_create", "hd_kv_arena_free", "hd_kv_layer", "hd_kv_allocate", "hd_kv_release", "hd_kv_session",
     "hd_kv_advance", "hd_kv_soul_sessions", "hd_kv_snapshot", "hd_kv_restore", "hd_kv_snapshot_free",
-    "hd_kv_append_slots", "hd_attention_decode_slots",
+    "hd_kv_append_slots", "hd_attention_decode_slots", "hd_quantize_q8_1", "hd_qgemv_q8_1",
 ]
 
 
@@ -96,6 +96,7 @@ def lib() -> C.CDLL:
         "hd_kv_restore": [V, V, C.c_char_p], "hd_kv_snapshot_free": [V, V],
         "hd_kv_append_slots": [V, V, V, V, V, V, V, I, I, I, I],
         "hd_attention_decode_slots": [V, V, V, V, V, V, I, I, I, I, I, V],
+        "hd_quantize_q8_1": [V, V, I, I64, V], "hd_qgemv_q8_1": [V, V, V, V, I],
     }
     for name, args in sig.items():
         fn = getattr(L, name)
@@ -197,6 +198,14 @@ class Context:
         return Weight(self, ggml_type, raw, rows, cols)
 
     # ---- kernels (device tensors) ----
+    def quantize_q8_1(self, x, blocks):
+        """x [B, K] f32 -> blocks (uint8 device tensor of B*K/32*48 bytes)."""
+        B, K = x.shape
+        self._check(lib().hd_quantize_q8_1(self.h, _ptr(x), B, K, _ptr(blocks)))
+
+    def qgemv_q8_1(self, w: Weight, blocks, y, B: int):
+        self._check(lib().hd_qgemv_q8_1(self.h, w.h, _ptr(blocks), _ptr(y), B))
+
     def logits_process(self, logits, temperature: float, top_p: float, top_k: int):
         """LogitsProcessor::process in place on a [rows, n] device tensor."""
         rows, n = (1, logits.numel()) if logits.dim() == 1 else logits.shape

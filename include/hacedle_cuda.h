@@ -254,6 +254,20 @@ int hd_decoder_generate(hd_decoder *dec, const int32_t *prompts_host, int seqs, 
                         int n_gen, int prefill_precision, int32_t *out_host, float *decode_ms_out,
                         float *prefill_ms_out);
 
+/* ------------------------------------------------------ Q8_1 integer path */
+/* Activations as 8-bit blocks of 32 (48 bytes each, 16-byte aligned):
+ * int8 q[32]; float d; int16 s0, s1; 4 bytes zero -- d = max|x| / 127,
+ * q = round-half-even(x * (1/d)), s0 / s1 = sum of q over values 0-15 / 16-31.
+ * blocks_dev holds B * K / 32 blocks, row b's blocks contiguous. */
+int hd_quantize_q8_1(hd_ctx *ctx, const float *x_dev, int B, int64_t K, void *blocks_dev);
+/* y[b][n] = sum over 32-value units of d_x (a_0 dot_0 - o_0 s0 + a_1 dot_1 - o_1 s1),
+ * dot_h the int32 dot of the weight's small-integer quants with q over half h
+ * (dp4a), w = a_h q - o_h per half (Q8_0: d, 0; Q5_0: d, 16d; Q4_K: d sc,
+ * dmin m; Q6_K: d sc_h, 32 d sc_h).  B 1..16.  Accuracy: the 2e-2 relative
+ * contract of the bf16 path (activations rounded to 1/254 of a block's range).
+ * The next step after the reference's i8 ops (ops/q_ops.rs:11-13). */
+int hd_qgemv_q8_1(hd_ctx *ctx, const hd_weight *w, const void *blocks_dev, float *y_dev, int B);
+
 /* ---------------------------------------------------------------- sampler */
 /* LogitsProcessor::process (src/x/provider/candle/lmhead.rs:42-111) in place on
  * rows x n logits, with the reference's definitions: l /= max(temperature,

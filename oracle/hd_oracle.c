@@ -571,3 +571,111 @@ int hdo_decoder_generate(const hdo_model_cfg *c, const hdo_layer_w *L, const flo
     free(kc); free(vc); free(ws); free(logits);
     return 0;
 }
+
+/* ---------------------------------------------------------------- Q8_1 path
+ * The integer activation path of libhacedle_cuda (no reference counterpart;
+ * it follows on the i8 ops of ops/q_ops.rs:11-13).  Blocks of 32 activations:
+ * d = max|x| / 127, q = rint(x * (1/d)) (round half to even; 0 for a zero
+ * block), s0 / s1 = sum of q over values 0-15 / 16-31. */
+void hdo_quantize_q8_1(const float *x, int64_t nblocks, int8_t *q, float *d, int32_t *s) {
+    for (int64_t b = 0; b < nblocks; b++) {
+        const float *v = x + b * 32;
+        float m = 0.f;
+        for (int j = 0; j < 32; j++) m = fabsf(v[j]) > m ? fabsf(v[j]) : m;
+        float db = m / 127.f, id = db > 0.f ? 1.f / db : 0.f;
+        int s0 = 0, s1 = 0;
+        for (int j = 0; j < 32; j++) {
+            int qq = (int)nearbyintf(v[j] * id);
+            q[b * 32 + j] = (int8_t)qq;
+            if (j < 16) s0 += qq; else s1 += qq;
+        }
+        d[b] = db;
+        s[2 * b] = s0;
+        s[2 * b + 1] = s1;
+    }
+}
+
+/* Unit u (32 values) of a row of GGUF blocks as small integers q[32] with
+ * per-half scale a and offset o (w = a q - o), the decomposition the device
+ * kernel uses: Q8_0 (q, d, 0); Q5_0 (q5, d, 16 d); Q4_K (q4, d sc, dmin m);
+ * Q6_K (q6 unsigned, d sc_h, 32 d sc_h). */
+static int unit_ints(int type, const uint8_t *row, int u, int q[32], float a[2], float o[2]) {
+    if (type == 8) {
+        const uint8_t *blk = row + (size_t)u * 34;
+        float d = hdo_f16_to_f32(rd16(blk));
+        for (int j = 0; j < 32; j++) q[j] = (int8_t)blk[2 + j];
+        a[0] = a[1] = d;
+        o[0] = o[1] = 0.f;
+    } else if (type == 6) {
+        const uint8_t *blk = row + (size_t)u * 22;
+        float d = hdo_f16_to_f32(rd16(blk));
+        uint32_t qh = rd32(blk + 2);
+        for (int j = 0; j < 32; j++) {
+            uint32_t ql = j < 16 ? (blk[6 + j] & 0x0Fu) : (blk[6 + j - 16] >> 4);
+            q[j] = (int)(ql | (((qh >> j) & 1u) << 4));
+        }
+        a[0] = a[1] = d;
+        o[0] = o[1] = 16.f * d;
+    } else if (type == 12) {
+        const uint8_t *blk = row + (size_t)(u / 8) * 144;
+        const int uu = u % 8, c = uu / 2, hi = uu % 2;
+        float d = hdo_f16_to_f32(rd16(blk)), dmin = hdo_f16_to_f32(rd16(blk + 2));
+        uint8_t sc, mn;
+        q4k_scale_min(uu, blk + 4, &sc, &mn);
+        for (int l = 0; l < 32; l++) {
+            uint8_t byte = blk[16 + 32 * c + l];
+            q[l] = hi ? (byte >> 4) : (byte & 0x0F);
+        }
+        a[0] = a[1] = d * (float)sc;
+        o[0] = o[1] = dmin * (float)mn;
+    } else if (type == 14) {
+        const uint8_t *blk = row + (size_t)(u / 8) * 210;
+        const uint8_t *ql = blk, *qh = blk + 128;
+        const int8_t *sc = (const int8_t *)(blk + 192);
+        float d = hdo_f16_to_f32(rd16(blk + 208));
+        const int uu = u % 8;
+        for (int l = 0; l < 32; l++) {
+            int e = 32 * uu + l, h = e / 128, k = (e % 128) / 32, ll = e % 32;
+            uint8_t lb = ql[64 * h + 32 * (k & 1) + ll];
+            uint32_t lo = (k < 2) ? (lb & 0x0Fu) : (lb >> 4);
+            uint32_t hb = (qh[32 * h + ll] >> (2 * k)) & 3u;
+            q[l] = (int)(lo | (hb << 4));
+        }
+        a[0] = d * (float)sc[2 * uu];
+        a[1] = d * (float)sc[2 * uu + 1];
+        o[0] = 32.f * a[0];
+        o[1] = 32.f * a[1];
+    } else {
+        return -1;
+    }
+    return 0;
+}
+
+/* y[b][r] = sum over units (in order) of dx (a0 dot0 - o0 s0 + a1 dot1 - o1 s1). */
+int hdo_qgemv_q8_1(int type, const uint8_t *W, int64_t N, int64_t K, const int8_t *xq, const float *xd,
+                   const int32_t *xs, int B, float *y) {
+    int be, bb;
+    if (hdo_type_block(type, &be, &bb) != 0) return -1;
+    const int64_t units = K / 32, row_bytes = K / be * bb;
+    int q[32];
+    float a[2], o[2];
+    for (int64_t r = 0; r < N; r++) {
+        const uint8_t *row = W + r * row_bytes;
+        for (int b = 0; b < B; b++) {
+            float acc = 0.f;
+            for (int64_t u = 0; u < units; u++) {
+                if (unit_ints(type, row, (int)u, q, a, o) != 0) return -1;
+                const int8_t *x = xq + ((int64_t)b * units + u) * 32;
+                int d0 = 0, d1 = 0;
+                for (int j = 0; j < 16; j++) d0 += q[j] * x[j];
+                for (int j = 16; j < 32; j++) d1 += q[j] * x[j];
+                const int32_t *s = xs + 2 * ((int64_t)b * units + u);
+                float h0 = a[0] * (float)d0 - o[0] * (float)s[0];
+                float h1 = a[1] * (float)d1 - o[1] * (float)s[1];
+                acc = acc + xd[(int64_t)b * units + u] * (h0 + h1);
+            }
+            y[(int64_t)b * N + r] = acc;
+        }
+    }
+    return 0;
+}

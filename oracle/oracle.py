@@ -70,6 +70,9 @@ def lib():
         L.hdo_dot_i8.argtypes = [_i8p, _i8p, C.c_int64]
         L.hdo_fused_qdot_qadd_qacc_i8.restype = C.c_int32
         L.hdo_fused_qdot_qadd_qacc_i8.argtypes = [_i8p, _i8p, C.c_int64, C.c_int32, _i32p]
+        L.hdo_quantize_q8_1.argtypes = [_f32p, C.c_int64, _i8p, _f32p, _i32p]
+        L.hdo_qgemv_q8_1.restype = C.c_int
+        L.hdo_qgemv_q8_1.argtypes = [C.c_int, _u8p, C.c_int64, C.c_int64, _i8p, _f32p, _i32p, C.c_int, _f32p]
         L.hdo_decoder_generate.restype = C.c_int
         L.hdo_decoder_generate.argtypes = [C.c_void_p, C.c_void_p, _f32p, _f32p, _i32p, C.c_int,
                                            C.c_int, _i32p, _f32p, C.c_int]
@@ -386,3 +389,28 @@ def sample_rows(logits, seed: int, offset: int = 0, nt: int = 256):
         idx.append(pick)
         margin.append(float(min(target - lo, hi - target)) / float(total))
     return np.array(idx, np.int32), np.array(margin)
+
+
+# ---------------------------------------------------------------- Q8_1 path
+def quantize_q8_1(X):
+    """X [B, K] f32 -> (q int8 [B, K], d f32 [B, K/32], s int32 [B, K/32, 2])."""
+    X = np.ascontiguousarray(X, np.float32)
+    B, K = X.shape
+    nb = B * (K // 32)
+    q = np.zeros(B * K, np.int8)
+    d = np.zeros(nb, np.float32)
+    s = np.zeros(2 * nb, np.int32)
+    lib().hdo_quantize_q8_1(_p(X, _f32p), nb, _p(q, _i8p), _p(d, _f32p), _p(s, _i32p))
+    return q.reshape(B, K), d.reshape(B, K // 32), s.reshape(B, K // 32, 2)
+
+
+def qgemv_q8_1(ggml_type: int, raw, N: int, K: int, q, d, s) -> np.ndarray:
+    """Y [B, N] of the integer path over GGUF blocks and quantized activations."""
+    raw = np.ascontiguousarray(raw, np.uint8)
+    q, d, s = (np.ascontiguousarray(a) for a in (q, d, s))
+    B = q.shape[0]
+    y = np.zeros((B, N), np.float32)
+    rc = lib().hdo_qgemv_q8_1(ggml_type, _p(raw, _u8p), N, K, _p(q, _i8p), _p(d, _f32p), _p(s, _i32p), B,
+                              _p(y, _f32p))
+    assert rc == 0
+    return y
