@@ -84,7 +84,9 @@ __global__ void __launch_bounds__(ANT) k_attention(const float *__restrict__ q, 
                                                    const float *__restrict__ vc, const int32_t *__restrict__ lens,
                                                    int pos0, int seqT, int n_heads, int n_kv, int max_ctx,
                                                    float scale, int P, int cpc, float *ws, int *tickets,
-                                                   const int32_t *__restrict__ slots, float *__restrict__ out) {
+                                                   const int32_t *__restrict__ slots, const float *__restrict__ rfreq,
+                                                   const int32_t *__restrict__ rpos, float *kcw, float *vcw,
+                                                   float *__restrict__ out) {
     extern __shared__ float sm[];
     constexpr int KP = HD + 1;                      // padded K row
     constexpr int OPT = (MAXREP * HD + ANT - 1) / ANT;
@@ -104,8 +106,48 @@ __global__ void __launch_bounds__(ANT) k_attention(const float *__restrict__ q, 
     float *Vs = sm + ((rep * KP + CH * KP + 3) & ~3);      // [CH][HD], 16-byte aligned for float4 stores
     float *S = Vs + CH * HD;                               // [rep][CH]
     float *mrun = S + rep * CH, *lrun = mrun + MAXREP, *alpha = lrun + MAXREP;
+    float *knew = alpha + MAXREP, *vnew = knew + HD;       // fused decode: the new position's k and v
     const float *qr = q + (int64_t)r * qld + (int64_t)h0 * HD;
-    for (int i = tid; i < rep * HD; i += ANT) qs[(i / HD) * KP + i % HD] = qr[i];
+    // Fused decode (rfreq != null): q of the fused q|k|v row is rotated here
+    // (NEOX RoPE with the arithmetic of k_rope_kv_append), and the CTA whose
+    // chunk holds the new position rotates this kv head's k, appends k and v
+    // to the cache, and uses them from shared memory for that position.
+    const bool fused = rfreq != nullptr;
+    const int pn = fused ? rpos[r] : -1;
+    const bool owner = fused && pn >= 0 && pn < L && (pn / CH) / cpc == p;
+    if (fused) {
+        constexpr int half = HD / 2;
+        for (int i = tid; i < rep * half; i += ANT) {
+            const int h = i / half, d = i % half;
+            const float angle = __fdiv_rn((float)pn, rfreq[d]);
+            const float c = cosf(angle), sn = sinf(angle);
+            const float x0 = qr[h * HD + d], x1 = qr[h * HD + d + half];
+            qs[h * KP + d] = __fsub_rn(__fmul_rn(x0, c), __fmul_rn(x1, sn));
+            qs[h * KP + d + half] = __fadd_rn(__fmul_rn(x0, sn), __fmul_rn(x1, c));
+        }
+        if (owner) {
+            const float *kr = q + (int64_t)r * qld + (int64_t)(n_heads + kvh) * HD;
+            const float *vr = q + (int64_t)r * qld + (int64_t)(n_heads + n_kv + kvh) * HD;
+            const int64_t dst = (((int64_t)cseq * max_ctx + pn) * n_kv + kvh) * HD;
+            for (int d = tid; d < half; d += ANT) {
+                const float angle = __fdiv_rn((float)pn, rfreq[d]);
+                const float c = cosf(angle), sn = sinf(angle);
+                const float x0 = kr[d], x1 = kr[d + half];
+                const float y0 = __fsub_rn(__fmul_rn(x0, c), __fmul_rn(x1, sn));
+                const float y1 = __fadd_rn(__fmul_rn(x0, sn), __fmul_rn(x1, c));
+                knew[d] = y0;
+                knew[d + half] = y1;
+                kcw[dst + d] = y0;
+                kcw[dst + d + half] = y1;
+            }
+            for (int d = tid; d < HD; d += ANT) {
+                vnew[d] = vr[d];
+                vcw[dst + d] = vr[d];
+            }
+        }
+    } else {
+        for (int i = tid; i < rep * HD; i += ANT) qs[(i / HD) * KP + i % HD] = qr[i];
+    }
     if (tid < rep) {
         mrun[tid] = -INFINITY;
         lrun[tid] = 0.f;
@@ -146,6 +188,14 @@ __global__ void __launch_bounds__(ANT) k_attention(const float *__restrict__ q, 
             }
         }
         __syncthreads();
+        if (owner && c == pn / CH) {  // the new position, from shared memory (not re-read from the cache)
+            const int j = pn - j0;
+            for (int d = tid; d < HD; d += ANT) {
+                Ks[j * KP + d] = knew[d];
+                Vs[j * HD + d] = vnew[d];
+            }
+            __syncthreads();
+        }
         for (int i = tid; i < rep * nj; i += ANT) {
             const int h = i / nj, j = i % nj;
             const float *qh = qs + h * KP, *kj = Ks + j * KP;
@@ -242,13 +292,14 @@ __global__ void __launch_bounds__(ANT) k_attention(const float *__restrict__ q, 
 
 template <int HD>
 size_t attn_smem(int rep) {
-    return (size_t)(((rep * (HD + 1) + CH * (HD + 1) + 3) & ~3) + CH * HD + rep * CH + 3 * MAXREP) * sizeof(float);
+    return (size_t)(((rep * (HD + 1) + CH * (HD + 1) + 3) & ~3) + CH * HD + rep * CH + 3 * MAXREP + 2 * HD) *
+           sizeof(float);
 }
 
 template <int HD>
 cudaError_t launch_attn(hd_ctx *ctx, int rows, int n_heads, int n_kv, int P, int cpc, const float *q, int64_t qld,
                         const float *kc, const float *vc, const int32_t *lens, int pos0, int seqT, int max_ctx,
-                        const int32_t *slots, float *out) {
+                        const int32_t *slots, const float *rfreq, const int32_t *rpos, float *out) {
     const int rep = n_heads / n_kv;
     const size_t smem = attn_smem<HD>(rep);
     if (smem > 48 * 1024) {
@@ -257,14 +308,15 @@ cudaError_t launch_attn(hd_ctx *ctx, int rows, int n_heads, int n_kv, int P, int
     }
     const float scale = sqrtf((float)HD);
     return hd_launch(ctx, k_attention<HD>, dim3(rows, n_kv, P), dim3(ANT), smem, q, qld, kc, vc, lens, pos0, seqT,
-                     n_heads, n_kv, max_ctx, scale, P, cpc, (float *)ctx->ws, ctx->tickets, slots, out);
+                     n_heads, n_kv, max_ctx, scale, P, cpc, (float *)ctx->ws, ctx->tickets, slots, rfreq, rpos,
+                     (float *)kc, (float *)vc, out);
 }
 
 }  // namespace
 
 int hd_attention_run(hd_ctx *ctx, const float *q, int64_t qld, const float *kc, const float *vc, const int32_t *lens,
                      int rows, int pos0, int seqT, int n_heads, int n_kv, int hd, int max_ctx, int maxlen, float *out,
-                     const char *name, const int32_t *slots) {
+                     const char *name, const int32_t *slots, const float *rope_freq, const int32_t *rope_pos) {
     if (!ctx || !q || !kc || !vc || !out) return hd_fail(ctx, HD_E_ARG, "%s: null argument", name);
     HD_REQUIRE(ctx, n_heads > 0 && n_kv > 0 && n_heads % n_kv == 0 && n_heads / n_kv <= MAXREP, HD_E_SHAPE,
                "%s: n_heads %d must be a multiple of n_kv %d, at most %d per kv head", name, n_heads, n_kv, MAXREP);
@@ -290,10 +342,10 @@ int hd_attention_run(hd_ctx *ctx, const float *q, int64_t qld, const float *kc, 
     }
     cudaError_t e;
     if (qld == 0) qld = (int64_t)n_heads * hd;
-    if (hd == 64) e = launch_attn<64>(ctx, rows, n_heads, n_kv, P, cpc, q, qld, kc, vc, lens, pos0, seqT, max_ctx, slots, out);
+    if (hd == 64) e = launch_attn<64>(ctx, rows, n_heads, n_kv, P, cpc, q, qld, kc, vc, lens, pos0, seqT, max_ctx, slots, rope_freq, rope_pos, out);
     else if (hd == 128)
-        e = launch_attn<128>(ctx, rows, n_heads, n_kv, P, cpc, q, qld, kc, vc, lens, pos0, seqT, max_ctx, slots, out);
-    else e = launch_attn<32>(ctx, rows, n_heads, n_kv, P, cpc, q, qld, kc, vc, lens, pos0, seqT, max_ctx, slots, out);
+        e = launch_attn<128>(ctx, rows, n_heads, n_kv, P, cpc, q, qld, kc, vc, lens, pos0, seqT, max_ctx, slots, rope_freq, rope_pos, out);
+    else e = launch_attn<32>(ctx, rows, n_heads, n_kv, P, cpc, q, qld, kc, vc, lens, pos0, seqT, max_ctx, slots, rope_freq, rope_pos, out);
     if (e != cudaSuccess) return hd_fail(ctx, HD_E_CUDA, "%s: %s", name, cudaGetErrorString(e));
     return HD_OK;
 }

@@ -160,13 +160,14 @@ int layer_forward(hd_decoder *d, int li, int rows, const int32_t *pos, const int
         if (!rc)
             rc = gemv ? hd_qgemv_norm(ctx, l.wqkv, nullptr, d->h, l.attn_norm, c.eps, d->qkv, rows, l.bqkv, nullptr)
                       : linear(d, l.wqkv, d->xn, d->qkv, rows, l.bqkv, nullptr, prec);
-        if (!rc)
-            rc = hd_rope_kv_append(ctx, d->qkv, ld, pos, rows, lens ? 1 : T, c.n_heads, c.n_kv, hd, d->kc + lay,
-                                   d->vc + lay, c.max_ctx);
+        // decode: RoPE and the cache append run inside the attention kernel
+        if (!rc && !lens)
+            rc = hd_rope_kv_append(ctx, d->qkv, ld, pos, rows, T, c.n_heads, c.n_kv, hd, d->kc + lay, d->vc + lay,
+                                   c.max_ctx);
         if (rc) return rc;
         if (lens)
             rc = hd_attention_run(ctx, d->qkv, ld, d->kc + lay, d->vc + lay, lens, S, 0, 1, c.n_heads, c.n_kv, hd,
-                                  c.max_ctx, c.max_ctx, d->att, "decoder attention");
+                                  c.max_ctx, c.max_ctx, d->att, "decoder attention", nullptr, ctx->rope_freq, pos);
         else
             rc = hd_attention_run(ctx, d->qkv, ld, d->kc + lay, d->vc + lay, nullptr, rows, 0, T, c.n_heads, c.n_kv,
                                   hd, c.max_ctx, T, d->att, "decoder prefill attention");
@@ -390,6 +391,9 @@ extern "C" int hd_decoder_generate(hd_decoder *d, const int32_t *prompts, int S,
     float t_pre = 0.f, t_dec = 0.f;
     do {
         if ((rc = hd_ctx_reserve_workspace(ctx, (size_t)64 << 20))) break;
+        // the context's RoPE table may have been rebuilt for another head
+        // size since create (hd_rope_neox); the kernels below read it
+        if ((rc = hd_ensure_rope(ctx, c.head_dim, c.theta))) break;
         if ((rc = hd_ensure_hbuf(ctx, &ctx->scratch, &ctx->scratch_bytes, (size_t)2 * 16 * c.ffn * sizeof(float))))
             break;
         if (cudaMemcpyAsync(ids, prompts, (size_t)R * 4, cudaMemcpyHostToDevice, st) != cudaSuccess ||

@@ -111,7 +111,8 @@ int hd_qgemm_f32(hd_ctx *ctx, const hd_weight *w, const float *X, float *Y, int 
 // Attention over `rows` query rows (see k_attention in hd_attention.cu).
 int hd_attention_run(hd_ctx *ctx, const float *q, int64_t qld, const float *kc, const float *vc, const int32_t *lens,
                      int rows, int pos0, int seqT, int n_heads, int n_kv, int hd, int max_ctx, int maxlen, float *out,
-                     const char *name, const int32_t *slots = nullptr);
+                     const char *name, const int32_t *slots = nullptr, const float *rope_freq = nullptr,
+                     const int32_t *rope_pos = nullptr);
 // Q-GEMV (B <= 16) of rmsnorm(x) with the norm in each CTA's prologue;
 // w_up != null: SwiGLU pair.
 int hd_qgemv_norm(hd_ctx *ctx, const hd_weight *w, const hd_weight *w_up, const float *x, const float *norm_w,
