@@ -76,7 +76,7 @@ __global__ void k_rope_kv_append(float *qkv, int64_t ld, const int32_t *__restri
 //   prefill (lens == null): rows are seqT consecutive tokens per sequence,
 //                           cseq = r / seqT, len = pos0 + r % seqT + 1
 constexpr int CH = 64;     // positions per chunk
-constexpr int ANT = 128;   // threads per CTA
+constexpr int ANT = 512;   // threads per CTA: one score and one output chain each (rep x 64 <= 512 for rep <= 8)
 constexpr int MAXREP = 16;
 
 template <int HD>
