@@ -31,6 +31,7 @@
 #include <cstdlib>
 
 #include "hd_internal.cuh"
+#include "hd_units.cuh"
 
 namespace {
 
@@ -81,63 +82,6 @@ __device__ __forceinline__ void norm_scales(const float *__restrict__ x, int K, 
     }
     __syncthreads();
 }
-template <int TYPE>
-struct URegs;
-template <>
-struct URegs<HD_TYPE_Q8_0> { uint4 a, b; uint32_t d; };
-template <>
-struct URegs<HD_TYPE_Q5_0> { uint4 a; uint32_t qh, d; };
-template <>
-struct URegs<HD_TYPE_Q4_K> { uint4 a, m; };
-template <>
-struct URegs<HD_TYPE_Q6_K> { uint4 a, sc; uint2 h; uint32_t d; };
-
-template <int TYPE>
-__device__ __forceinline__ void load_unit(const WView &w, int64_t r, int u, URegs<TYPE> &g) {
-    const int64_t ur = (int64_t)u * w.rows + r;
-    if constexpr (TYPE == HD_TYPE_Q8_0) {
-        const uint4 *p = (const uint4 *)(w.q + ur * 32);
-        g.a = __ldg(p);
-        g.b = __ldg(p + 1);
-        g.d = __ldg((const unsigned short *)w.meta + ur);
-    } else if constexpr (TYPE == HD_TYPE_Q5_0) {
-        g.a = __ldg((const uint4 *)(w.q + ur * 16));
-        g.qh = __ldg((const unsigned int *)w.aux + ur);
-        g.d = __ldg((const unsigned short *)w.meta + ur);
-    } else if constexpr (TYPE == HD_TYPE_Q4_K) {
-        g.a = __ldg((const uint4 *)(w.q + ur * 16));
-        g.m = __ldg((const uint4 *)(w.meta + ((int64_t)(u >> 3) * w.rows + r) * 16));
-    } else {
-        const int64_t sr = (int64_t)(u >> 3) * w.rows + r;
-        g.a = __ldg((const uint4 *)(w.q + ur * 16));
-        g.h = __ldg((const uint2 *)w.aux + ur);
-        g.sc = __ldg((const uint4 *)(w.meta + sr * 16));
-        g.d = __ldg(w.dsb + sr);
-    }
-}
-
-template <int TYPE>
-__device__ __forceinline__ void zero_unit(URegs<TYPE> &g) {
-    if constexpr (TYPE == HD_TYPE_Q8_0) {
-        g.a = g.b = make_uint4(0, 0, 0, 0);
-        g.d = 0;
-    } else if constexpr (TYPE == HD_TYPE_Q5_0) {
-        g.a = make_uint4(0, 0, 0, 0);
-        g.qh = 0;
-        g.d = 0;
-    } else if constexpr (TYPE == HD_TYPE_Q4_K) {
-        g.a = g.m = make_uint4(0, 0, 0, 0);
-    } else {
-        g.a = g.sc = make_uint4(0, 0, 0, 0);
-        g.h = make_uint2(0, 0);
-        g.d = 0;
-    }
-}
-
-__device__ __forceinline__ uint32_t w4(const uint4 &v, int i) {
-    return i == 0 ? v.x : i == 1 ? v.y : i == 2 ? v.z : v.w;
-}
-__device__ __forceinline__ uint32_t shl_or_shr(uint32_t v, int s) { return s >= 0 ? (v << s) : (v >> -s); }
 
 __device__ __forceinline__ float dot4(float a0, float a1, float a2, float a3, const float4 &x, float s) {
     s = fmaf(a0, x.x, s);
@@ -416,60 +360,6 @@ __global__ void __launch_bounds__(GemvShape<NB, P>::MAXT) k_qgemv(GemvArgs a) {
 // in shared memory, and a tile spread over several CTAs meets in the
 // workspace, where the last CTA to arrive adds the segments in CTA order --
 // fixed orders throughout, so results are bitwise reproducible.
-
-// Scales of one unit of one row: values 0-15 use s0, 16-31 use s1; Q4_K
-// subtracts mn.  Decoded once per unit, applied per value.
-struct URowScale {
-    float s0, s1, mn;
-};
-template <int TYPE>
-__device__ __forceinline__ URowScale unit_scale(const URegs<TYPE> &g, int u) {
-    URowScale r;
-    r.mn = 0.f;
-    if constexpr (TYPE == HD_TYPE_Q8_0 || TYPE == HD_TYPE_Q5_0) {
-        r.s0 = r.s1 = h2f((uint16_t)g.d);
-    } else if constexpr (TYPE == HD_TYPE_Q4_K) {
-        int sc, m;
-        q4k_sm_regs(u & 7, g.m.y, g.m.z, g.m.w, sc, m);
-        r.s0 = r.s1 = __fmul_rn(h2f((uint16_t)(g.m.x & 0xFFFF)), (float)sc);
-        r.mn = __fmul_rn(h2f((uint16_t)(g.m.x >> 16)), (float)m);
-    } else {
-        const int s0 = 2 * (u & 7);
-        const uint32_t scw = w4(g.sc, s0 >> 2);
-        const float d = h2f((uint16_t)g.d);
-        r.s0 = __fmul_rn(d, (float)(int8_t)((scw >> (8 * (s0 & 3))) & 255));
-        r.s1 = __fmul_rn(d, (float)(int8_t)((scw >> (8 * ((s0 & 3) + 1))) & 255));
-    }
-    return r;
-}
-
-// Values 4wd..4wd+3 of a unit, exact (the dequantized weights).
-template <int TYPE>
-__device__ __forceinline__ void chunk_vals(const URegs<TYPE> &g, const URowScale &sc, int wd, float (&v)[4]) {
-    const float s = wd < 4 ? sc.s0 : sc.s1;
-    if constexpr (TYPE == HD_TYPE_Q8_0) {
-        const uint32_t x = (wd < 4 ? w4(g.a, wd) : w4(g.b, wd - 4)) ^ 0x80808080u;
-#pragma unroll
-        for (int c = 0; c < 4; c++) v[c] = __fmul_rn(mag(x, c) - 8388736.0f, s);
-    } else if constexpr (TYPE == HD_TYPE_Q5_0) {
-        const uint32_t q = w4(g.a, wd & 3);
-        const uint32_t b = wd < 4 ? ((q & 0x0F0F0F0Fu) | ((g.qh >> wd) & 0x10101010u))
-                                  : (((q >> 4) & 0x0F0F0F0Fu) | ((g.qh << (8 - wd)) & 0x10101010u));
-#pragma unroll
-        for (int c = 0; c < 4; c++) v[c] = __fmul_rn(mag(b, c) - 8388624.0f, s);
-    } else if constexpr (TYPE == HD_TYPE_Q4_K) {
-        const uint32_t q = w4(g.a, wd & 3);
-        const uint32_t b = wd < 4 ? (q & 0x0F0F0F0Fu) : ((q >> 4) & 0x0F0F0F0Fu);
-#pragma unroll
-        for (int c = 0; c < 4; c++) v[c] = __fsub_rn(__fmul_rn(mag(b, c) - 8388608.0f, s), sc.mn);
-    } else {
-        const int i = wd & 3;
-        const uint32_t hsel = wd < 4 ? g.h.x : g.h.y;
-        const uint32_t b = ((w4(g.a, i) >> (wd < 4 ? 0 : 4)) & 0x0F0F0F0Fu) | (shl_or_shr(hsel, 4 - 2 * i) & 0x30303030u);
-#pragma unroll
-        for (int c = 0; c < 4; c++) v[c] = __fmul_rn(mag(b, c) - 8388640.0f, s);
-    }
-}
 
 template <int TYPE, int NB, int PT>
 __global__ void __launch_bounds__(32 * NB, 1)
@@ -795,6 +685,11 @@ int run_gemv(hd_ctx *ctx, const hd_weight *w, const hd_weight *w_up, const float
         if (!rc) rc = run_gemv(ctx, w_up, nullptr, x, ctx->scratch + one, B, nullptr, nullptr, name, nw, eps);
         if (!rc) rc = hd_swiglu(ctx, ctx->scratch, ctx->scratch + one, y, (int64_t)one);
         return rc;
+    }
+    if (!w_up && !nw) {  // batch 5..16 on the tensor cores, where the shape fits
+        bool done = false;
+        const int rc = hd_qgemv_tc(ctx, w, x, y, B, bias, residual, &done);
+        if (rc || done) return rc;
     }
     GemvArgs a;
     a.w0 = wview(w);

@@ -117,6 +117,11 @@ int hd_attention_run(hd_ctx *ctx, const float *q, int64_t qld, const float *kc, 
 // w_up != null: SwiGLU pair.
 int hd_qgemv_norm(hd_ctx *ctx, const hd_weight *w, const hd_weight *w_up, const float *x, const float *norm_w,
                   float eps, float *y, int B, const float *bias, const float *residual);
+// Q-GEMV at batch 5..16 on the tensor cores (hd_gemv_tc.cu).  *done = false
+// (and HD_OK) when the batch or shape is outside what the kernel takes; the
+// caller then runs the CUDA-core kernels.
+int hd_qgemv_tc(hd_ctx *ctx, const hd_weight *w, const float *x, float *y, int B, const float *bias,
+                const float *residual, bool *done);
 // Fused q|k|v rows (row stride ld): RoPE on q and k heads in place, rotated k
 // and v appended to cache sequence r / T at position pos[r].
 int hd_rope_kv_append(hd_ctx *ctx, float *qkv, int64_t ld, const int32_t *pos, int rows, int T, int n_heads, int n_kv,
@@ -137,6 +142,29 @@ static inline cudaError_t hd_launch(hd_ctx *ctx, void (*kern)(KArgs...), dim3 gr
     attr[0].val.programmaticStreamSerializationAllowed = ctx->pdl ? 1 : 0;
     cfg.attrs = attr;
     cfg.numAttrs = 1;
+    ctx->launches++;
+    return cudaLaunchKernelEx(&cfg, kern, static_cast<KArgs>(args)...);
+}
+
+// The same with thread-block clusters of `cluster` CTAs along x (grid.x a
+// multiple of it).
+template <typename... KArgs, typename... Args>
+static inline cudaError_t hd_launch_cluster(hd_ctx *ctx, void (*kern)(KArgs...), dim3 grid, dim3 block, size_t smem,
+                                            int cluster, Args... args) {
+    cudaLaunchConfig_t cfg = {};
+    cfg.gridDim = grid;
+    cfg.blockDim = block;
+    cfg.dynamicSmemBytes = smem;
+    cfg.stream = ctx->stream;
+    cudaLaunchAttribute attr[2];
+    attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+    attr[0].val.programmaticStreamSerializationAllowed = ctx->pdl ? 1 : 0;
+    attr[1].id = cudaLaunchAttributeClusterDimension;
+    attr[1].val.clusterDim.x = (unsigned)cluster;
+    attr[1].val.clusterDim.y = 1;
+    attr[1].val.clusterDim.z = 1;
+    cfg.attrs = attr;
+    cfg.numAttrs = 2;
     ctx->launches++;
     return cudaLaunchKernelEx(&cfg, kern, static_cast<KArgs>(args)...);
 }

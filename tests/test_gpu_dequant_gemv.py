@@ -190,11 +190,15 @@ def test_gemv_lm_head_q8_0(ctx):
                                                     (S.GGML_Q8_0, 384, 2048, 6, False, False),
                                                     (S.GGML_Q5_0, 19000, 512, 16, False, True),
                                                     (S.GGML_Q4_K, 18944, 256, 9, True, False)])
-def test_gemv_batched_register_blocked(ctx, t, N, K, B, bias, residual):
-    """Batch 5..16 (the register-blocked kernel): epilogues, the K split over
-    CTAs, the one-CTA-per-tile mode of tall matrices (>= 148 tiles of 128
-    rows), and bitwise-stable reruns."""
+@pytest.mark.parametrize("tensor_cores", [True, False])
+def test_gemv_batched_register_blocked(ctx, monkeypatch, t, N, K, B, bias, residual, tensor_cores):
+    """Batch 5..16: epilogues and bitwise-stable reruns, through the tensor-core
+    kernel where the shape fits it and, with it switched off, through the
+    register-blocked CUDA-core kernel (the K split over CTAs, the
+    one-CTA-per-tile mode of tall matrices with >= 148 tiles of 128 rows)."""
     torch = _torch()
+    if not tensor_cores:
+        monkeypatch.setenv("HACEDLE_GEMV_TC", "0")
     y, ref = _gemv_case(ctx, t, N, K, B, 200 + B, bias=bias, residual=residual)
     assert _rel_err(y, ref) <= REL_TOL
     raw = S.gen_weight(t, N, K, 300 + B)
@@ -206,6 +210,33 @@ def test_gemv_batched_register_blocked(ctx, t, N, K, B, bias, residual):
     ctx.qgemv(w, x, y2)
     torch.cuda.synchronize()
     assert torch.equal(y1, y2)
+
+
+# Tensor-core batch kernel: K parts S (1 = no cluster, 16 = the largest
+# cluster), units per part up to 16 (the accumulator ring reused for Q6_K's
+# half-unit groups and past 8 units), ragged row tiles, batch 5 and 16.
+@pytest.mark.parametrize("t,N,K,B,parts", [(S.GGML_Q5_0, 4864, 512, 16, "1"), (S.GGML_Q8_0, 300, 2048, 5, "4"),
+                                           (S.GGML_Q6_K, 896, 4864, 16, "16"), (S.GGML_Q4_K, 384, 4096, 12, "8"),
+                                           (S.GGML_Q6_K, 257, 2048, 7, "4"), (S.GGML_Q8_0, 4864, 896, 9, ""),
+                                           (S.GGML_Q5_0, 896, 4864, 13, ""), (S.GGML_Q8_0, 1000, 512, 16, "3")])
+def test_gemv_tensor_core_k_parts(ctx, monkeypatch, t, N, K, B, parts):
+    """Batch 5..16 on the tensor cores (exact integer weights times an exact
+    three-way bf16 split of x, fp32 scales per group) against the oracle, with
+    bias and residual epilogues, and bitwise-equal reruns."""
+    torch = _torch()
+    if parts:
+        monkeypatch.setenv("HACEDLE_GEMV_TC_S", parts)
+    y, ref = _gemv_case(ctx, t, N, K, B, 500 + B, bias=True, residual=(B % 2 == 1))
+    assert _rel_err(y, ref) <= REL_TOL
+    w = ctx.weight(t, S.gen_weight(t, N, K, 600 + B), N, K)
+    x = torch.from_numpy(S.gen_activations(B, K, 601)).cuda()
+    y1 = torch.empty(B, N, device="cuda")
+    y2 = torch.empty(B, N, device="cuda")
+    ctx.qgemv(w, x, y1)
+    ctx.qgemv(w, x, y2)
+    torch.cuda.synchronize()
+    assert torch.equal(y1, y2)
+    ctx.check_device_errors()
 
 
 @pytest.mark.parametrize("t,N,K,B", [(S.GGML_Q5_0, 1152, 896, 1), (S.GGML_Q5_0, 896, 896, 3), (S.GGML_Q8_0, 896, 896, 4),
