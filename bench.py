@@ -230,9 +230,14 @@ def run_ours(args, rank, world, local):
                 "gbs": round(case_bytes(t, N, K, B) / (per * 1e-3) / 1e9, 1), "us_per_launch": round(per * 1e3, 3)}
     launches = launches_per_step * args.steps
     achieved = step_bytes * args.steps / (kernel_ms * 1e-3) / 1e9
+    # Batch 1 and 4 run the CUDA-core k_qgemv, batch 16 the tensor-core
+    # k_qgemv_tc (hd_qgemv picks by batch): their shares of the step's time.
+    tc_ms = sum(case_ms[(t, B)] for (t, N, K) in CASES for B in BATCHES if B >= 5)
     roofline = {"bound": "hbm", "achieved": round(achieved, 1), "peak": hbm, "unit": "GB/s",
                 "frac": round(achieved / hbm, 4), "traffic": None, "peak_kind": peak_kind,
-                "kernel": "k_qgemv", "algorithmic_bytes_per_step": step_bytes}
+                "kernel": "k_qgemv", "algorithmic_bytes_per_step": step_bytes,
+                "kernel_time_share": {"k_qgemv (B=1,4)": round(1 - tc_ms / kernel_ms, 3),
+                                      "k_qgemv_tc (B=16)": round(tc_ms / kernel_ms, 3)}}
     # DRAM bytes of one captured launch (ncu --set full, Q5_0 batch 1), with its
     # algorithmic bytes: profiles/qgemv_q5_0_b1_ncu.md.
     trf = os.path.join(ROOT, "profiles", "qgemv_q5_0_b1_ncu.md")
