@@ -554,8 +554,8 @@ int max_threads(int nb, bool pair) { return (nb <= 2 ? 1024 : nb <= 4 ? 512 : 25
 // Launch shape, from a sweep of rows-per-CTA x threads-per-CTA on B200 in a
 // PDL chain of back-to-back GEMVs:
 //  - about 2 units per thread (4 at batch >= 8 or for very tall matrices);
-//  - CTAs small enough in registers (<= 512 threads at batch <= 2, 128
-//    above) that the next kernel's CTA fits beside them, so its weight
+//  - CTAs small enough in registers (<= 512 threads at batch <= 2, 256 at
+//    3..4, 128 above) that the next kernel's CTA fits beside them, so its weight
 //    prefetch overlaps this one -- unless the row tiles leave SMs idle anyway;
 //  - 8..32 rows per CTA (whole 32-byte sectors, x broadcast across lanes),
 //    at most about rows / SMs rounded up to a power of two.
@@ -579,7 +579,7 @@ Plan plan_gemv(int N, int units, int B, bool pair, int sms) {
     const int upt = (p.nb >= 8 || tall) ? 4 : 2;
     int G = pow2ceil((units + upt - 1) / upt);
     if (G > units) G = units;
-    const int ntcap = p.nb <= 2 ? 512 : 128;
+    const int ntcap = p.nb <= 2 ? 512 : p.nb <= 4 ? 256 : 128;
     int rc_hi = pow2ceil((N + sms - 1) / sms);
     rc_hi = rc_hi < 8 ? 8 : rc_hi > 32 ? 32 : rc_hi;
     int RC = ntcap / G;
