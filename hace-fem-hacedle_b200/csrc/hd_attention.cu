@@ -79,7 +79,13 @@ constexpr int CH = 64;     // positions per chunk
 constexpr int ANT = 512;   // threads per CTA: one score and one output chain each (rep x 64 <= 512 for rep <= 8)
 constexpr int MAXREP = 16;
 
-template <int HD>
+// EARLY (the decoder's decode steps): the K and V rows of the CTA's first
+// chunk are loaded before griddepcontrol.wait, overlapping the previous
+// kernel.  Only callers whose cache rows below the new position were written
+// at least one kernel before the previous one may set it (the decoder: a step
+// earlier), and lens / slots likewise; the new position's row is replaced
+// from shared memory as usual.
+template <int HD, bool EARLY>
 __global__ void __launch_bounds__(ANT) k_attention(const float *__restrict__ q, int64_t qld, const float *__restrict__ kc,
                                                    const float *__restrict__ vc, const int32_t *__restrict__ lens,
                                                    int pos0, int seqT, int n_heads, int n_kv, int max_ctx,
@@ -90,6 +96,33 @@ __global__ void __launch_bounds__(ANT) k_attention(const float *__restrict__ q, 
     extern __shared__ float sm[];
     constexpr int KP = HD + 1;                      // padded K row
     constexpr int OPT = (MAXREP * HD + ANT - 1) / ANT;
+    // A chunk's K and V rows: CH * HD / 4 float4 each, NLD per thread per
+    // batch.  All loads of a batch are issued before any is stored, so the
+    // chunk costs one memory latency per batch rather than one per float4.
+    constexpr int NF4 = CH * (HD / 4) / ANT, NB = HD > 64 ? 4 : 8, NLD = NF4 < NB ? NF4 : NB;
+    float4 pk[EARLY ? NLD : 1], pv[EARLY ? NLD : 1];
+    bool pre = false;
+    if constexpr (EARLY) {
+        static_assert(NF4 == NLD, "one load batch per chunk");
+        const int re = blockIdx.x, pe = blockIdx.z;
+        const int cs = lens ? (slots ? slots[re] : re) : re / seqT;
+        int Le = lens ? lens[re] : pos0 + re % seqT + 1;
+        Le = Le < 0 ? 0 : Le > max_ctx ? max_ctx : Le;
+        const int ce = pe * cpc, j0 = ce * CH;
+        if (ce < (Le + CH - 1) / CH) {
+            const int nj = min(CH, Le - j0);
+#pragma unroll
+            for (int u = 0; u < NLD; u++) {
+                const int i = threadIdx.x + u * ANT, j = i / (HD / 4), d4 = i % (HD / 4);
+                if (j < nj) {
+                    const int64_t g = (((int64_t)cs * max_ctx + j0 + j) * n_kv + blockIdx.y) * HD + 4 * d4;
+                    pk[u] = __ldg((const float4 *)(kc + g));
+                    pv[u] = __ldg((const float4 *)(vc + g));
+                }
+            }
+            pre = true;
+        }
+    }
     pdl_wait();
     pdl_trigger();
     const int r = blockIdx.x, kvh = blockIdx.y, p = blockIdx.z;
@@ -158,23 +191,27 @@ __global__ void __launch_bounds__(ANT) k_attention(const float *__restrict__ q, 
     for (int k = 0; k < OPT; k++) o[k] = 0.f;
     const int64_t cbase = (int64_t)cseq * max_ctx;
     const int c1 = min(nchunks, (p + 1) * cpc);
-    // A chunk's K and V rows: CH * HD / 4 float4 each, NLD per thread per
-    // batch.  All loads of a batch are issued before any is stored, so the
-    // chunk costs one memory latency per batch rather than one per float4.
-    constexpr int NF4 = CH * (HD / 4) / ANT, NB = HD > 64 ? 4 : 8, NLD = NF4 < NB ? NF4 : NB;
     for (int c = p * cpc; c < c1; c++) {
         const int j0 = c * CH, nj = min(CH, L - j0);
         __syncthreads();
 #pragma unroll
         for (int b0 = 0; b0 < NF4; b0 += NLD) {
             float4 kr[NLD], vr[NLD];
+            if (EARLY && pre && c == p * cpc) {   // loaded before the dependency wait
 #pragma unroll
-            for (int u = 0; u < NLD; u++) {
-                const int i = tid + (b0 + u) * ANT, j = i / (HD / 4), d4 = i % (HD / 4);
-                if (j < nj) {
-                    const int64_t g = ((cbase + j0 + j) * n_kv + kvh) * HD + 4 * d4;
-                    kr[u] = __ldg((const float4 *)(kc + g));
-                    vr[u] = __ldg((const float4 *)(vc + g));
+                for (int u = 0; u < NLD; u++) {
+                    kr[u] = pk[EARLY ? u : 0];
+                    vr[u] = pv[EARLY ? u : 0];
+                }
+            } else {
+#pragma unroll
+                for (int u = 0; u < NLD; u++) {
+                    const int i = tid + (b0 + u) * ANT, j = i / (HD / 4), d4 = i % (HD / 4);
+                    if (j < nj) {
+                        const int64_t g = ((cbase + j0 + j) * n_kv + kvh) * HD + 4 * d4;
+                        kr[u] = __ldg((const float4 *)(kc + g));
+                        vr[u] = __ldg((const float4 *)(vc + g));
+                    }
                 }
             }
 #pragma unroll
@@ -296,27 +333,39 @@ size_t attn_smem(int rep) {
            sizeof(float);
 }
 
-template <int HD>
-cudaError_t launch_attn(hd_ctx *ctx, int rows, int n_heads, int n_kv, int P, int cpc, const float *q, int64_t qld,
-                        const float *kc, const float *vc, const int32_t *lens, int pos0, int seqT, int max_ctx,
-                        const int32_t *slots, const float *rfreq, const int32_t *rpos, float *out) {
+template <int HD, bool EARLY>
+cudaError_t launch_attn_t(hd_ctx *ctx, int rows, int n_heads, int n_kv, int P, int cpc, const float *q, int64_t qld,
+                          const float *kc, const float *vc, const int32_t *lens, int pos0, int seqT, int max_ctx,
+                          const int32_t *slots, const float *rfreq, const int32_t *rpos, float *out) {
     const int rep = n_heads / n_kv;
     const size_t smem = attn_smem<HD>(rep);
     if (smem > 48 * 1024) {
-        cudaError_t e = cudaFuncSetAttribute(k_attention<HD>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
+        cudaError_t e =
+            cudaFuncSetAttribute(k_attention<HD, EARLY>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
         if (e != cudaSuccess) return e;
     }
     const float scale = sqrtf((float)HD);
-    return hd_launch(ctx, k_attention<HD>, dim3(rows, n_kv, P), dim3(ANT), smem, q, qld, kc, vc, lens, pos0, seqT,
-                     n_heads, n_kv, max_ctx, scale, P, cpc, (float *)ctx->ws, ctx->tickets, slots, rfreq, rpos,
+    return hd_launch(ctx, k_attention<HD, EARLY>, dim3(rows, n_kv, P), dim3(ANT), smem, q, qld, kc, vc, lens, pos0,
+                     seqT, n_heads, n_kv, max_ctx, scale, P, cpc, (float *)ctx->ws, ctx->tickets, slots, rfreq, rpos,
                      (float *)kc, (float *)vc, out);
+}
+
+template <int HD>
+cudaError_t launch_attn(hd_ctx *ctx, int rows, int n_heads, int n_kv, int P, int cpc, const float *q, int64_t qld,
+                        const float *kc, const float *vc, const int32_t *lens, int pos0, int seqT, int max_ctx,
+                        const int32_t *slots, const float *rfreq, const int32_t *rpos, float *out, bool early) {
+    return early ? launch_attn_t<HD, true>(ctx, rows, n_heads, n_kv, P, cpc, q, qld, kc, vc, lens, pos0, seqT, max_ctx,
+                                           slots, rfreq, rpos, out)
+                 : launch_attn_t<HD, false>(ctx, rows, n_heads, n_kv, P, cpc, q, qld, kc, vc, lens, pos0, seqT,
+                                            max_ctx, slots, rfreq, rpos, out);
 }
 
 }  // namespace
 
 int hd_attention_run(hd_ctx *ctx, const float *q, int64_t qld, const float *kc, const float *vc, const int32_t *lens,
                      int rows, int pos0, int seqT, int n_heads, int n_kv, int hd, int max_ctx, int maxlen, float *out,
-                     const char *name, const int32_t *slots, const float *rope_freq, const int32_t *rope_pos) {
+                     const char *name, const int32_t *slots, const float *rope_freq, const int32_t *rope_pos,
+                     bool early_kv) {
     if (!ctx || !q || !kc || !vc || !out) return hd_fail(ctx, HD_E_ARG, "%s: null argument", name);
     HD_REQUIRE(ctx, n_heads > 0 && n_kv > 0 && n_heads % n_kv == 0 && n_heads / n_kv <= MAXREP, HD_E_SHAPE,
                "%s: n_heads %d must be a multiple of n_kv %d, at most %d per kv head", name, n_heads, n_kv, MAXREP);
@@ -342,10 +391,10 @@ int hd_attention_run(hd_ctx *ctx, const float *q, int64_t qld, const float *kc, 
     }
     cudaError_t e;
     if (qld == 0) qld = (int64_t)n_heads * hd;
-    if (hd == 64) e = launch_attn<64>(ctx, rows, n_heads, n_kv, P, cpc, q, qld, kc, vc, lens, pos0, seqT, max_ctx, slots, rope_freq, rope_pos, out);
+    if (hd == 64) e = launch_attn<64>(ctx, rows, n_heads, n_kv, P, cpc, q, qld, kc, vc, lens, pos0, seqT, max_ctx, slots, rope_freq, rope_pos, out, early_kv);
     else if (hd == 128)
-        e = launch_attn<128>(ctx, rows, n_heads, n_kv, P, cpc, q, qld, kc, vc, lens, pos0, seqT, max_ctx, slots, rope_freq, rope_pos, out);
-    else e = launch_attn<32>(ctx, rows, n_heads, n_kv, P, cpc, q, qld, kc, vc, lens, pos0, seqT, max_ctx, slots, rope_freq, rope_pos, out);
+        e = launch_attn<128>(ctx, rows, n_heads, n_kv, P, cpc, q, qld, kc, vc, lens, pos0, seqT, max_ctx, slots, rope_freq, rope_pos, out, early_kv);
+    else e = launch_attn<32>(ctx, rows, n_heads, n_kv, P, cpc, q, qld, kc, vc, lens, pos0, seqT, max_ctx, slots, rope_freq, rope_pos, out, early_kv);
     if (e != cudaSuccess) return hd_fail(ctx, HD_E_CUDA, "%s: %s", name, cudaGetErrorString(e));
     return HD_OK;
 }

@@ -167,7 +167,8 @@ int layer_forward(hd_decoder *d, int li, int rows, const int32_t *pos, const int
         if (rc) return rc;
         if (lens)
             rc = hd_attention_run(ctx, d->qkv, ld, d->kc + lay, d->vc + lay, lens, S, 0, 1, c.n_heads, c.n_kv, hd,
-                                  c.max_ctx, c.max_ctx, d->att, "decoder attention", nullptr, ctx->rope_freq, pos);
+                                  c.max_ctx, c.max_ctx, d->att, "decoder attention", nullptr, ctx->rope_freq, pos,
+                                  true);  // cache rows below pos were written a step or more earlier
         else
             rc = hd_attention_run(ctx, d->qkv, ld, d->kc + lay, d->vc + lay, nullptr, rows, 0, T, c.n_heads, c.n_kv,
                                   hd, c.max_ctx, T, d->att, "decoder prefill attention");

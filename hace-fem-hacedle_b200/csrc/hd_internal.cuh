@@ -109,10 +109,12 @@ bool hd_type_supported(int t);
 int hd_ensure_hbuf(hd_ctx *ctx, float **buf, size_t *have, size_t need);
 int hd_qgemm_f32(hd_ctx *ctx, const hd_weight *w, const float *X, float *Y, int T);
 // Attention over `rows` query rows (see k_attention in hd_attention.cu).
+// early_kv: cache rows below each row's length are final before the
+// previous kernel starts (loads may be issued before the dependency wait).
 int hd_attention_run(hd_ctx *ctx, const float *q, int64_t qld, const float *kc, const float *vc, const int32_t *lens,
                      int rows, int pos0, int seqT, int n_heads, int n_kv, int hd, int max_ctx, int maxlen, float *out,
                      const char *name, const int32_t *slots = nullptr, const float *rope_freq = nullptr,
-                     const int32_t *rope_pos = nullptr);
+                     const int32_t *rope_pos = nullptr, bool early_kv = false);
 // Q-GEMV (B <= 16) of rmsnorm(x) with the norm in each CTA's prologue;
 // w_up != null: SwiGLU pair.
 int hd_qgemv_norm(hd_ctx *ctx, const hd_weight *w, const hd_weight *w_up, const float *x, const float *norm_w,
