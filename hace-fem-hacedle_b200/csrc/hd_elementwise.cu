@@ -216,15 +216,20 @@ __global__ void __launch_bounds__(NT) k_argmax(const float *__restrict__ x, int6
     }
 }
 
+// dst[b][g*n + j] = src[g][b][j]: CTA (column block, b, g), no index
+// division; float4 accesses when n % 4 == 0 and both buffers are 16-byte
+// aligned (VEC = 4), else one float per thread.
+template <int VEC>
 __global__ void k_gather_columns(const float *__restrict__ src, float *__restrict__ dst, int G, int B, int64_t n) {
     pdl_wait();
     pdl_trigger();
-    int64_t i = (int64_t)blockIdx.x * blockDim.x + threadIdx.x;
-    int64_t total = (int64_t)G * B * n;
-    if (i >= total) return;
-    int64_t j = i % n, gb = i / n;
-    int b = (int)(gb % B), g = (int)(gb / B);
-    dst[(int64_t)b * G * n + (int64_t)g * n + j] = src[i];
+    const int64_t j = ((int64_t)blockIdx.x * blockDim.x + threadIdx.x) * VEC;
+    if (j >= n) return;
+    const int b = blockIdx.y, g = blockIdx.z;
+    const float *s = src + ((int64_t)g * B + b) * n + j;
+    float *d = dst + ((int64_t)b * G + g) * n + j;
+    if constexpr (VEC == 4) *(float4 *)d = __ldg((const float4 *)s);
+    else *d = __ldg(s);
 }
 
 inline unsigned blocks_for(int64_t n, int nt) { return (unsigned)((n + nt - 1) / nt); }
@@ -325,7 +330,13 @@ extern "C" int hd_argmax_rows(hd_ctx *ctx, const float *x, int64_t rows, int64_t
 extern "C" int hd_gather_columns(hd_ctx *ctx, const float *src, float *dst, int G, int B, int64_t n) {
     if (!ctx || !src || !dst) return hd_fail(ctx, HD_E_ARG, "hd_gather_columns: null argument");
     HD_REQUIRE(ctx, G > 0 && B > 0 && n > 0, HD_E_SHAPE, "hd_gather_columns: bad shape");
-    int64_t total = (int64_t)G * B * n;
-    HD_CUDA_TRY(ctx, hd_launch(ctx, k_gather_columns, dim3(blocks_for(total, 256)), dim3(256), 0, src, dst, G, B, n));
+    HD_REQUIRE(ctx, B <= 65535 && G <= 65535, HD_E_SHAPE, "hd_gather_columns: B and G at most 65535");
+    const bool v4 = n % 4 == 0 && ((uintptr_t)src & 15) == 0 && ((uintptr_t)dst & 15) == 0;
+    if (v4)
+        HD_CUDA_TRY(ctx, hd_launch(ctx, k_gather_columns<4>, dim3(blocks_for(n / 4, 256), (unsigned)B, (unsigned)G),
+                                   dim3(256), 0, src, dst, G, B, n));
+    else
+        HD_CUDA_TRY(ctx, hd_launch(ctx, k_gather_columns<1>, dim3(blocks_for(n, 256), (unsigned)B, (unsigned)G),
+                                   dim3(256), 0, src, dst, G, B, n));
     return HD_OK;
 }

@@ -220,3 +220,16 @@ def test_qgemm_fp32_exact_weights(ctx, t, N, K, Tn):
     got = host(Y)
     assert np.abs(got - ref).max() <= 1e-5 * np.abs(ref).max()
     assert np.array_equal(ctx.qgemm_host(w, X, precision=0).view(np.uint32), got.view(np.uint32))
+
+
+@pytest.mark.parametrize("G,B,n", [(1, 1, 4), (2, 5, 1792), (8, 3, 64), (3, 7, 33), (2, 512, 9472)])
+def test_gather_columns(ctx, G, B, n):
+    """[G][B][n] rank blocks -> [B][G*n] rows (the row-sharded layer's
+    reassembly after the all-gather): float4 path when n % 4 == 0, scalar
+    otherwise; bit-exact copy."""
+    from hacedle_cuda import shard
+    src = np.random.default_rng(G * 1000 + B + n).standard_normal((G, B, n), dtype=np.float32)
+    dst = T().empty(B, G * n, device="cuda")
+    ctx.gather_columns(cuda(src), dst, G, B, n)
+    T().cuda.synchronize()
+    assert np.array_equal(host(dst), shard.gather_columns_reference(src, G, B, n))
