@@ -421,7 +421,10 @@ def layer7b_workload(ctx, args, rank, world, reps=5):
     """Config 5: the seven projections of a Qwen2.5-7B-shaped layer (q/k/v/o and
     gate/up Q4_K, down Q6_K), output rows sharded over the ranks.  Each rank
     computes its rows (GEMV at B=1, tcgen05 GEMM at B=64 and 512), then the
-    outputs are all-gathered over NVLink (NCCL) and reassembled on the device.
+    outputs are exchanged over NVLink: by default each rank's own kernel writes
+    its slice into every rank's full output (hd_push_columns, IPC-mapped
+    buffers); HACEDLE_EXCHANGE=nccl uses an NCCL all-gather plus
+    hd_gather_columns instead.
     Total work is fixed (strong scaling); times are device times (the work is
     queued behind a device-side spin), max over ranks, after a 256 MB L2 flush
     before every rep."""
@@ -442,13 +445,27 @@ def layer7b_workload(ctx, args, rank, world, reps=5):
     w_total = sum(S.nbytes(t, N, K) for _, t, N, K in mats)
     flops_per_tok = sum(2 * N * K for _, t, N, K in mats)
     flush = torch.empty(256 << 20, dtype=torch.uint8, device="cuda")
+    use_nccl = os.environ.get("HACEDLE_EXCHANGE", "") == "nccl"
+    peer = None
+    if world > 1 and not use_nccl:
+        import torch.distributed as dist
+
+        def ago(obj):
+            out = [None] * world
+            dist.all_gather_object(out, obj)
+            return out
+        peer = shard.PeerExchange(ctx, world, rank, [(512, N) for _, _, N, _ in mats], ago)
     res = {"scaling": "strong", "ranks": world, "weight_bytes_layer": w_total, "peak_kind": kind,
-           "exchange": "NCCL all_gather_into_tensor (torch.distributed) + hd_gather_columns" if world > 1 else "none"}
+           "exchange": ("none" if world == 1 else
+                        "NCCL all_gather_into_tensor (torch.distributed) + hd_gather_columns" if use_nccl else
+                        "hd_push_columns: P2P stores over NVLink into IPC-mapped outputs, epoch flags")}
     for B in (1, 64, 512):
         xs = {K: torch.from_numpy(S.gen_activations(B, K, 60)).cuda() for K in (H, F)}
         ys = [torch.empty(B, N // world, device="cuda") for _, _, N, _, _ in ws]
-        gath = [torch.empty(world, B, N // world, device="cuda") for _, _, N, _, _ in ws]
-        full = [torch.empty(B, N, device="cuda") for _, _, N, _, _ in ws]
+        gath = ([torch.empty(world, B, N // world, device="cuda") for _, _, N, _, _ in ws] if world > 1 and not peer
+                else [None] * len(ws))
+        full = ([peer.full(i, B) for i in range(len(ws))] if peer else
+                [torch.empty(B, N, device="cuda") for _, _, N, _, _ in ws])
 
         def compute():
             for (nm, t, N, K, w), y in zip(ws, ys):
@@ -459,8 +476,10 @@ def layer7b_workload(ctx, args, rank, world, reps=5):
 
         def exchange():
             import torch.distributed as dist
-            for (nm, t, N, K, w), y, g, f in zip(ws, ys, gath, full):
-                if world > 1:
+            for i, ((nm, t, N, K, w), y, g, f) in enumerate(zip(ws, ys, gath, full)):
+                if peer:
+                    peer.push(i, y, B, N // world)
+                elif world > 1:
                     dist.all_gather_into_tensor(g.view(-1), y.view(-1))
                     ctx.gather_columns(g, f, world, B, N // world)
                 else:
@@ -497,6 +516,9 @@ def layer7b_workload(ctx, args, rank, world, reps=5):
             ent["tflops"] = round(flops_per_tok * B / (tm * 1e-3) / 1e12, 2)
             ent["compute_tflops_per_gpu"] = round(flops_per_tok * B / world / (cm * 1e-3) / 1e12, 2)
         res[f"B{B}"] = ent
+    if peer:
+        barrier(world)
+        peer.close()
     for *_, w in ws:
         w.free()
     return res

@@ -193,6 +193,35 @@ int hd_embed(hd_ctx *ctx, const hd_weight *table, const int32_t *ids_dev, int n,
  * row-sharded 7B-shaped layer. */
 int hd_gather_columns(hd_ctx *ctx, const float *src_dev, float *dst_dev, int G, int B, int64_t n);
 
+/* Exchange of row-sharded outputs over NVLink, our own kernel in place of
+ * an all-gather plus hd_gather_columns.  The reference has no multi-GPU
+ * path; this is the exchange step of the row-sharded 7B-shaped layer.
+ *
+ * Each rank allocates one exchange buffer (hd_xbuf_alloc: cudaMalloc'd,
+ * zeroed) that holds its flag array (int32 [G]) and its full output buffers,
+ * passes hd_ipc_handle's 64 bytes to the other ranks (any host channel), and
+ * maps theirs with hd_ipc_open (hd_ipc_close undoes it).
+ *
+ * hd_push_columns: rank `rank` of `world` writes y_dev [B][n] (its output rows
+ * rank*n..) into every rank's full buffer [B][world*n] at columns rank*n..,
+ * then raises its flag (= epoch) in every peer's flag array, and waits until
+ * every peer's flag has reached epoch in its own.  full_ptrs_dev and
+ * flag_ptrs_dev are DEVICE arrays of `world` pointers, indexed by rank
+ * (this rank's own buffers, the peers' IPC mappings); full buffers 16-byte
+ * aligned.  Every rank makes the same sequence of calls with the same,
+ * growing epochs (> 0).  The wait is bounded (about 1 s): on expiry the
+ * context's device error flag holds HD_E_TIMEOUT (hd_ctx_check_device_errors).
+ * A rank must not start the next exchange into a full buffer while some rank
+ * still reads that buffer's previous contents. */
+#define HD_IPC_HANDLE_BYTES 64
+int hd_xbuf_alloc(hd_ctx *ctx, size_t bytes, void **dev_ptr);
+int hd_xbuf_free(hd_ctx *ctx, void *dev_ptr);
+int hd_ipc_handle(hd_ctx *ctx, void *dev_ptr, void *handle_out);
+int hd_ipc_open(hd_ctx *ctx, const void *handle, void **peer_ptr);
+int hd_ipc_close(hd_ctx *ctx, void *peer_ptr);
+int hd_push_columns(hd_ctx *ctx, const float *y_dev, float *const *full_ptrs_dev, int32_t *const *flag_ptrs_dev,
+                    int world, int rank, int B, int64_t n, int32_t epoch);
+
 /* ------------------------------------------------------- KV and attention */
 /* Device KV cache (KvCache::append, core/ops/block.rs:268-282, KvArena
  * runtime/kv_cache.rs:8-34): caches are [seq][max_ctx][n_kv][head_dim] f32;
