@@ -103,7 +103,6 @@ __global__ void __launch_bounds__(ANT) k_attention(const float *__restrict__ q, 
     float4 pk[EARLY ? NLD : 1], pv[EARLY ? NLD : 1];
     bool pre = false;
     if constexpr (EARLY) {
-        static_assert(NF4 == NLD, "one load batch per chunk");
         const int re = blockIdx.x, pe = blockIdx.z;
         const int cs = lens ? (slots ? slots[re] : re) : re / seqT;
         int Le = lens ? lens[re] : pos0 + re % seqT + 1;
@@ -191,39 +190,48 @@ __global__ void __launch_bounds__(ANT) k_attention(const float *__restrict__ q, 
     for (int k = 0; k < OPT; k++) o[k] = 0.f;
     const int64_t cbase = (int64_t)cseq * max_ctx;
     const int c1 = min(nchunks, (p + 1) * cpc);
+    static_assert(NF4 == NLD, "one load batch per chunk");
+    // Software pipeline over the CTA's chunks: chunk c + 1's K and V rows are
+    // loaded into registers while chunk c is computed, so a CTA that walks
+    // several chunks pays one memory latency, not one per chunk.  Only the
+    // timing of the loads changes, not any arithmetic.
+    float4 kr[NLD], vr[NLD];
+    auto load_chunk = [&](int c) {
+        const int j0 = c * CH, nj = min(CH, L - j0);
+#pragma unroll
+        for (int u = 0; u < NLD; u++) {
+            const int i = tid + u * ANT, j = i / (HD / 4), d4 = i % (HD / 4);
+            if (j < nj) {
+                const int64_t g = ((cbase + j0 + j) * n_kv + kvh) * HD + 4 * d4;
+                kr[u] = __ldg((const float4 *)(kc + g));
+                vr[u] = __ldg((const float4 *)(vc + g));
+            }
+        }
+    };
+    if (p * cpc < c1) {
+        if (EARLY && pre) {   // loaded before the dependency wait
+#pragma unroll
+            for (int u = 0; u < NLD; u++) {
+                kr[u] = pk[EARLY ? u : 0];
+                vr[u] = pv[EARLY ? u : 0];
+            }
+        } else {
+            load_chunk(p * cpc);
+        }
+    }
     for (int c = p * cpc; c < c1; c++) {
         const int j0 = c * CH, nj = min(CH, L - j0);
         __syncthreads();
 #pragma unroll
-        for (int b0 = 0; b0 < NF4; b0 += NLD) {
-            float4 kr[NLD], vr[NLD];
-            if (EARLY && pre && c == p * cpc) {   // loaded before the dependency wait
-#pragma unroll
-                for (int u = 0; u < NLD; u++) {
-                    kr[u] = pk[EARLY ? u : 0];
-                    vr[u] = pv[EARLY ? u : 0];
-                }
-            } else {
-#pragma unroll
-                for (int u = 0; u < NLD; u++) {
-                    const int i = tid + (b0 + u) * ANT, j = i / (HD / 4), d4 = i % (HD / 4);
-                    if (j < nj) {
-                        const int64_t g = ((cbase + j0 + j) * n_kv + kvh) * HD + 4 * d4;
-                        kr[u] = __ldg((const float4 *)(kc + g));
-                        vr[u] = __ldg((const float4 *)(vc + g));
-                    }
-                }
-            }
-#pragma unroll
-            for (int u = 0; u < NLD; u++) {
-                const int i = tid + (b0 + u) * ANT, j = i / (HD / 4), d4 = i % (HD / 4);
-                if (j < nj) {
-                    float *kd = Ks + j * KP + 4 * d4;
-                    kd[0] = kr[u].x; kd[1] = kr[u].y; kd[2] = kr[u].z; kd[3] = kr[u].w;
-                    *(float4 *)(Vs + j * HD + 4 * d4) = vr[u];
-                }
+        for (int u = 0; u < NLD; u++) {
+            const int i = tid + u * ANT, j = i / (HD / 4), d4 = i % (HD / 4);
+            if (j < nj) {
+                float *kd = Ks + j * KP + 4 * d4;
+                kd[0] = kr[u].x; kd[1] = kr[u].y; kd[2] = kr[u].z; kd[3] = kr[u].w;
+                *(float4 *)(Vs + j * HD + 4 * d4) = vr[u];
             }
         }
+        if (c + 1 < c1) load_chunk(c + 1);   // in flight during this chunk's compute
         __syncthreads();
         if (owner && c == pn / CH) {  // the new position, from shared memory (not re-read from the cache)
             const int j = pn - j0;
