@@ -293,7 +293,7 @@ def _median(v):
 
 
 def prefill_workload(ctx, args, reps=3):
-    """Config 3: prefill Q-GEMM, Q5_0 [4864 x 896] and Q4_K [896 x 4864] times
+    """Prefill Q-GEMM, Q5_0 [4864 x 896] and Q4_K [896 x 4864] times
     X [T x K] for T = 128, 512, 2048.  A timed batch runs the GEMM once on each
     of `nrot` weight copies and activation buffers (more than 256 MB of inputs
     in all, so that no call finds its inputs in the 126 MB L2), back to back
@@ -343,7 +343,7 @@ def prefill_workload(ctx, args, reps=3):
 
 
 def dequant_workload(ctx, copies=160):
-    """Config 1: Q8_0 [896 x 896] full dequant (bit-exact f32 out) and its B=1
+    """Q8_0 [896 x 896] full dequant (bit-exact f32 out) and its B=1
     GEMV, rotating over `copies` weights and outputs (> L2)."""
     import torch
 
@@ -385,7 +385,7 @@ def dequant_workload(ctx, copies=160):
 
 
 def decode_workload(ctx, args, rank, world):
-    """Config 4: Qwen2.5-0.5B-shaped decoder with random weights -- prefill 512
+    """Qwen2.5-0.5B-shaped decoder with random weights -- prefill 512
     ids, greedy 128 tokens -- at batch 1, and 256 sequences split over the
     ranks (replicated weights, no collective)."""
     import hacedle_cuda as hc
@@ -418,7 +418,7 @@ def decode_workload(ctx, args, rank, world):
 
 
 def layer7b_workload(ctx, args, rank, world, reps=5):
-    """Config 5: the seven projections of a Qwen2.5-7B-shaped layer (q/k/v/o and
+    """The seven projections of a Qwen2.5-7B-shaped layer (q/k/v/o and
     gate/up Q4_K, down Q6_K), output rows sharded over the ranks.  Each rank
     computes its rows (GEMV at B=1, tcgen05 GEMM at B=64 and 512), then the
     outputs are exchanged over NVLink: by default each rank's own kernel writes
@@ -526,8 +526,8 @@ def layer7b_workload(ctx, args, rank, world, reps=5):
 
 def gemv_shapes_workload(ctx, args):
     """Sweep of the GEMV launch shape (rows per CTA x thread cap, through the
-    HACEDLE_GEMV_RC / HACEDLE_GEMV_NT planner overrides) for the config-2
-    matrices and the tied LM head: microseconds per launch in a CUDA-graph
+    HACEDLE_GEMV_RC / HACEDLE_GEMV_NT planner overrides) for the sweep's
+    matrices (Q5_0 4864x896, Q6_K/Q4_K 896x4864) and the tied LM head: microseconds per launch in a CUDA-graph
     chain of launches over weight copies larger than L2 (PDL on)."""
     import torch
 
