@@ -1422,8 +1422,9 @@ int hd_tc4_min_t() {
     return env ? atoi(env) : 128;
 }
 
-// From hd_tc4_min_t() tokens the two-pass kernel; below, rows % 128 == 0 uses
-// the streamed v3 kernel, other shapes the v1 kernel.
+// From hd_tc4_min_t() tokens, and for rows % 128 != 0 at any T, the two-pass
+// kernel; below, rows % 128 == 0 uses the streamed v3 kernel (the v1 kernel
+// only runs with the two-pass kernel off, HACEDLE_TC4_MIN_T=0).
 // exact != 0 (rows % 128 == 0 only): the fp32-accuracy mode -- exact weights
 // and x, each split into fp16 hi + lo, three MMAs per product.
 int hd_qgemm_tc(hd_ctx *ctx, const hd_weight *w, const float *X, float *Y, int T, int exact) {
@@ -1435,9 +1436,13 @@ int hd_qgemm_tc(hd_ctx *ctx, const hd_weight *w, const float *X, float *Y, int T
         // oracle's greedy tokens on the 0.5B-shaped decoder, the two-pass
         // order (one K chain per tile) flips a near tie after 15 tokens.
         // HACEDLE_TC4_EXACT=1 sends it to the two-pass kernel as well.
+        // Rows not a multiple of 128 take the two-pass kernel at any T: the v1
+        // kernel it replaces there is 3-4x slower (T = 64 on the 8-rank
+        // slices of the 7B-shaped layer: 65-347 against 22-93 us).
         const int min_t = hd_tc4_min_t();
         const bool ex_v4 = w->rows % 128 != 0 || getenv("HACEDLE_TC4_EXACT") != nullptr;
-        if (min_t > 0 && T >= min_t && (!exact || ex_v4)) return qgemm_tc4(ctx, w, X, Y, T, exact);
+        if (min_t > 0 && (T >= min_t || w->rows % 128 != 0) && (!exact || ex_v4))
+            return qgemm_tc4(ctx, w, X, Y, T, exact);
     }
     cudaError_t e = cudaSuccess;
     const bool v3 = w->rows % 128 == 0 && ((uintptr_t)Y & 15) == 0 && (exact || getenv("HACEDLE_TC_V1") == nullptr);
