@@ -432,12 +432,15 @@ int env_int(const char *name, int dflt) {
     return (v && *v) ? atoi(v) : dflt;
 }
 
-// Clusters of S CTAs that fit on the device at once (0: none), per type and
-// S, asked once.
+// Clusters of S CTAs that fit on the device at once (0: none), per device,
+// type and S, asked once; the first ask on a device also sets the kernel's
+// attributes there (function attributes are per device).
+constexpr int TV_MAX_DEVICES = 64;
 template <int TYPE>
-int max_clusters(int S) {
-    static int known[TV_SMAX + 1] = {0};   // value + 1; 0 = not asked yet
-    if (known[S]) return known[S] - 1;
+int max_clusters(int device, int S) {
+    static int known[TV_MAX_DEVICES][TV_SMAX + 1] = {};   // value + 1; 0 = not asked yet
+    if (device < 0 || device >= TV_MAX_DEVICES) return 0;
+    if (known[device][S]) return known[device][S] - 1;
     cudaFuncSetAttribute(k_qgemv_tc<TYPE>, cudaFuncAttributeMaxDynamicSharedMemorySize, TV_SMEM_CAP);
     cudaFuncSetAttribute(k_qgemv_tc<TYPE>, cudaFuncAttributeNonPortableClusterSizeAllowed, 1);
     cudaLaunchConfig_t cfg = {};
@@ -456,7 +459,7 @@ int max_clusters(int S) {
         cudaGetLastError();
         n = 0;
     }
-    known[S] = n + 1;
+    known[device][S] = n + 1;
     return n;
 }
 
@@ -473,9 +476,9 @@ int run_tc(hd_ctx *ctx, const hd_weight *w, const float *x, float *y, int B, con
     S = S > units ? units : S;
     const int s_env = env_int("HACEDLE_GEMV_TC_S", 0);
     if (s_env >= 1 && s_env <= TV_SMAX && s_env <= units) S = s_env;
-    while (S >= smin && S > 1 && max_clusters<TYPE>(S) < 1) S--;
+    while (S >= smin && S > 1 && max_clusters<TYPE>(ctx->device, S) < 1) S--;
     if (S < smin || S < 1) return HD_OK;
-    if (S == 1 && max_clusters<TYPE>(1) < 1) return HD_OK;
+    if (max_clusters<TYPE>(ctx->device, 1) < 1) return HD_OK;   // also sets the attributes on this device
     TvArgs a;
     a.w = wview(w);
     a.x = x;
