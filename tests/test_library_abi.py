@@ -46,6 +46,13 @@ def test_null_arguments_are_rejected_without_a_gpu():
     assert L.hd_ctx_create(0, None) == hc.HD_E_ARG
     assert L.hd_ctx_destroy(None) == hc.HD_E_ARG
     assert L.hd_last_error(None) == b"null context"
+    # NVLink exchange entry points
+    assert L.hd_xbuf_alloc(None, 1024, None) == hc.HD_E_ARG
+    assert L.hd_xbuf_free(None, None) == hc.HD_E_ARG
+    assert L.hd_ipc_handle(None, None, None) == hc.HD_E_ARG
+    assert L.hd_ipc_open(None, None, None) == hc.HD_E_ARG
+    assert L.hd_ipc_close(None, None) == hc.HD_E_ARG
+    assert L.hd_push_columns(None, None, None, None, 2, 0, 1, 4, 1) == hc.HD_E_ARG
 
 
 def test_context_creation_fails_cleanly_without_device():
