@@ -13,18 +13,25 @@
 // per-row arrival counter.  They live in g_argmax_scratch below, a
 // file-scope __device__ array of HD_ARGMAX_NOALLOC_SCRATCH_BYTES (208 KiB)
 // that every GPU which loads this library holds until the process exits.
-// Limits: at most HD_ARGMAX_NOALLOC_MAX_ROWS rows, and rows x chunks <=
-// 16384 partials (chunks are widened to fit; n itself is not limited).
+// Limits: at most HD_ARGMAX_NOALLOC_MAX_ROWS rows, n < 2^31 (the indices
+// are int32), and rows x chunks <= 16384 partials (chunks are widened to
+// fit).
 //
 // Set-up.  In host code the array's name is only a stand-in for the device
 // address, so the first call on each device (with that device current) asks
-// the runtime for the real address with cudaGetSymbolAddress and keeps it.
-// Make that first call before any stream capture.
+// the runtime for the real address with cudaGetSymbolAddress and keeps it,
+// with the id of the context it belongs to; a call that finds a different
+// context (the device was reset) looks the address up again.  Make the
+// first call on a device, and the first after a reset, before any stream
+// capture.
 //
 // Sharing.  Every call uses the same array and leaves its contents behind;
 // the counters that must start at zero are cleared on the caller's stream
 // before each launch.  Two calls whose work overlaps on the GPU (different
 // streams without ordering between them) race on the array.
+#include <cuda.h>
+#include <stdint.h>
+
 #include <mutex>
 
 #include "hd_internal.cuh"
@@ -119,19 +126,55 @@ __global__ void __launch_bounds__(NT) k_argmax_noalloc(const float *__restrict__
 constexpr int kMaxDevices = 64;
 std::mutex g_mu;
 unsigned char *g_addr[kMaxDevices] = {};
+unsigned long long g_ctx_id[kMaxDevices] = {};  // context the address belongs to
 
-// Device address of g_argmax_scratch on the current device (looked up once).
+// Unique id of the current CUDA context (cuCtxGetId through the runtime's
+// driver entry points, so the library needs no link against libcuda); 0 if
+// it cannot be read.
+unsigned long long current_context_id() {
+    typedef CUresult (*GetCurrent)(CUcontext *);
+    typedef CUresult (*GetId)(CUcontext, unsigned long long *);
+    static GetCurrent get_current = nullptr;
+    static GetId get_id = nullptr;
+    static bool looked = false;
+    if (!looked) {
+        void *p = nullptr;
+        cudaDriverEntryPointQueryResult q;
+        if (cudaGetDriverEntryPoint("cuCtxGetCurrent", &p, cudaEnableDefault, &q) == cudaSuccess &&
+            q == cudaDriverEntryPointSuccess)
+            get_current = (GetCurrent)p;
+        if (cudaGetDriverEntryPoint("cuCtxGetId", &p, cudaEnableDefault, &q) == cudaSuccess &&
+            q == cudaDriverEntryPointSuccess)
+            get_id = (GetId)p;
+        cudaGetLastError();
+        looked = true;
+    }
+    CUcontext c = nullptr;
+    unsigned long long id = 0;
+    if (get_current && get_id && get_current(&c) == CUDA_SUCCESS && c && get_id(c, &id) == CUDA_SUCCESS) return id;
+    return 0;
+}
+
+// Device address of g_argmax_scratch on the current device: looked up once
+// per device, and again when the device's context is a new one (after
+// cudaDeviceReset the module is loaded again and the array moves).
 int scratch_address(unsigned char **out) {
     int dev = 0;
-    if (cudaGetDevice(&dev) != cudaSuccess || dev < 0 || dev >= kMaxDevices) return HD_E_CUDA;
+    if (cudaGetDevice(&dev) != cudaSuccess) {
+        cudaGetLastError();
+        return HD_E_CUDA;
+    }
+    if (dev < 0 || dev >= kMaxDevices) return HD_E_UNSUPPORTED;
     std::lock_guard<std::mutex> lk(g_mu);
-    if (!g_addr[dev]) {
+    const unsigned long long id = current_context_id();
+    if (!g_addr[dev] || (id && id != g_ctx_id[dev])) {
         void *p = nullptr;
         if (cudaGetSymbolAddress(&p, g_argmax_scratch) != cudaSuccess || !p) {
             cudaGetLastError();
             return HD_E_CUDA;
         }
         g_addr[dev] = (unsigned char *)p;
+        g_ctx_id[dev] = id;
     }
     *out = g_addr[dev];
     return HD_OK;
@@ -143,6 +186,7 @@ extern "C" int hd_argmax_rows_noalloc(const float *x_dev, int64_t rows, int64_t 
     if (!idx_dev || (rows > 0 && n > 0 && !x_dev)) return HD_E_ARG;
     if (rows < 0 || n < 0) return HD_E_ARG;
     if (rows > kMaxRows) return HD_E_SHAPE;
+    if (n > INT32_MAX) return HD_E_SHAPE;  // the indices are int32
     if (rows == 0) return HD_OK;
     cudaStream_t st = (cudaStream_t)stream;
     if (n == 0) return cudaMemsetAsync(idx_dev, 0, (size_t)rows * sizeof(int32_t), st) == cudaSuccess ? HD_OK

@@ -12,6 +12,7 @@ import pytest
 
 import hacedle_cuda as hc
 from hacedle_cuda import synth as S
+from oracle import oracle as O
 
 pytestmark = pytest.mark.gpu
 
@@ -38,7 +39,10 @@ def _reference(ctx, x, rows):
     return idx.cpu().numpy()
 
 
-@pytest.mark.parametrize("rows,n", [(1, 151936), (3, 2_000_000), (64, 100_000), (300, 8193), (5, 7)])
+# (1000, 140000): 16384 partials allow 16 chunks per row, so each of the 18
+# chunks of 8192 values is widened to 8750.
+@pytest.mark.parametrize("rows,n", [(1, 151936), (3, 2_000_000), (64, 100_000), (300, 8193), (5, 7),
+                                    (1000, 140_000)])
 def test_noalloc_argmax_matches_existing_entry_point_twice(ctx, rows, n):
     import torch
     for call in range(2):
@@ -50,6 +54,9 @@ def test_noalloc_argmax_matches_existing_entry_point_twice(ctx, rows, n):
         got = _noalloc(xd, rows, n)
         exp = _reference(ctx, xd, rows)
         assert np.array_equal(got, exp), (call, got[:8], exp[:8])
+        # and directly against the oracle's ArgMaxSampler::sample
+        assert [int(v) for v in got] == [O.argmax(x[r]) for r in range(rows)]
+        del xd
 
 
 def test_noalloc_rejects_rows_beyond_its_scratch():
@@ -58,4 +65,6 @@ def test_noalloc_rejects_rows_beyond_its_scratch():
     idx = torch.zeros(4097, dtype=torch.int32, device="cuda")
     rc = hc.lib().hd_argmax_rows_noalloc(x.data_ptr(), 4097, 16, idx.data_ptr(), _stream())
     assert rc == hc.HD_E_SHAPE
+    # indices are int32: rows of 2^31 values or more are refused before any access
+    assert hc.lib().hd_argmax_rows_noalloc(x.data_ptr(), 1, 1 << 31, idx.data_ptr(), _stream()) == hc.HD_E_SHAPE
     assert hc.lib().hd_argmax_rows_noalloc(None, 1, 16, None, None) == hc.HD_E_ARG
