@@ -34,17 +34,21 @@ def gather_columns_reference(gathered: np.ndarray, world: int, B: int, n_shard: 
     return np.ascontiguousarray(gathered.reshape(world, B, n_shard).transpose(1, 0, 2).reshape(B, world * n_shard))
 
 
-def exchange_layout(world: int, shapes: list[tuple[int, int]]) -> tuple[list[int], int]:
-    """Byte offsets of the full output buffers [B][N] (shapes) in an exchange
-    buffer that starts with the int32 flag array [world]; every region is
-    256-byte aligned.  Returns (offsets, total bytes)."""
+def exchange_layout(world: int, shapes: list[tuple[int, int]]) -> tuple[list[tuple[int, int]], int]:
+    """Byte offsets of the two full output buffers [B][N] of every entry of
+    `shapes` in an exchange buffer that starts with the int32 flag array
+    [world]; every region is 256-byte aligned.  Returns ([(offset of buffer 0,
+    offset of buffer 1)] per entry, total bytes)."""
     def up(x):
         return (x + 255) // 256 * 256
     off = up(4 * world)
     offs = []
     for B, N in shapes:
-        offs.append(off)
-        off += up(4 * B * N)
+        pair = []
+        for _ in range(2):
+            pair.append(off)
+            off += up(4 * B * N)
+        offs.append(tuple(pair))
     return offs, off
 
 
@@ -59,13 +63,19 @@ class _DeviceView:
 class PeerExchange:
     """NVLink exchange of row-sharded outputs without a collective library.
 
-    Every rank allocates one buffer (flags + a full output [B_max][N] per
+    Every rank allocates one buffer (flags + two full outputs [B_max][N] per
     entry of `shapes`), shares its IPC handle through `all_gather_object`
     (e.g. torch.distributed.all_gather_object on any backend) and maps the
     others'.  push(i, y, B, n) writes this rank's slice y [B][n] into every
-    rank's output i at columns rank*n.. and returns once all ranks' slices
-    are in this rank's output i (full(i, B) views it).  Every rank must make
-    the same sequence of push calls."""
+    rank's output i at columns rank*n.. and, on the device, completes once
+    all ranks' slices are in this rank's output i (full(i, B) views the
+    latest).  Every rank must make the same sequence of push calls.
+
+    Consecutive pushes of output i alternate between its two buffers, so a
+    push's result stays valid for every kernel this rank enqueues before its
+    next push of output i: the peers write the push after that into the same
+    buffer only once this rank's next push has raised its flag, which happens
+    after everything enqueued before it has completed."""
 
     def __init__(self, ctx, world: int, rank: int, shapes: list[tuple[int, int]], all_gather_object):
         import ctypes as C
@@ -95,15 +105,20 @@ class PeerExchange:
             self.peers.append(q.value)
             bases.append(q.value)
         self.flag_ptrs = torch.tensor(bases, dtype=torch.int64, device="cuda")
-        self.full_ptrs = [torch.tensor([b + o for b in bases], dtype=torch.int64, device="cuda") for o in self.offs]
+        # full_ptrs[i][k]: every rank's buffer k of output i, indexed by rank
+        self.full_ptrs = [[torch.tensor([b + o for b in bases], dtype=torch.int64, device="cuda") for o in pair]
+                          for pair in self.offs]
         self.epoch = 0
+        self.uses = [0] * len(self.shapes)   # pushes of each output so far
 
     def full(self, i: int, B: int):
+        """This rank's output i [B][N] as written by the latest push(i)."""
         import torch
         Bmax, N = self.shapes[i]
         if B > Bmax:
             raise ValueError(f"batch {B} beyond the exchange buffer's {Bmax}")
-        return torch.as_tensor(_DeviceView(self.base + self.offs[i], B, N), device="cuda")
+        k = (self.uses[i] + 1) % 2   # buffer of the latest push (push u uses buffer (u - 1) % 2)
+        return torch.as_tensor(_DeviceView(self.base + self.offs[i][k], B, N), device="cuda")
 
     def push(self, i: int, y, B: int, n: int):
         from . import lib
@@ -111,7 +126,9 @@ class PeerExchange:
         if B > Bmax or n * self.world != N:
             raise ValueError(f"slice [{B}][{n}] does not fit output {i} [{Bmax}][{N}] over {self.world} ranks")
         self.epoch += 1
-        self.ctx._check(lib().hd_push_columns(self.ctx.h, y.data_ptr(), self.full_ptrs[i].data_ptr(),
+        k = self.uses[i] % 2
+        self.uses[i] += 1
+        self.ctx._check(lib().hd_push_columns(self.ctx.h, y.data_ptr(), self.full_ptrs[i][k].data_ptr(),
                                               self.flag_ptrs.data_ptr(), self.world, self.rank, B, n, self.epoch))
 
     def close(self):

@@ -75,14 +75,17 @@ def test_row_range_rejects_uneven_split():
 
 
 def test_exchange_layout():
-    """PeerExchange buffer layout: the int32 flag array [world] first, then one
-    full output [B][N] per projection, each region 256-byte aligned, nothing
-    overlapping, identical on every rank (it is a function of the shapes)."""
+    """PeerExchange buffer layout: the int32 flag array [world] first, then two
+    full outputs [B][N] per projection (consecutive pushes alternate), each
+    region 256-byte aligned, nothing overlapping, identical on every rank (it
+    is a function of the shapes)."""
     from hacedle_cuda import shard
     shapes = [(512, 3584), (512, 512), (1, 33), (64, 18944)]
     for world in (1, 2, 8, 65):
         offs, total = shard.exchange_layout(world, shapes)
-        assert offs[0] >= 4 * world and all(o % 256 == 0 for o in offs)
-        ends = [o + 4 * B * N for o, (B, N) in zip(offs, shapes)]
-        assert all(e <= o2 for e, o2 in zip(ends, offs[1:]))
+        flat = [o for pair in offs for o in pair]
+        sizes = [4 * B * N for (B, N) in shapes for _ in range(2)]
+        assert flat[0] >= 4 * world and all(o % 256 == 0 for o in flat)
+        ends = [o + sz for o, sz in zip(flat, sizes)]
+        assert all(e <= o2 for e, o2 in zip(ends, flat[1:]))
         assert total >= ends[-1] and total % 256 == 0
