@@ -71,6 +71,8 @@ extern "C" int hd_ctx_destroy(hd_ctx *ctx) {
     cudaFree(ctx->xbf);
     cudaFree(ctx->wbf);
     cudaFree(ctx->samp);
+    cudaFree(ctx->kt_x);
+    cudaFree(ctx->kt_y);
     if (ctx->own_stream) cudaStreamDestroy(ctx->own_stream);
     delete ctx;
     return HD_OK;

@@ -63,14 +63,15 @@ __global__ void k_gather_last(const float *__restrict__ src, float *__restrict__
     dst[i] = src[((int64_t)s * T + T - 1) * n + j];
 }
 
-// After prefill: first generated token, positions and lengths.
+// After prefill: first generated token, positions and lengths.  With
+// teacher forcing (forced [S][n_gen]) the next input is the forced id.
 __global__ void k_start(const int32_t *amax, int32_t *tok, int32_t *pos, int32_t *lens, int32_t *step,
-                        int32_t *hist, int S, int n_prompt, int n_gen) {
+                        int32_t *hist, int S, int n_prompt, int n_gen, const int32_t *forced) {
     pdl_wait();
     pdl_trigger();
     int s = threadIdx.x + blockIdx.x * blockDim.x;
     if (s < S) {
-        tok[s] = amax[s];
+        tok[s] = forced ? forced[(int64_t)s * n_gen] : amax[s];
         hist[(int64_t)s * n_gen] = amax[s];
         pos[s] = n_prompt;
         lens[s] = n_prompt + 1;
@@ -78,16 +79,17 @@ __global__ void k_start(const int32_t *amax, int32_t *tok, int32_t *pos, int32_t
     if (s == 0) *step = 0;
 }
 
-// End of a decode step: the argmax becomes the next input and is recorded.
+// End of a decode step: the argmax is recorded and becomes the next input
+// (with teacher forcing, the forced id of this step does).
 __global__ void k_step_end(const int32_t *amax, int32_t *tok, int32_t *pos, int32_t *lens, int32_t *step,
-                           int32_t *hist, int S, int n_gen) {
+                           int32_t *hist, int S, int n_gen, const int32_t *forced) {
     pdl_wait();
     pdl_trigger();
     __shared__ int st;
     if (threadIdx.x == 0) st = *step + 1;
     __syncthreads();
     for (int s = threadIdx.x; s < S; s += blockDim.x) {
-        tok[s] = amax[s];
+        tok[s] = forced && st < n_gen ? forced[(int64_t)s * n_gen + st] : amax[s];
         if (st < n_gen) hist[(int64_t)s * n_gen + st] = amax[s];
         pos[s] += 1;
         lens[s] += 1;
@@ -214,14 +216,14 @@ int head(hd_decoder *d, const float *hid, int S, int prec) {
     return rc;
 }
 
-int decode_step(hd_decoder *d, int S, int n_gen, int prec) {
+int decode_step(hd_decoder *d, int S, int n_gen, int prec, const int32_t *forced) {
     hd_ctx *ctx = d->ctx;
     int rc = hd_embed(ctx, d->embed, d->tok, S, d->h);
     for (int li = 0; !rc && li < d->c.n_layers; li++) rc = layer_forward(d, li, S, d->pos, d->lens, S, 1, prec, nullptr);
     if (!rc) rc = head(d, d->h, S, prec);
     if (rc) return rc;
     HD_CUDA_TRY(ctx, hd_launch(ctx, k_step_end, dim3(1), dim3(256), 0, (const int32_t *)d->amax, d->tok, d->pos,
-                               d->lens, d->step, d->hist, S, n_gen));
+                               d->lens, d->step, d->hist, S, n_gen, forced));
     return HD_OK;
 }
 
@@ -330,6 +332,12 @@ extern "C" int hd_decoder_free(hd_decoder *d) {
 
 extern "C" int hd_decoder_generate(hd_decoder *d, const int32_t *prompts, int S, int n_prompt, int n_gen, int prec,
                                    int32_t *out, float *decode_ms, float *prefill_ms) {
+    return hd_decoder_generate_ex(d, prompts, S, n_prompt, n_gen, prec, nullptr, out, nullptr, decode_ms, prefill_ms);
+}
+
+extern "C" int hd_decoder_generate_ex(hd_decoder *d, const int32_t *prompts, int S, int n_prompt, int n_gen,
+                                      int prec, const int32_t *forced_host, int32_t *out, float *logits_host,
+                                      float *decode_ms, float *prefill_ms) {
     if (!d || !prompts || !out) return d ? hd_fail(d->ctx, HD_E_ARG, "hd_decoder_generate: null argument") : HD_E_ARG;
     hd_ctx *ctx = d->ctx;
     const hd_decoder_config &c = d->c;
@@ -360,7 +368,8 @@ extern "C" int hd_decoder_generate(hd_decoder *d, const int32_t *prompts, int S,
     size_t tmpn = (size_t)Rm * (c.ffn > c.hidden ? c.ffn : c.hidden);
     if (!rc) rc = dalloc(d, &d->tmp, tmpn);
     if (!rc) rc = dalloc(d, &d->logits, (size_t)S * c.vocab);
-    int32_t *ids = nullptr, *ppos = nullptr, *zero = nullptr;
+    int32_t *ids = nullptr, *ppos = nullptr, *zero = nullptr, *forced = nullptr;
+    if (!rc && forced_host) rc = dalloc(d, &forced, (size_t)S * n_gen);
     if (!rc) rc = dalloc(d, &ids, (size_t)R);
     if (!rc) rc = dalloc(d, &ppos, (size_t)R);
     if (!rc) rc = dalloc(d, &zero, (size_t)S);
@@ -399,7 +408,9 @@ extern "C" int hd_decoder_generate(hd_decoder *d, const int32_t *prompts, int S,
             break;
         if (cudaMemcpyAsync(ids, prompts, (size_t)R * 4, cudaMemcpyHostToDevice, st) != cudaSuccess ||
             cudaMemcpyAsync(ppos, hp.data(), (size_t)R * 4, cudaMemcpyHostToDevice, st) != cudaSuccess ||
-            cudaMemsetAsync(zero, 0, (size_t)S * 4, st) != cudaSuccess) {
+            cudaMemsetAsync(zero, 0, (size_t)S * 4, st) != cudaSuccess ||
+            (forced && cudaMemcpyAsync(forced, forced_host, (size_t)S * n_gen * 4, cudaMemcpyHostToDevice, st) !=
+                           cudaSuccess)) {
             rc = hd_fail(ctx, HD_E_CUDA, "hd_decoder_generate: staging copies failed");
             break;
         }
@@ -416,11 +427,17 @@ extern "C" int hd_decoder_generate(hd_decoder *d, const int32_t *prompts, int S,
         if ((rc = head(d, d->tmp, S, HD_PREC_FP32))) break;
         if (cudaSuccess != hd_launch(ctx, k_start, dim3((unsigned)((S + 255) / 256)), dim3(256), 0,
                                      (const int32_t *)d->amax, d->tok, d->pos, d->lens, d->step, d->hist, S, n_prompt,
-                                     n_gen)) {
+                                     n_gen, (const int32_t *)forced)) {
             rc = hd_fail(ctx, HD_E_CUDA, "hd_decoder_generate: start");
             break;
         }
         cudaEventRecord(e1, st);
+        const size_t step_logits = (size_t)S * c.vocab;
+        if (logits_host && cudaMemcpyAsync(logits_host, d->logits, step_logits * 4, cudaMemcpyDeviceToHost, st) !=
+                               cudaSuccess) {
+            rc = hd_fail(ctx, HD_E_CUDA, "hd_decoder_generate: logits copy");
+            break;
+        }
         if (cudaStreamSynchronize(st) != cudaSuccess) {
             rc = hd_fail(ctx, HD_E_CUDA, "hd_decoder_generate: prefill: %s", cudaGetErrorString(cudaGetLastError()));
             break;
@@ -433,7 +450,7 @@ extern "C" int hd_decoder_generate(hd_decoder *d, const int32_t *prompts, int S,
                 rc = hd_fail(ctx, HD_E_CUDA, "hd_decoder_generate: begin capture");
                 break;
             }
-            rc = decode_step(d, S, n_gen, HD_PREC_FP32);
+            rc = decode_step(d, S, n_gen, HD_PREC_FP32, forced);
             cudaError_t ce = cudaStreamEndCapture(st, &graph);
             cudaGetLastError();
             if (rc) break;
@@ -445,6 +462,11 @@ extern "C" int hd_decoder_generate(hd_decoder *d, const int32_t *prompts, int S,
             for (int i = 0; i < n_gen - 1; i++) {
                 if (cudaGraphLaunch(exec, st) != cudaSuccess) {
                     rc = hd_fail(ctx, HD_E_CUDA, "hd_decoder_generate: graph launch");
+                    break;
+                }
+                if (logits_host && cudaMemcpyAsync(logits_host + (size_t)(i + 1) * step_logits, d->logits,
+                                                   step_logits * 4, cudaMemcpyDeviceToHost, st) != cudaSuccess) {
+                    rc = hd_fail(ctx, HD_E_CUDA, "hd_decoder_generate: logits copy");
                     break;
                 }
             }

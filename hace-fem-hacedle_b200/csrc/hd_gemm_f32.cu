@@ -180,6 +180,71 @@ extern "C" int hd_qgemm_host(hd_ctx *ctx, const hd_weight *w, const float *X_hos
     return hd_ctx_check_device_errors(ctx);
 }
 
+namespace {
+
+// dst [C][R] = src [R][C] transposed, 32 x 32 tiles through shared memory
+// (one padding column, so the column reads do not share banks).
+__global__ void __launch_bounds__(256) k_transpose(const float *__restrict__ src, float *__restrict__ dst, int64_t R,
+                                                   int64_t C) {
+    __shared__ float tile[32][33];
+    pdl_wait();
+    pdl_trigger();
+    const int64_t r0 = (int64_t)blockIdx.y * 32, c0 = (int64_t)blockIdx.x * 32;
+    const int tx = threadIdx.x & 31, ty = threadIdx.x >> 5;
+    for (int i = ty; i < 32; i += 8) {
+        const int64_t r = r0 + i, c = c0 + tx;
+        if (r < R && c < C) tile[i][tx] = src[r * C + c];
+    }
+    __syncthreads();
+    for (int i = ty; i < 32; i += 8) {
+        const int64_t c = c0 + i, r = r0 + tx;
+        if (r < R && c < C) dst[c * R + r] = tile[tx][i];
+    }
+}
+
+int transpose(hd_ctx *ctx, const float *src, float *dst, int64_t R, int64_t C) {
+    if (R == 0 || C == 0) return HD_OK;
+    HD_REQUIRE(ctx, (R + 31) / 32 < 65536, HD_E_SHAPE, "transpose: %lld rows", (long long)R);
+    HD_CUDA_TRY(ctx, hd_launch(ctx, k_transpose, dim3((unsigned)((C + 31) / 32), (unsigned)((R + 31) / 32)), dim3(256),
+                               0, src, dst, R, C));
+    return HD_OK;
+}
+
+}  // namespace
+
+// Y [N][T] = W X for X [K][T] (the [k, n] operand layout of
+// ComputeBackend::matmul_q4k/q6k): X is copied to token-major [T][K] on the
+// device, hd_qgemm runs, and its [T][N] result is copied to [N][T].
+extern "C" int hd_qgemm_kt(hd_ctx *ctx, const hd_weight *w, const float *X_kt, float *Y_nt, int T, int precision) {
+    if (!ctx || !w || !X_kt || !Y_nt) return hd_fail(ctx, HD_E_ARG, "hd_qgemm_kt: null argument");
+    HD_REQUIRE(ctx, T >= 0, HD_E_ARG, "hd_qgemm_kt: T < 0");
+    if (T == 0) return HD_OK;
+    const size_t xb = (size_t)T * w->cols * sizeof(float), yb = (size_t)T * w->rows * sizeof(float);
+    int rc = hd_ensure_hbuf(ctx, &ctx->kt_x, &ctx->kt_x_bytes, xb);
+    if (!rc) rc = hd_ensure_hbuf(ctx, &ctx->kt_y, &ctx->kt_y_bytes, yb);
+    if (!rc) rc = transpose(ctx, X_kt, ctx->kt_x, w->cols, T);
+    if (!rc) rc = hd_qgemm(ctx, w, ctx->kt_x, ctx->kt_y, T, precision);
+    if (!rc) rc = transpose(ctx, ctx->kt_y, Y_nt, T, w->rows);
+    return rc;
+}
+
+extern "C" int hd_qgemm_kt_host(hd_ctx *ctx, const hd_weight *w, const float *X_kt_host, float *Y_nt_host, int T,
+                                int precision) {
+    if (!ctx || !w || !X_kt_host || !Y_nt_host) return hd_fail(ctx, HD_E_ARG, "hd_qgemm_kt_host: null argument");
+    HD_REQUIRE(ctx, T >= 0, HD_E_ARG, "hd_qgemm_kt_host: T < 0");
+    if (T == 0) return HD_OK;
+    const size_t xb = (size_t)T * w->cols * sizeof(float), yb = (size_t)T * w->rows * sizeof(float);
+    int rc = hd_ensure_hbuf(ctx, &ctx->hbuf_x, &ctx->hbuf_x_bytes, xb);
+    if (!rc) rc = hd_ensure_hbuf(ctx, &ctx->hbuf_y, &ctx->hbuf_y_bytes, yb);
+    if (rc) return rc;
+    HD_CUDA_TRY(ctx, cudaMemcpyAsync(ctx->hbuf_x, X_kt_host, xb, cudaMemcpyHostToDevice, ctx->stream));
+    rc = hd_qgemm_kt(ctx, w, ctx->hbuf_x, ctx->hbuf_y, T, precision);
+    if (rc) return rc;
+    HD_CUDA_TRY(ctx, cudaMemcpyAsync(Y_nt_host, ctx->hbuf_y, yb, cudaMemcpyDeviceToHost, ctx->stream));
+    HD_CUDA_TRY(ctx, cudaStreamSynchronize(ctx->stream));
+    return hd_ctx_check_device_errors(ctx);
+}
+
 extern "C" int hd_matmul_f32(hd_ctx *ctx, const float *a, const float *b, float *out, int64_t m, int64_t n,
                              int64_t k) {
     if (!ctx || !a || !b || !out) return hd_fail(ctx, HD_E_ARG, "hd_matmul_f32: null argument");

@@ -58,6 +58,8 @@ struct hd_ctx {
     size_t wbf_bytes = 0;
     float *samp = nullptr;           // logits processor: sorted rows, segment offsets, sort scratch
     size_t samp_bytes = 0;
+    float *kt_x = nullptr, *kt_y = nullptr;   // token-major copies for the [K][T] Q-GEMM entry points
+    size_t kt_x_bytes = 0, kt_y_bytes = 0;
 };
 
 struct hd_weight {
@@ -119,6 +121,16 @@ int hd_attention_run(hd_ctx *ctx, const float *q, int64_t qld, const float *kc, 
 // w_up != null: SwiGLU pair.
 int hd_qgemv_norm(hd_ctx *ctx, const hd_weight *w, const hd_weight *w_up, const float *x, const float *norm_w,
                   float eps, float *y, int B, const float *bias, const float *residual);
+// Streamed Q-GEMV at batch 1..4 (hd_gemv_sk.cu): y = W x (+bias, +residual);
+// the weight must satisfy hd_qgemv_sk_fits (cols % 128 == 0).
+bool hd_qgemv_sk_fits(const hd_weight *w);
+// Q-GEMV at batch 1..4 with the products on the tensor cores (hd_gemv_mma.cu);
+// the weight must satisfy hd_qgemv_mma_fits.
+bool hd_qgemv_mma_fits(const hd_weight *w);
+int hd_qgemv_mma(hd_ctx *ctx, const hd_weight *w, const float *x, float *y, int B, const float *bias,
+                 const float *residual, const char *name);
+int hd_qgemv_sk(hd_ctx *ctx, const hd_weight *w, const float *x, float *y, int B, const float *bias,
+                const float *residual, const char *name);
 // Q-GEMV at batch 5..16 on the tensor cores (hd_gemv_tc.cu).  *done = false
 // (and HD_OK) when the batch or shape is outside what the kernel takes; the
 // caller then runs the CUDA-core kernels.

@@ -27,11 +27,12 @@ EXPORTS = [
     "hd_ctx_create", "hd_ctx_destroy", "hd_ctx_set_stream", "hd_ctx_synchronize", "hd_ctx_reserve_workspace",
     "hd_last_error", "hd_ctx_launch_count", "hd_version", "hd_ctx_check_device_errors",
     "hd_weight_upload", "hd_weight_upload_device", "hd_weight_free", "hd_weight_info", "hd_weight_download",
-    "hd_dequantize", "hd_qgemv", "hd_qgemv_swiglu", "hd_qgemv_rmsnorm", "hd_qgemv_host", "hd_qgemm", "hd_qgemm_host", "hd_matmul_f32",
+    "hd_dequantize", "hd_qgemv", "hd_qgemv_swiglu", "hd_qgemv_rmsnorm", "hd_qgemv_host", "hd_qgemm", "hd_qgemm_host",
+    "hd_qgemm_kt", "hd_qgemm_kt_host", "hd_matmul_f32",
     "hd_rmsnorm", "hd_rmsnorm_graph", "hd_rope_neox", "hd_rope_interleaved", "hd_softmax_rows", "hd_swiglu",
     "hd_add", "hd_argmax_rows", "hd_argmax_rows_noalloc", "hd_embed", "hd_kv_append", "hd_attention_decode", "hd_attention_prefill",
     "hd_dot_i8", "hd_fused_qdot_qadd_qacc_i8", "hd_gather_columns", "hd_decoder_create", "hd_decoder_free", "hd_decoder_generate",
-    "hd_gguf_open", "hd_gguf_open_memory", "hd_gguf_close", "hd_gguf_error", "hd_gguf_counts", "hd_gguf_tensor",
+    "hd_decoder_generate_ex", "hd_gguf_open", "hd_gguf_open_memory", "hd_gguf_close", "hd_gguf_error", "hd_gguf_counts", "hd_gguf_tensor",
     "hd_gguf_find_tensor", "hd_gguf_kv", "hd_gguf_find_key", "hd_gguf_kv_int", "hd_gguf_kv_float", "hd_gguf_kv_string",
     "hd_gguf_kv_array", "hd_gguf_upload", "hd_logits_process", "hd_sample_rows",
     "hd_xbuf_alloc", "hd_xbuf_free", "hd_ipc_handle", "hd_ipc_open", "hd_ipc_close", "hd_push_columns",
@@ -70,7 +71,8 @@ def lib() -> C.CDLL:
         "hd_weight_download": [V, V, V, SZ], "hd_dequantize": [V, V, V, SZ],
         "hd_qgemv": [V, V, V, V, I, V, V], "hd_qgemv_swiglu": [V, V, V, V, V, I], "hd_qgemv_host": [V, V, V, V, I],
         "hd_qgemv_rmsnorm": [V, V, V, V, V, F, V, I, V, V],
-        "hd_qgemm": [V, V, V, V, I, I], "hd_qgemm_host": [V, V, V, V, I, I], "hd_matmul_f32": [V, V, V, V, I64, I64, I64],
+        "hd_qgemm": [V, V, V, V, I, I], "hd_qgemm_host": [V, V, V, V, I, I],
+        "hd_qgemm_kt": [V, V, V, V, I, I], "hd_qgemm_kt_host": [V, V, V, V, I, I], "hd_matmul_f32": [V, V, V, V, I64, I64, I64],
         "hd_rmsnorm": [V, V, V, V, V, I64, I, F], "hd_rmsnorm_graph": [V, V, V, V, I64, I, F],
         "hd_rope_neox": [V, V, V, I, I, I, F], "hd_rope_interleaved": [V, V, V, V, V, I64, I],
         "hd_softmax_rows": [V, V, I64, I], "hd_swiglu": [V, V, V, V, I64], "hd_add": [V, V, V, V, I64],
@@ -86,6 +88,7 @@ def lib() -> C.CDLL:
         "hd_dot_i8": [V, V, V, I64, I, V], "hd_fused_qdot_qadd_qacc_i8": [V, V, V, I64, I, V, V, V],
         "hd_decoder_create": [V, V, V, V, V, C.POINTER(V)], "hd_decoder_free": [V],
         "hd_decoder_generate": [V, V, I, I, I, I, V, V, V],
+        "hd_decoder_generate_ex": [V, V, I, I, I, I, V, V, V, V, V],
         "hd_gguf_open": [C.c_char_p, C.POINTER(V)], "hd_gguf_open_memory": [V, SZ, C.POINTER(V)], "hd_gguf_close": [V],
         "hd_gguf_error": [], "hd_gguf_counts": [V, V, V, V, V], "hd_gguf_tensor": [V, I64, V],
         "hd_gguf_find_tensor": [V, C.c_char_p, V], "hd_gguf_kv": [V, I64, V, V, V, V],
@@ -255,6 +258,16 @@ class Context:
         X = np.ascontiguousarray(X, np.float32).reshape(-1, w.cols)
         Y = np.zeros((X.shape[0], w.rows), np.float32)
         self._check(lib().hd_qgemm_host(self.h, w.h, X.ctypes.data, Y.ctypes.data, X.shape[0], precision))
+        return Y
+
+    def qgemm_kt(self, w: Weight, X_kt, Y_nt, precision: int = PREC_FP32):
+        """Y_nt [N][T] = W X_kt for X_kt [K][T] (ComputeBackend::matmul_q4k's layout)."""
+        self._check(lib().hd_qgemm_kt(self.h, w.h, _ptr(X_kt), _ptr(Y_nt), X_kt.shape[1], precision))
+
+    def qgemm_kt_host(self, w: Weight, X_kt: np.ndarray, precision: int = PREC_FP32) -> np.ndarray:
+        X_kt = np.ascontiguousarray(X_kt, np.float32).reshape(w.cols, -1)
+        Y = np.zeros((w.rows, X_kt.shape[1]), np.float32)
+        self._check(lib().hd_qgemm_kt_host(self.h, w.h, X_kt.ctypes.data, Y.ctypes.data, X_kt.shape[1], precision))
         return Y
 
     def matmul_f32(self, a, b, out):
@@ -462,6 +475,24 @@ class Decoder:
         self.ctx._check(lib().hd_decoder_generate(self.h, p.ctypes.data, p.shape[0], p.shape[1], n_gen, precision,
                                                   out.ctypes.data, C.byref(dm), C.byref(pm)))
         return out, dm.value, pm.value
+
+    def generate_forced(self, prompts: np.ndarray, forced: np.ndarray | None, n_gen: int,
+                        precision: int = PREC_FP32):
+        """Teacher-forced decode (hd_decoder_generate_ex): the input of step g
+        >= 1 is forced[s, g - 1] (forced None: the greedy ids, as generate).
+        Returns (greedy ids [seqs, n_gen], logits [n_gen, seqs, vocab],
+        decode_ms, prefill_ms)."""
+        p = np.ascontiguousarray(prompts, np.int32)
+        if p.ndim == 1:
+            p = p[None]
+        f = None if forced is None else np.ascontiguousarray(forced, np.int32).reshape(p.shape[0], n_gen)
+        out = np.zeros((p.shape[0], n_gen), np.int32)
+        logits = np.zeros((n_gen, p.shape[0], self.cfg["vocab"]), np.float32)
+        dm, pm = C.c_float(), C.c_float()
+        self.ctx._check(lib().hd_decoder_generate_ex(self.h, p.ctypes.data, p.shape[0], p.shape[1], n_gen, precision,
+                                                     None if f is None else f.ctypes.data, out.ctypes.data,
+                                                     logits.ctypes.data, C.byref(dm), C.byref(pm)))
+        return out, logits, dm.value, pm.value
 
     def free(self):
         if getattr(self, "h", None) and getattr(self.ctx, "h", None):

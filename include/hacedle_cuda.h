@@ -135,6 +135,16 @@ int hd_qgemm(hd_ctx *ctx, const hd_weight *w, const float *X_dev, float *Y_dev, 
              int precision);
 int hd_qgemm_host(hd_ctx *ctx, const hd_weight *w, const float *X_host, float *Y_host, int T,
                   int precision);
+/* The same product in the operand layout of ComputeBackend::matmul_q4k /
+ * matmul_q6k (src/quant_view/dequant_dispatcher.rs:10-48): a = the quantized
+ * weight [N][K], b = X_kt [K][T] (b[l][j] at X_kt[l*T + j]), output Y_nt
+ * [N][T] (out[i][j] at Y_nt[i*T + j]).  The operands are rearranged on the
+ * device around hd_qgemm; a caller holding b quantized dequantizes it first
+ * (hd_dequantize of a [K][T] weight gives exactly this layout).  _host: host
+ * buffers, copies in and out and a synchronization inside the call. */
+int hd_qgemm_kt(hd_ctx *ctx, const hd_weight *w, const float *X_kt_dev, float *Y_nt_dev, int T, int precision);
+int hd_qgemm_kt_host(hd_ctx *ctx, const hd_weight *w, const float *X_kt_host, float *Y_nt_host, int T,
+                     int precision);
 /* Dense f32 GEMM, out[m][n] = sum_k a[m][k] b[k][n] (core/ops/matmul.rs:16-51,
  * ComputeBackend::matmul_f32 dequant_dispatcher.rs:72-83). */
 int hd_matmul_f32(hd_ctx *ctx, const float *a_dev, const float *b_dev, float *out_dev, int64_t m,
@@ -175,10 +185,12 @@ int hd_argmax_rows(hd_ctx *ctx, const float *x_dev, int64_t rows, int64_t n, int
  * cudaStream_t; NULL = the legacy default stream) for the current device.
  * Its scratch is one static device array of HD_ARGMAX_NOALLOC_SCRATCH_BYTES
  * that each GPU loading the library keeps until exit.  rows above
- * HD_ARGMAX_NOALLOC_MAX_ROWS are rejected with HD_E_SHAPE (n is not limited).
- * The first call on a device looks up the array's device address
- * (cudaGetSymbolAddress) and should come before any stream capture.  All
- * calls share the array: calls that overlap on the GPU race. */
+ * HD_ARGMAX_NOALLOC_MAX_ROWS, and n of 2^31 or more (the indices are int32),
+ * are rejected with HD_E_SHAPE; a device index of 64 or more gives
+ * HD_E_UNSUPPORTED.  The first call on a device looks up the array's device
+ * address (cudaGetSymbolAddress), and so does the first call after the
+ * device was reset (cudaDeviceReset); make those calls before any stream
+ * capture.  All calls share the array: calls that overlap on the GPU race. */
 #define HD_ARGMAX_NOALLOC_MAX_ROWS 4096
 #define HD_ARGMAX_NOALLOC_SCRATCH_BYTES 212992
 int hd_argmax_rows_noalloc(const float *x_dev, int64_t rows, int64_t n, int32_t *idx_dev, void *stream);
@@ -211,8 +223,15 @@ int hd_gather_columns(hd_ctx *ctx, const float *src_dev, float *dst_dev, int G, 
  * aligned.  Every rank makes the same sequence of calls with the same,
  * growing epochs (> 0).  The wait is bounded (about 1 s): on expiry the
  * context's device error flag holds HD_E_TIMEOUT (hd_ctx_check_device_errors).
- * A rank must not start the next exchange into a full buffer while some rank
- * still reads that buffer's previous contents. */
+ * Reuse: give each output two full buffers and alternate them between
+ * consecutive exchanges of that output (hacedle_cuda.shard.PeerExchange does).
+ * Then no peer overwrites what a rank still reads: a peer writes exchange
+ * u + 2 of an output into the buffer that holds exchange u only after its own
+ * exchange u + 1 has seen this rank's flag, which this rank raises only after
+ * every kernel it enqueued before that exchange has completed (the kernel
+ * waits for its stream predecessors before it stores).  So the result of an
+ * exchange stays valid for every kernel a rank enqueues before its next
+ * exchange of the same output. */
 #define HD_IPC_HANDLE_BYTES 64
 int hd_xbuf_alloc(hd_ctx *ctx, size_t bytes, void **dev_ptr);
 int hd_xbuf_free(hd_ctx *ctx, void *dev_ptr);
@@ -282,6 +301,17 @@ int hd_decoder_free(hd_decoder *dec);
 int hd_decoder_generate(hd_decoder *dec, const int32_t *prompts_host, int seqs, int n_prompt,
                         int n_gen, int prefill_precision, int32_t *out_host, float *decode_ms_out,
                         float *prefill_ms_out);
+/* hd_decoder_generate with two additions (either may be NULL):
+ * forced_host [seqs][n_gen]: teacher forcing -- the input of decode step g
+ * (g >= 1) is forced_host[s][g - 1] instead of the previous greedy id; out_host
+ * still receives the greedy id of every step (the argmax of its logits).
+ * logits_host [n_gen][seqs][vocab]: the logits of every step (row g chose
+ * out_host[s][g]): LMHead::forward's output (src/x/provider/candle/lmhead.rs:22-38)
+ * for each generated position.  Copying the logits out adds a device-to-host
+ * copy per step to the decode time. */
+int hd_decoder_generate_ex(hd_decoder *dec, const int32_t *prompts_host, int seqs, int n_prompt,
+                           int n_gen, int prefill_precision, const int32_t *forced_host, int32_t *out_host,
+                           float *logits_host, float *decode_ms_out, float *prefill_ms_out);
 
 /* ------------------------------------------------------ Q8_1 integer path */
 /* Activations as 8-bit blocks of 32 (48 bytes each, 16-byte aligned):

@@ -547,9 +547,29 @@ static void decoder_step(const hdo_model_cfg *c, const hdo_layer_w *L, const flo
  * (ArgMaxSampler).  The LM head is the tied f32 embedding.  out_tokens gets
  * n_gen ids; if last_logits is not NULL it receives the logits that chose the
  * final id.  Returns 0, or -1 on a bad size or allocation failure. */
+int hdo_decoder_generate_all(const hdo_model_cfg *c, const hdo_layer_w *L, const float *out_norm,
+                             const float *embed, const int32_t *prompt, int n_prompt, int n_gen,
+                             int32_t *out_tokens, float *all_logits, int threads);
+
 int hdo_decoder_generate(const hdo_model_cfg *c, const hdo_layer_w *L, const float *out_norm,
                          const float *embed, const int32_t *prompt, int n_prompt, int n_gen,
                          int32_t *out_tokens, float *last_logits, int threads) {
+    float *all = NULL;
+    if (last_logits && n_gen > 0) {
+        all = (float *)malloc((size_t)n_gen * c->vocab * sizeof(float));
+        if (!all) return -1;
+    }
+    int rc = hdo_decoder_generate_all(c, L, out_norm, embed, prompt, n_prompt, n_gen, out_tokens, all, threads);
+    if (rc == 0 && all) memcpy(last_logits, all + (size_t)(n_gen - 1) * c->vocab, (size_t)c->vocab * sizeof(float));
+    free(all);
+    return rc;
+}
+
+/* The same, keeping the logits that chose every generated id: all_logits
+ * [n_gen][vocab] (row g chose out_tokens[g]), or NULL. */
+int hdo_decoder_generate_all(const hdo_model_cfg *c, const hdo_layer_w *L, const float *out_norm,
+                             const float *embed, const int32_t *prompt, int n_prompt, int n_gen,
+                             int32_t *out_tokens, float *all_logits, int threads) {
     if (n_prompt < 1 || n_prompt + n_gen > c->max_ctx || c->head_dim > 1024) return -1;
     set_threads(threads);
     size_t kv = (size_t)c->n_layers * c->max_ctx * c->n_kv * c->head_dim;
@@ -564,10 +584,10 @@ int hdo_decoder_generate(const hdo_model_cfg *c, const hdo_layer_w *L, const flo
     for (int g = 0; g < n_gen; g++) {
         int32_t next = (int32_t)hdo_argmax(logits, c->vocab);
         out_tokens[g] = next;
+        if (all_logits) memcpy(all_logits + (size_t)g * c->vocab, logits, (size_t)c->vocab * sizeof(float));
         if (g + 1 < n_gen)
             decoder_step(c, L, out_norm, embed, next, n_prompt + g, kc, vc, logits, ws);
     }
-    if (last_logits) memcpy(last_logits, logits, (size_t)c->vocab * sizeof(float));
     free(kc); free(vc); free(ws); free(logits);
     return 0;
 }

@@ -73,9 +73,9 @@ def lib():
         L.hdo_quantize_q8_1.argtypes = [_f32p, C.c_int64, _i8p, _f32p, _i32p]
         L.hdo_qgemv_q8_1.restype = C.c_int
         L.hdo_qgemv_q8_1.argtypes = [C.c_int, _u8p, C.c_int64, C.c_int64, _i8p, _f32p, _i32p, C.c_int, _f32p]
-        L.hdo_decoder_generate.restype = C.c_int
-        L.hdo_decoder_generate.argtypes = [C.c_void_p, C.c_void_p, _f32p, _f32p, _i32p, C.c_int,
-                                           C.c_int, _i32p, _f32p, C.c_int]
+        for fn in (L.hdo_decoder_generate, L.hdo_decoder_generate_all):
+            fn.restype = C.c_int
+            fn.argtypes = [C.c_void_p, C.c_void_p, _f32p, _f32p, _i32p, C.c_int, C.c_int, _i32p, _f32p, C.c_int]
         _lib = L
     return _lib
 
@@ -255,12 +255,14 @@ class _Layer(C.Structure):
 
 
 def decoder_generate(cfg: dict, layers: list, out_norm, embed, prompt, n_gen: int, threads: int = 8,
-                     return_logits: bool = False):
+                     return_logits: bool = False, all_logits: bool = False):
     """Prefill `prompt` token by token, then greedy-decode `n_gen` ids.
 
     cfg: hidden, n_layers, n_heads, n_kv, head_dim, ffn, vocab, eps, theta.
     layers: list of dicts of f32 arrays (attn_norm, ffn_norm, wq, bq, wk, bk, wv, bv, wo, wg, wu, wd),
-    already dequantized.  embed: f32 [vocab, hidden] (tied LM head)."""
+    already dequantized.  embed: f32 [vocab, hidden] (tied LM head).
+    return_logits: also the logits that chose the last id; all_logits: also
+    the logits of every step, [n_gen, vocab] (row g chose id g)."""
     prompt = np.ascontiguousarray(prompt, dtype=np.int32)
     c = _Cfg(cfg["hidden"], cfg["n_layers"], cfg["n_heads"], cfg["n_kv"], cfg["head_dim"], cfg["ffn"],
              cfg["vocab"], prompt.size + n_gen, cfg["eps"], cfg["theta"])
@@ -273,13 +275,17 @@ def decoder_generate(cfg: dict, layers: list, out_norm, embed, prompt, n_gen: in
             setattr(arr[i], name[0], _p(a, _f32p))
     on, em = _f32(out_norm), _f32(embed)
     out = np.zeros(n_gen, np.int32)
-    logits = np.zeros(cfg["vocab"], np.float32) if return_logits else None
-    rc = lib().hdo_decoder_generate(C.addressof(c), C.addressof(arr), _p(on, _f32p), _p(em, _f32p),
-                                    _p(prompt, _i32p), prompt.size, n_gen, _p(out, _i32p),
-                                    _p(logits, _f32p) if logits is not None else None, threads)
+    if all_logits:
+        logits = np.zeros((n_gen, cfg["vocab"]), np.float32)
+        fn = lib().hdo_decoder_generate_all
+    else:
+        logits = np.zeros(cfg["vocab"], np.float32) if return_logits else None
+        fn = lib().hdo_decoder_generate
+    rc = fn(C.addressof(c), C.addressof(arr), _p(on, _f32p), _p(em, _f32p), _p(prompt, _i32p), prompt.size, n_gen,
+            _p(out, _i32p), _p(logits, _f32p) if logits is not None else None, threads)
     if rc != 0:
         raise RuntimeError("oracle: decoder_generate failed")
-    return (out, logits) if return_logits else out
+    return (out, logits) if (return_logits or all_logits) else out
 
 
 def dequant_model(model: dict):

@@ -1,9 +1,10 @@
 """Regenerates the committed golden fixtures in this folder.
 
-Run in a container that has the reference checkout at /root/reference and the
-gguf package (gguf-py 0.19.0, the version the reference's own goldens cite in
-tests/golden/manifest.yaml:6).  Nothing at test time reads /root/reference;
-the tests read only the files written here.
+Usage: python make_golden.py REFERENCE_CHECKOUT -- the path of a checkout of
+the reference repository -- with the gguf package installed (gguf-py 0.19.0,
+the version the reference's own goldens cite in tests/golden/manifest.yaml:6).
+Nothing at test time reads the reference checkout; the tests read only the
+files written here.
 
 Fixtures:
   ref_<type>_block.raw / .f32   one real GGUF block and its gguf-py dequant,
@@ -37,7 +38,7 @@ import sys
 import numpy as np
 
 HERE = os.path.dirname(os.path.abspath(__file__))
-REF = "/root/reference"
+REF = ""  # the reference checkout, from the command line
 sys.path[:0] = [os.path.join(HERE, "..", "..", "hace-fem-hacedle_b200", "python")]
 
 from hacedle_cuda import synth as S  # noqa: E402
@@ -130,4 +131,7 @@ def _edge_blocks(t: int) -> np.ndarray:
 
 
 if __name__ == "__main__":
+    if len(sys.argv) != 2 or not os.path.isdir(sys.argv[1]):
+        sys.exit("usage: python make_golden.py REFERENCE_CHECKOUT")
+    REF = sys.argv[1]
     main()

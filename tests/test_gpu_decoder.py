@@ -1,8 +1,12 @@
 """The device decoder (hd_decoder_*) against the oracle's greedy tokens.
 
 The fp32 path (exact dequantized weights, fp32 accumulation everywhere) must
-reproduce the oracle's greedy tokens exactly.  The bf16 tensor-core prefill
-is reported by its agreement with them.
+reproduce the oracle's greedy tokens exactly.  Teacher-forced runs compare
+every step's logits with the oracle's, with a bound that follows each step's
+conditioning (the oracle's own sensitivity to a one-ulp change).  The bf16
+tensor-core prefill meets the 2e-2 contract at the well-conditioned steps;
+at an ill-conditioned step its rounding of the prompt's projections can flip
+a greedy id, which the free-running bf16 test reports.
 """
 import json
 import os
@@ -55,9 +59,93 @@ def test_q05b_greedy_tokens_match_oracle_golden(ctx, golden_dir):
     prompt = S.gen_prompt(gold["n_prompt"], S.QWEN05B["vocab"], seed=4)
     dec = hc.Decoder(ctx, model, max_ctx=gold["n_prompt"] + gold["n_gen"], max_seqs=1)
     toks, dms, pms = dec.generate(prompt[None], gold["n_gen"])
+    print(f"decode {dms:.2f} ms for {gold['n_gen'] - 1} steps, prefill {pms:.2f} ms")
     assert toks[0].tolist() == gold["tokens"]
-    tb, _, _ = dec.generate(prompt[None], gold["n_gen"], precision=hc.PREC_BF16_TC)
-    agree = int(np.sum(tb[0] == np.array(gold["tokens"])))
-    print(f"decode {dms:.2f} ms for {gold['n_gen'] - 1} steps, prefill {pms:.2f} ms; bf16 prefill agrees on "
-          f"{agree}/{gold['n_gen']} tokens")
     dec.free()
+
+
+def test_q05b_bf16_prefill_greedy_tokens(ctx, golden_dir):
+    """bf16 tensor-core prefill (decode steps fp32), free running: the greedy
+    ids must equal the oracle's at least up to the first ill-conditioned step
+    (where a one-ulp change of the oracle's own input moves its logits by more
+    than 1e-4 of max |logit|); beyond such a step bf16's 2^-9 rounding of the
+    prompt's projections may legitimately flip a greedy id.  The agreement is
+    printed."""
+    gold = json.load(open(os.path.join(golden_dir, "decoder_q05b_tokens.json")))
+    tf = np.load(os.path.join(golden_dir, "decoder_q05b_teacher.npz"))
+    model = S.gen_decoder(S.QWEN05B, seed=4)
+    prompt = S.gen_prompt(gold["n_prompt"], S.QWEN05B["vocab"], seed=4)
+    dec = hc.Decoder(ctx, model, max_ctx=gold["n_prompt"] + gold["n_gen"], max_seqs=1)
+    tb, _, _ = dec.generate(prompt[None], gold["n_gen"], precision=hc.PREC_BF16_TC)
+    dec.free()
+    same = tb[0] == np.array(gold["tokens"])
+    first_bad = int(np.argmin(same)) if not same.all() else len(same)
+    first_ill = int(np.argmax(tf["sens"] > 1e-4))
+    print(f"bf16 prefill agrees on {int(same.sum())}/{gold['n_gen']} tokens, first difference at step {first_bad}; "
+          f"first ill-conditioned step {first_ill}")
+    assert same[:first_ill + 1].all()
+
+
+# Teacher forcing: every decode step gets the oracle's previous greedy id, so
+# the device's and the oracle's logits can be compared step by step whatever
+# either would have chosen.  Error of a step: the largest difference over the
+# sampled logits relative to that step's max |logit|.  The fp32 bound grows
+# with the step's conditioning `sens` (the oracle's own response to a one-ulp
+# change of one norm vector): 1e-4 + 64 sens -- each device kernel differs
+# from the oracle by up to ~1e-5 relative (summation order), tens of ulps.
+# The bf16 prefill (prompt projections rounded to bf16, decode steps fp32)
+# keeps the 2e-2 contract at most steps; at nearly degenerate attention steps
+# its rounding moves the logits by far more, so that test asserts the median
+# and the share of steps within 2e-2 and reports the rest.
+
+
+@pytest.mark.parametrize("prec", [hc.PREC_FP32, hc.PREC_BF16_TC])
+def test_q05b_teacher_forced_logits(ctx, golden_dir, prec):
+    gold = json.load(open(os.path.join(golden_dir, "decoder_q05b_tokens.json")))
+    tf = np.load(os.path.join(golden_dir, "decoder_q05b_teacher.npz"))
+    n_gen = gold["n_gen"]
+    model = S.gen_decoder(S.QWEN05B, seed=4)
+    prompt = S.gen_prompt(gold["n_prompt"], S.QWEN05B["vocab"], seed=4)
+    dec = hc.Decoder(ctx, model, max_ctx=gold["n_prompt"] + n_gen, max_seqs=1)
+    forced = np.array(gold["tokens"], np.int32)[None]
+    toks, logits, _, _ = dec.generate_forced(prompt[None], forced, n_gen, precision=prec)
+    dec.free()
+    got = np.take_along_axis(logits[:, 0, :], tf["idx"], axis=1)
+    err = np.abs(got - tf["val"]).max(axis=1) / tf["absmax"]
+    lead = tf["margin"] / tf["absmax"]
+    sens = tf["sens"]
+    well = sens <= 1e-5
+    agree = toks[0] == tf["top1"]
+    worst = np.argsort(-err)[:4]
+    within = float(np.mean(err <= 2e-2))
+    print(f"precision {prec}: step error median {np.median(err):.2e}, max over well-conditioned steps "
+          f"{err[well].max():.2e} ({int(well.sum())} steps), steps within 2e-2 {within:.3f}, worst steps "
+          f"{[(int(i), float(err[i]), float(sens[i])) for i in worst]}; greedy ids equal on {int(agree.sum())}/{n_gen}; "
+          f"smallest oracle lead {lead.min():.2e} (step {int(lead.argmin())})")
+    if prec == hc.PREC_FP32:
+        bound = 1e-4 + 64 * sens
+        assert (err <= bound).all(), [(int(i), float(err[i]), float(bound[i])) for i in np.nonzero(err > bound)[0]]
+        # every step whose top-1 lead exceeds twice the step's error bound picks the oracle's id
+        sure = lead > 2 * bound
+        assert np.array_equal(toks[0][sure], tf["top1"][sure])
+    else:
+        assert np.median(err) <= 1e-3
+        assert within >= 0.9
+
+
+def test_small_decoder_teacher_forced_full_logits(ctx):
+    """Small decoder, 3 sequences: all logits of every step against the
+    oracle's, teacher-forced with the oracle's greedy ids."""
+    model = S.gen_decoder(SMALL, seed=23)
+    n_prompt, n_gen = 9, 12
+    prompts = np.stack([S.gen_prompt(n_prompt, SMALL["vocab"], seed=40 + s) for s in range(3)])
+    layers, on, emb = O.dequant_model(model)
+    ref_tok, ref_lg = zip(*(O.decoder_generate(model["cfg"], layers, on, emb, p, n_gen, threads=8, all_logits=True)
+                            for p in prompts))
+    dec = hc.Decoder(ctx, model, max_ctx=n_prompt + n_gen, max_seqs=4)
+    toks, logits, _, _ = dec.generate_forced(prompts, np.stack(ref_tok), n_gen)
+    dec.free()
+    for s in range(3):
+        err = np.abs(logits[:, s, :] - ref_lg[s]).max(axis=1) / np.abs(ref_lg[s]).max(axis=1)
+        assert err.max() <= 1e-4, (s, err)
+        assert np.array_equal(toks[s], ref_tok[s])
