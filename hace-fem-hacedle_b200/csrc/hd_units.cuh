@@ -133,4 +133,119 @@ __device__ __forceinline__ void chunk_vals(const URegs<TYPE> &g, const URowScale
     }
 }
 
+__device__ __forceinline__ float dot4(float a0, float a1, float a2, float a3, const float4 &x, float s) {
+    s = fmaf(a0, x.x, s);
+    s = fmaf(a1, x.y, s);
+    s = fmaf(a2, x.z, s);
+    return fmaf(a3, x.w, s);
+}
+
+// acc[b] += unit(u) . x[b][unit]; xs points at this unit's 32 floats of batch
+// row 0, batch row b at float4 offset xoff[b].
+// The float 2 + byte/64, exact for byte < 128: byte c of v goes to bits
+// 16..23 under the exponent byte 0x40 (one byte_perm, no subtraction).  The
+// constant 2 is removed per unit with the sum of x (see unit_fma).
+__device__ __forceinline__ float f2q(uint32_t v, int c) {
+    return __uint_as_float(__byte_perm(v, 0x40000000u, 0x7044u | ((uint32_t)c << 8)));
+}
+
+// acc[b] += unit(u) . x[b][unit].  xs points at this unit's 32 floats of batch
+// row 0 (float4), batch row b at float4 offset xoff[b] (padded rows read row
+// 0, so nothing past the B rows of x is touched); xh holds the sums of
+// x over the unit's two 16-value halves, batch rows `xh_stride` apart.
+//
+// Q5_0, Q4_K and Q6_K form S = sum_j f_j x_j with f_j = 2 + q_j/64, so
+// sum_j q_j x_j = 64 S - 128 X (X = sum_j x_j) and each type's offset folds
+// into the X term:  Q5_0  d (64 S - 144 X);  Q4_K  64 d1 S - (128 d1 + m1) X;
+// Q6_K  dl (64 S_lo - 160 X_lo) + dh (64 S_hi - 160 X_hi).  Q8_0 (signed
+// bytes) uses 2^23 + byte and one subtraction per value.
+template <int TYPE, int NB>
+__device__ __forceinline__ void unit_fma(const URegs<TYPE> &g, int u, const float4 *xs, const int (&xoff)[NB],
+                                         const float *xh, int xh_stride, float (&acc)[NB]) {
+    if constexpr (TYPE == HD_TYPE_Q8_0) {
+        float s[NB];
+#pragma unroll
+        for (int b = 0; b < NB; b++) s[b] = 0.f;
+#pragma unroll
+        for (int wd = 0; wd < 8; wd++) {
+            uint32_t v = (wd < 4 ? w4(g.a, wd) : w4(g.b, wd - 4)) ^ 0x80808080u;
+            const float o = 8388736.0f;  // 2^23 + 128
+            float f0 = mag(v, 0) - o, f1 = mag(v, 1) - o, f2 = mag(v, 2) - o, f3 = mag(v, 3) - o;
+#pragma unroll
+            for (int b = 0; b < NB; b++) s[b] = dot4(f0, f1, f2, f3, xs[xoff[b] + wd], s[b]);
+        }
+        float d = h2f((uint16_t)g.d);
+#pragma unroll
+        for (int b = 0; b < NB; b++) acc[b] = fmaf(d, s[b], acc[b]);
+    } else if constexpr (TYPE == HD_TYPE_Q6_K) {
+        float sl[NB], sh[NB];
+#pragma unroll
+        for (int b = 0; b < NB; b++) sl[b] = sh[b] = 0.f;
+#pragma unroll
+        for (int wd = 0; wd < 4; wd++) {
+            uint32_t v = w4(g.a, wd);
+            uint32_t lo = (v & 0x0F0F0F0Fu) | (shl_or_shr(g.h.x, 4 - 2 * wd) & 0x30303030u);
+            uint32_t hi = ((v >> 4) & 0x0F0F0F0Fu) | (shl_or_shr(g.h.y, 4 - 2 * wd) & 0x30303030u);
+            float l0 = f2q(lo, 0), l1 = f2q(lo, 1), l2 = f2q(lo, 2), l3 = f2q(lo, 3);
+            float h0 = f2q(hi, 0), h1 = f2q(hi, 1), h2 = f2q(hi, 2), h3 = f2q(hi, 3);
+#pragma unroll
+            for (int b = 0; b < NB; b++) {
+                sl[b] = dot4(l0, l1, l2, l3, xs[xoff[b] + wd], sl[b]);
+                sh[b] = dot4(h0, h1, h2, h3, xs[xoff[b] + 4 + wd], sh[b]);
+            }
+        }
+        int s0 = 2 * (u & 7);
+        uint32_t scw = w4(g.sc, s0 >> 2);
+        int8_t c0 = (int8_t)((scw >> (8 * (s0 & 3))) & 255), c1 = (int8_t)((scw >> (8 * ((s0 & 3) + 1))) & 255);
+        float d = h2f((uint16_t)g.d);
+        float dl = d * (float)c0, dh = d * (float)c1;
+#pragma unroll
+        for (int b = 0; b < NB; b++) {
+            const float xl = xh[b * xh_stride], xr = xh[b * xh_stride + 1];
+            acc[b] = fmaf(dl, fmaf(64.f, sl[b], -160.f * xl), acc[b]);
+            acc[b] = fmaf(dh, fmaf(64.f, sh[b], -160.f * xr), acc[b]);
+        }
+    } else {  // Q5_0, Q4_K: one scale per unit
+        float s[NB];
+#pragma unroll
+        for (int b = 0; b < NB; b++) s[b] = 0.f;
+#pragma unroll
+        for (int wd = 0; wd < 4; wd++) {
+            uint32_t v = w4(g.a, wd), lo, hi;
+            if constexpr (TYPE == HD_TYPE_Q5_0) {
+                lo = (v & 0x0F0F0F0Fu) | ((g.qh >> wd) & 0x10101010u);
+                hi = ((v >> 4) & 0x0F0F0F0Fu) | ((g.qh << (4 - wd)) & 0x10101010u);
+            } else {
+                lo = v & 0x0F0F0F0Fu;
+                hi = (v >> 4) & 0x0F0F0F0Fu;
+            }
+            float l0 = f2q(lo, 0), l1 = f2q(lo, 1), l2 = f2q(lo, 2), l3 = f2q(lo, 3);
+            float h0 = f2q(hi, 0), h1 = f2q(hi, 1), h2 = f2q(hi, 2), h3 = f2q(hi, 3);
+#pragma unroll
+            for (int b = 0; b < NB; b++) {
+                float t = dot4(l0, l1, l2, l3, xs[xoff[b] + wd], s[b]);
+                s[b] = dot4(h0, h1, h2, h3, xs[xoff[b] + 4 + wd], t);
+            }
+        }
+        if constexpr (TYPE == HD_TYPE_Q5_0) {
+            float d = h2f((uint16_t)g.d);
+#pragma unroll
+            for (int b = 0; b < NB; b++) {
+                const float X = xh[b * xh_stride] + xh[b * xh_stride + 1];
+                acc[b] = fmaf(d, fmaf(64.f, s[b], -144.f * X), acc[b]);
+            }
+        } else {
+            int sc, m;
+            q4k_sm_regs(u & 7, g.m.y, g.m.z, g.m.w, sc, m);
+            float d = h2f((uint16_t)(g.m.x & 0xFFFF)), dmin = h2f((uint16_t)(g.m.x >> 16));
+            float d1 = d * (float)sc, m1 = dmin * (float)m;
+#pragma unroll
+            for (int b = 0; b < NB; b++) {
+                const float X = xh[b * xh_stride] + xh[b * xh_stride + 1];
+                acc[b] = fmaf(64.f * d1, s[b], fmaf(-(128.f * d1 + m1), X, acc[b]));
+            }
+        }
+    }
+}
+
 }  // namespace
