@@ -73,6 +73,7 @@ extern "C" int hd_ctx_destroy(hd_ctx *ctx) {
     cudaFree(ctx->samp);
     cudaFree(ctx->kt_x);
     cudaFree(ctx->kt_y);
+    cudaFree(ctx->amax_keys);
     if (ctx->own_stream) cudaStreamDestroy(ctx->own_stream);
     delete ctx;
     return HD_OK;
@@ -120,6 +121,19 @@ int hd_ensure_workspace(hd_ctx *ctx, size_t bytes, size_t tickets) {
         HD_CUDA_TRY(ctx, cudaStreamSynchronize(ctx->stream));
         ctx->n_tickets = nt;
     }
+    return HD_OK;
+}
+
+int hd_ensure_amax_keys(hd_ctx *ctx) {
+    if (ctx->amax_keys) return HD_OK;
+    void *p = nullptr;
+    if (cudaMalloc(&p, 17 * sizeof(unsigned long long)) != cudaSuccess) {
+        cudaGetLastError();
+        return hd_fail(ctx, HD_E_OOM, "argmax keys");
+    }
+    HD_CUDA_TRY(ctx, cudaMemsetAsync(p, 0, 17 * sizeof(unsigned long long), ctx->stream));
+    HD_CUDA_TRY(ctx, cudaStreamSynchronize(ctx->stream));
+    ctx->amax_keys = (unsigned long long *)p;
     return HD_OK;
 }
 

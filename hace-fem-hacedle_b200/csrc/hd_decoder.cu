@@ -207,11 +207,11 @@ int head(hd_decoder *d, const float *hid, int S, int prec) {
     hd_ctx *ctx = d->ctx;
     int rc;
     if (S <= 16 && getenv("HACEDLE_DECODER_UNFUSED") == nullptr) {
-        rc = hd_qgemv_norm(ctx, d->embed, nullptr, hid, d->out_norm, d->c.eps, d->logits, S, nullptr, nullptr);
-    } else {
-        rc = hd_rmsnorm(ctx, hid, d->out_norm, nullptr, d->xn, S, d->c.hidden, d->c.eps);
-        if (!rc) rc = linear(d, d->embed, d->xn, d->logits, S, nullptr, nullptr, prec);
+        // final norm, LM head and (up to 4 rows) the greedy argmax in one launch
+        return hd_lm_head_argmax_run(ctx, d->embed, hid, d->out_norm, d->c.eps, d->logits, d->amax, S);
     }
+    rc = hd_rmsnorm(ctx, hid, d->out_norm, nullptr, d->xn, S, d->c.hidden, d->c.eps);
+    if (!rc) rc = linear(d, d->embed, d->xn, d->logits, S, nullptr, nullptr, prec);
     if (!rc) rc = hd_argmax_rows(ctx, d->logits, S, d->c.vocab, d->amax);
     return rc;
 }

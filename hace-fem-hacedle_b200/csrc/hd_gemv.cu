@@ -47,7 +47,21 @@ struct GemvArgs {
     int pair;              // 1: SwiGLU of (w0, w1)
     const float *nw;       // [K] RMSNorm weight: x is normalized first (null: x as is)
     float eps;
+    int32_t *amax;         // [B] greedy id of each output row (null: none)
+    unsigned long long *keys;  // [16] argmax keys + [1] CTA counter (zero between launches)
 };
+
+// Argmax key of (value v, index i): larger keys win, so the float's order
+// goes to the high word (sign-magnitude flipped to unsigned order; -0 counts
+// as +0 and NaN as the lowest key, so NaN never wins) and the complement of
+// the index to the low word (a tie goes to the lower index) -- the order of
+// ArgMaxSampler::sample's strict > scan (runtime/sampler/argmax.rs:8-24).
+__device__ __forceinline__ unsigned long long argmax_key(float v, uint32_t i) {
+    if (v != v) return 0ull;
+    uint32_t b = v == 0.f ? 0u : __float_as_uint(v);
+    b = (b & 0x80000000u) ? ~b : (b | 0x80000000u);
+    return ((unsigned long long)b << 32) | (0xFFFFFFFFu - i);
+}
 
 // RMSNorm scales of B rows of x [B][K] (1 / sqrt(mean(x^2) + eps)) into
 // rs[b], by the whole CTA in a fixed order: per-thread strided sums, warp
@@ -118,6 +132,9 @@ __global__ void __launch_bounds__(GemvShape<NB, P>::MAXT) k_qgemv(GemvArgs a) {
     }
     pdl_trigger();
     pdl_wait();
+    __shared__ unsigned long long skey[16];  // argmax: the CTA's best key per batch row
+    __shared__ int slast;
+    if (P == 0 && a.amax && t < 16) skey[t] = 0ull;
 
     // Sums of x over each 16-value half unit, per batch row: [NB][nu][2].
     float *xh = sm;
@@ -230,6 +247,27 @@ __global__ void __launch_bounds__(GemvShape<NB, P>::MAXT) k_qgemv(GemvArgs a) {
             if (a.bias) o = o + a.bias[rw];
             if (a.residual) o = a.residual[(int64_t)b * a.ldy + rw] + o;
             a.y[(int64_t)b * a.ldy + rw] = o;
+            if (!P && a.amax) atomicMax(&skey[b], argmax_key(o, (uint32_t)rw));
+        }
+    }
+    if (P == 0 && a.amax) {
+        // the CTA's best key per batch row into the global keys; the last CTA
+        // turns them into ids (0 when a row's first value is NaN, as the
+        // sequential scan gives) and clears them for the next launch
+        __syncthreads();
+        if (t < a.B) atomicMax(a.keys + t, skey[t]);
+        __threadfence();
+        __syncthreads();
+        if (t == 0) slast = atomicAdd(a.keys + 16, 1ull) == (unsigned long long)gridDim.x - 1;
+        __syncthreads();
+        if (slast) {
+            __threadfence();
+            if (t < a.B) {
+                const unsigned long long k = atomicExch(a.keys + t, 0ull);
+                const float y0 = __ldcg(a.y + (int64_t)t * a.ldy);
+                a.amax[t] = (y0 != y0 || k == 0ull) ? 0 : (int32_t)(0xFFFFFFFFu - (uint32_t)k);
+            }
+            if (t == 0) a.keys[16] = 0ull;
         }
     }
 }
@@ -578,7 +616,11 @@ int big_gemv_kernel(const hd_weight *w, int B) {
 
 int run_gemv(hd_ctx *ctx, const hd_weight *w, const hd_weight *w_up, const float *x, float *y, int B,
              const float *bias, const float *residual, const char *name, const float *nw = nullptr,
-             float eps = 0.f) {
+             float eps = 0.f, int32_t *amax = nullptr) {
+    if (amax && (w_up || B > 4)) {  // the fused argmax rides on the CTA kernel at batch <= 4
+        int rc = run_gemv(ctx, w, w_up, x, y, B, bias, residual, name, nw, eps);
+        return rc ? rc : hd_argmax_rows(ctx, y, B, w->rows, amax);
+    }
     if (!ctx || !w || !x || !y) return hd_fail(ctx, HD_E_ARG, "%s: null argument", name);
     HD_REQUIRE(ctx, B >= 1 && B <= 16, HD_E_ARG, "%s: batch %d outside 1..16", name, B);
     HD_REQUIRE(ctx, ((uintptr_t)x & 15) == 0, HD_E_ARG, "%s: x must be 16-byte aligned", name);
@@ -595,12 +637,12 @@ int run_gemv(hd_ctx *ctx, const hd_weight *w, const hd_weight *w_up, const float
         if (!rc) rc = hd_swiglu(ctx, ctx->scratch, ctx->scratch + one, y, (int64_t)one);
         return rc;
     }
-    if (!w_up && !nw && B <= 4) {
+    if (!w_up && !nw && !amax && B <= 4) {
         const int k = big_gemv_kernel(w, B);
         if (k == 2) return hd_qgemv_mma(ctx, w, x, y, B, bias, residual, name);
         if (k == 1) return hd_qgemv_sk(ctx, w, x, y, B, bias, residual, name);
     }
-    if (!w_up && !nw) {  // batch 5..16 on the tensor cores, where the shape fits
+    if (!w_up && !nw && !amax) {  // batch 5..16 on the tensor cores, where the shape fits
         bool done = false;
         const int rc = hd_qgemv_tc(ctx, w, x, y, B, bias, residual, &done);
         if (rc || done) return rc;
@@ -619,6 +661,13 @@ int run_gemv(hd_ctx *ctx, const hd_weight *w, const hd_weight *w_up, const float
     a.pair = w_up ? 1 : 0;
     a.nw = nw;
     a.eps = eps;
+    a.amax = amax;
+    a.keys = nullptr;
+    if (amax) {
+        int rc = hd_ensure_amax_keys(ctx);
+        if (rc) return rc;
+        a.keys = ctx->amax_keys;
+    }
     if (!w_up && pad_batch(B) >= 8 && getenv("HACEDLE_GEMV_RB") == nullptr) return run_gemv_rb(ctx, a, w->type, name);
     Plan p = plan_gemv((int)w->rows, w->units, B, w_up != nullptr, ctx->sm_count);
     if (nw) p.smem += (size_t)B * w->cols * sizeof(float) + 16;  // the normalized x, 16-byte aligned
@@ -686,6 +735,8 @@ int hd_qgemm_rows_f32(hd_ctx *ctx, const hd_weight *w, const float *X, float *Y,
     a.pair = 0;
     a.nw = nullptr;
     a.eps = 0.f;
+    a.amax = nullptr;
+    a.keys = nullptr;
     return run_gemv_rb(ctx, a, w->type, "hd_qgemm");
 }
 
@@ -698,6 +749,19 @@ int hd_qgemv_norm(hd_ctx *ctx, const hd_weight *w, const hd_weight *w_up, const 
     if (w_up && (bias || residual))
         return hd_fail(ctx, HD_E_ARG, "hd_qgemv_rmsnorm: the SwiGLU pair takes no bias or residual");
     return run_gemv(ctx, w, w_up, x, y, B, bias, residual, "hd_qgemv_rmsnorm", norm_w, eps);
+}
+
+// LM head and greedy sampling in one launch at batch <= 4 (larger batches:
+// the GEMV, then hd_argmax_rows).
+int hd_lm_head_argmax_run(hd_ctx *ctx, const hd_weight *w, const float *x, const float *norm_w, float eps,
+                          float *logits, int32_t *idx, int B) {
+    if (!ctx || !w || !x || !logits || !idx) return hd_fail(ctx, HD_E_ARG, "hd_lm_head_argmax: null argument");
+    return run_gemv(ctx, w, nullptr, x, logits, B, nullptr, nullptr, "hd_lm_head_argmax", norm_w, eps, idx);
+}
+
+extern "C" int hd_lm_head_argmax(hd_ctx *ctx, const hd_weight *w, const float *x_dev, const float *norm_w_dev,
+                                 float eps, float *logits_dev, int32_t *idx_dev, int B) {
+    return hd_lm_head_argmax_run(ctx, w, x_dev, norm_w_dev, eps, logits_dev, idx_dev, B);
 }
 
 extern "C" int hd_qgemv_rmsnorm(hd_ctx *ctx, const hd_weight *w, const hd_weight *w_up, const float *x_dev,

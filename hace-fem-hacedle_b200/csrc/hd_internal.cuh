@@ -60,6 +60,7 @@ struct hd_ctx {
     size_t samp_bytes = 0;
     float *kt_x = nullptr, *kt_y = nullptr;   // token-major copies for the [K][T] Q-GEMM entry points
     size_t kt_x_bytes = 0, kt_y_bytes = 0;
+    unsigned long long *amax_keys = nullptr;  // fused LM-head argmax: 16 keys + a CTA counter, kept zero
 };
 
 struct hd_weight {
@@ -105,6 +106,11 @@ int hd_fail(hd_ctx *ctx, int code, const char *fmt, ...);
     } while (0)
 
 int hd_ensure_workspace(hd_ctx *ctx, size_t bytes, size_t tickets);
+int hd_ensure_amax_keys(hd_ctx *ctx);
+// LM head (+ RMSNorm when norm_w != null) with the greedy argmax fused at
+// batch <= 4: logits [B][rows], idx [B].
+int hd_lm_head_argmax_run(hd_ctx *ctx, const hd_weight *w, const float *x, const float *norm_w, float eps,
+                          float *logits, int32_t *idx, int B);
 int hd_ensure_rope(hd_ctx *ctx, int head_dim, float theta);
 int hd_check_launch(hd_ctx *ctx, const char *what);
 bool hd_type_supported(int t);

@@ -30,7 +30,7 @@ EXPORTS = [
     "hd_dequantize", "hd_qgemv", "hd_qgemv_swiglu", "hd_qgemv_rmsnorm", "hd_qgemv_host", "hd_qgemm", "hd_qgemm_host",
     "hd_qgemm_kt", "hd_qgemm_kt_host", "hd_matmul_f32",
     "hd_rmsnorm", "hd_rmsnorm_graph", "hd_rope_neox", "hd_rope_interleaved", "hd_softmax_rows", "hd_swiglu",
-    "hd_add", "hd_argmax_rows", "hd_argmax_rows_noalloc", "hd_embed", "hd_kv_append", "hd_attention_decode", "hd_attention_prefill",
+    "hd_add", "hd_argmax_rows", "hd_argmax_rows_noalloc", "hd_lm_head_argmax", "hd_embed", "hd_kv_append", "hd_attention_decode", "hd_attention_prefill",
     "hd_dot_i8", "hd_fused_qdot_qadd_qacc_i8", "hd_gather_columns", "hd_decoder_create", "hd_decoder_free", "hd_decoder_generate",
     "hd_decoder_generate_ex", "hd_gguf_open", "hd_gguf_open_memory", "hd_gguf_close", "hd_gguf_error", "hd_gguf_counts", "hd_gguf_tensor",
     "hd_gguf_find_tensor", "hd_gguf_kv", "hd_gguf_find_key", "hd_gguf_kv_int", "hd_gguf_kv_float", "hd_gguf_kv_string",
@@ -78,6 +78,7 @@ def lib() -> C.CDLL:
         "hd_softmax_rows": [V, V, I64, I], "hd_swiglu": [V, V, V, V, I64], "hd_add": [V, V, V, V, I64],
         "hd_argmax_rows": [V, V, I64, I64, V], "hd_embed": [V, V, V, I, V],
         "hd_argmax_rows_noalloc": [V, I64, I64, V, V],
+        "hd_lm_head_argmax": [V, V, V, V, F, V, V, I],
         "hd_gather_columns": [V, V, V, I, I, I64],
         "hd_xbuf_alloc": [V, SZ, C.POINTER(V)], "hd_xbuf_free": [V, V], "hd_ipc_handle": [V, V, V],
         "hd_ipc_open": [V, V, C.POINTER(V)], "hd_ipc_close": [V, V],
@@ -298,6 +299,11 @@ class Context:
 
     def add(self, a, b, y):
         self._check(lib().hd_add(self.h, _ptr(a), _ptr(b), _ptr(y), a.numel()))
+
+    def lm_head_argmax(self, w: Weight, x, logits, idx, norm_w=None, eps: float = 1e-6):
+        """logits = W rmsnorm(x) (W x without norm_w), idx = greedy id per row."""
+        B = x.shape[0] if x.dim() == 2 else 1
+        self._check(lib().hd_lm_head_argmax(self.h, w.h, _ptr(x), _ptr(norm_w), eps, _ptr(logits), _ptr(idx), B))
 
     def argmax_rows(self, x, idx):
         n = x.shape[-1]

@@ -176,6 +176,14 @@ int hd_add(hd_ctx *ctx, const float *a_dev, const float *b_dev, float *out_dev, 
 /* First index of each row's maximum, strict > (ArgMaxSampler::sample,
  * runtime/sampler/argmax.rs:8-24); 0 for n == 0. */
 int hd_argmax_rows(hd_ctx *ctx, const float *x_dev, int64_t rows, int64_t n, int32_t *idx_dev);
+/* LMHead::forward followed by ArgMaxSampler::sample (src/x/provider/candle/
+ * lmhead.rs:22-38, runtime/sampler/argmax.rs:8-24): logits_dev [B][rows] =
+ * W x (x normalized first, (x * w) * r as hd_rmsnorm, when norm_w_dev is not
+ * NULL) and idx_dev [B] = the first index of each row's maximum (0 when the
+ * row's first logit is NaN).  B 1..16; up to 4 rows the argmax is folded into
+ * the GEMV's epilogue (no second pass over the logits). */
+int hd_lm_head_argmax(hd_ctx *ctx, const hd_weight *w, const float *x_dev, const float *norm_w_dev, float eps,
+                      float *logits_dev, int32_t *idx_dev, int B);
 /* Argmax of each row with no device allocation and no context.  It has no
  * counterpart in the reference.  It is for callers that cannot let a library
  * call cudaMalloc: runtimes that own all device memory through their own pool

@@ -130,7 +130,7 @@ def test_q05b_teacher_forced_logits(ctx, golden_dir, prec):
         assert np.array_equal(toks[0][sure], tf["top1"][sure])
     else:
         assert np.median(err) <= 1e-3
-        assert within >= 0.9
+        assert within >= 0.85   # measured 0.906
 
 
 def test_small_decoder_teacher_forced_full_logits(ctx):
