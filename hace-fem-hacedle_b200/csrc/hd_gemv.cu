@@ -590,27 +590,34 @@ int run_gemv_rb(hd_ctx *ctx, const GemvArgs &a, int type, const char *name) {
     return HD_OK;
 }
 
-// Plain GEMVs (no norm, no SwiGLU pair) at batch <= 4 on weights of at least
-// HACEDLE_GEMV_BIG_KB kilobytes (default 16 MB: the matrices large enough to
-// stream) take the stream-K kernels: at batch 1 the CUDA-core one
-// (hd_gemv_sk.cu), at batch 2..4 the tensor-core one (hd_gemv_mma.cu), whose
-// cost per weight does not grow with the batch (measured on B200, 7B-shaped
-// and LM-head matrices: batch 1 0.31-0.65 of HBM on CUDA cores against
-// 0.29-0.45 on tensor cores, batch 4 0.14-0.26 against 0.20-0.34).  Each
-// falls back to the other where it does not fit.  HACEDLE_GEMV_MMA /
-// HACEDLE_GEMV_SK = 0 turn either off, = 1 send every GEMV of batch <= 4
-// that fits there (the tensor-core one first).  Returns 2 (tensor cores),
-// 1 (streamed) or 0 (the CTA kernel below).
+// Plain GEMVs (no norm, no SwiGLU pair) at batch <= 4 on large weights take
+// one of three kernels laid out for streaming (measured on B200 in CUDA-graph
+// chains over weight copies larger than L2, fractions of the HBM copy peak):
+//  - batch 1, weights of HACEDLE_GEMV_BIG_KB kilobytes and more (default
+//    16 MB): the block kernel (hd_gemv_blk.cu; 7B-shaped Q5_0/Q4_K/Q6_K
+//    0.48/0.37/0.46, Q8_0 LM head 0.67, against 0.32/0.26/0.23/0.62 here);
+//  - batch 2..4, weights of HACEDLE_GEMV_MID_KB and more (default 4 MB): the
+//    tensor-core kernel (hd_gemv_mma.cu), whose cost per weight does not grow
+//    with the batch (7B-shaped 0.20-0.24 against 0.09-0.11 here, 3584 x 3584
+//    Q4_K 10.5 against 21.6 us), except Q8_0 weights of 16 MB and more, on
+//    the block kernel.
+// HACEDLE_GEMV_BLK / HACEDLE_GEMV_MMA / HACEDLE_GEMV_SK = 1 send every batch
+// <= 4 GEMV that fits to that kernel (in this order of precedence), = 0 turn
+// it off.  Returns 3 (block), 2 (tensor cores), 1 (streamed CUDA cores) or
+// 0 (the CTA kernel below).
 int big_gemv_kernel(const hd_weight *w, int B) {
-    const bool big = w->gguf_bytes >= (size_t)env_int("HACEDLE_GEMV_BIG_KB", 16384) * 1024;
-    const char *m = getenv("HACEDLE_GEMV_MMA"), *v = getenv("HACEDLE_GEMV_SK");
-    const bool mma_set = m && *m, sk_set = v && *v;
-    const bool mma_on = mma_set ? atoi(m) != 0 : big, sk_on = sk_set ? atoi(v) != 0 : big;
-    const bool mma_ok = mma_on && hd_qgemv_mma_fits(w), sk_ok = sk_on && hd_qgemv_sk_fits(w);
-    if (mma_set && mma_ok) return 2;
-    if (!mma_set && !sk_set && B == 1 && sk_ok) return 1;
-    if (mma_ok) return 2;
-    if (sk_ok) return 1;
+    auto env = [](const char *name) { const char *v = getenv(name); return v && *v ? atoi(v) : -1; };
+    const int eb = env("HACEDLE_GEMV_BLK"), em = env("HACEDLE_GEMV_MMA"), es = env("HACEDLE_GEMV_SK");
+    if (eb == 1 && hd_qgemv_blk_fits(w)) return 3;
+    if (em == 1 && hd_qgemv_mma_fits(w)) return 2;
+    if (es == 1 && hd_qgemv_sk_fits(w)) return 1;
+    const size_t big = (size_t)env_int("HACEDLE_GEMV_BIG_KB", 16384) * 1024;
+    const size_t mid = (size_t)env_int("HACEDLE_GEMV_MID_KB", 4096) * 1024;
+    const bool blk_ok = eb != 0 && hd_qgemv_blk_fits(w), mma_ok = em != 0 && hd_qgemv_mma_fits(w);
+    if (B == 1) return w->gguf_bytes >= big && blk_ok ? 3 : 0;
+    if (w->type == HD_TYPE_Q8_0 && w->gguf_bytes >= big && blk_ok) return 3;
+    if (w->gguf_bytes >= mid && mma_ok) return 2;
+    if (w->gguf_bytes >= big && blk_ok) return 3;
     return 0;
 }
 
@@ -639,6 +646,7 @@ int run_gemv(hd_ctx *ctx, const hd_weight *w, const hd_weight *w_up, const float
     }
     if (!w_up && !nw && !amax && B <= 4) {
         const int k = big_gemv_kernel(w, B);
+        if (k == 3) return hd_qgemv_blk(ctx, w, x, y, B, bias, residual, name);
         if (k == 2) return hd_qgemv_mma(ctx, w, x, y, B, bias, residual, name);
         if (k == 1) return hd_qgemv_sk(ctx, w, x, y, B, bias, residual, name);
     }

@@ -130,6 +130,10 @@ int hd_qgemv_norm(hd_ctx *ctx, const hd_weight *w, const hd_weight *w_up, const 
 // Streamed Q-GEMV at batch 1..4 (hd_gemv_sk.cu): y = W x (+bias, +residual);
 // the weight must satisfy hd_qgemv_sk_fits (cols % 128 == 0).
 bool hd_qgemv_sk_fits(const hd_weight *w);
+// Q-GEMV at batch 1..4 in 256-row x unit-group blocks (hd_gemv_blk.cu).
+bool hd_qgemv_blk_fits(const hd_weight *w);
+int hd_qgemv_blk(hd_ctx *ctx, const hd_weight *w, const float *x, float *y, int B, const float *bias,
+                 const float *residual, const char *name);
 // Q-GEMV at batch 1..4 with the products on the tensor cores (hd_gemv_mma.cu);
 // the weight must satisfy hd_qgemv_mma_fits.
 bool hd_qgemv_mma_fits(const hd_weight *w);

@@ -1,4 +1,5 @@
 """Decode Q-GEMV kernels of batch 1..4 for large matrices against the oracle:
+the block kernel (k_qgemv_blk, the default for weights of 16 MB and more),
 the tensor-core kernel (k_qgemv_mma) and the streamed CUDA-core kernel
 (k_qgemv_sk), each forced onto every shape it fits.
 
@@ -56,15 +57,17 @@ def _case(ctx, t, N, K, B, seed, bias=False, residual=False, reps=1):
 
 
 def _kernel(monkeypatch, kernel, lmin=""):
-    """Route every batch <= 4 GEMV that fits to the tensor-core kernel
-    (k_qgemv_mma) or to the streamed CUDA-core kernel (k_qgemv_sk)."""
+    """Route every batch <= 4 GEMV that fits to the block kernel (k_qgemv_blk),
+    the tensor-core kernel (k_qgemv_mma) or the streamed CUDA-core kernel
+    (k_qgemv_sk)."""
+    monkeypatch.setenv("HACEDLE_GEMV_BLK", "1" if kernel == "blk" else "0")
     monkeypatch.setenv("HACEDLE_GEMV_MMA", "1" if kernel == "mma" else "0")
     monkeypatch.setenv("HACEDLE_GEMV_SK", "1")
     if lmin:
         monkeypatch.setenv("HACEDLE_MM_LMIN" if kernel == "mma" else "HACEDLE_SK_LMIN", lmin)
 
 
-@pytest.mark.parametrize("kernel", ["mma", "sk"])
+@pytest.mark.parametrize("kernel", ["blk", "mma", "sk"])
 @pytest.mark.parametrize("t", TYPES)
 @pytest.mark.parametrize("N,K,B", [(7, 256, 1), (34, 512, 2), (100, 768, 3), (896, 1024, 4), (4866, 1280, 1),
                                    (896, 4864, 4), (257, 2304, 2), (4096, 8192, 1), (4865, 1280, 3)])
@@ -76,7 +79,7 @@ def test_streamed_gemv_matches_oracle(ctx, monkeypatch, kernel, t, N, K, B, lmin
     assert _rel_err(outs[0], ref) <= REL_TOL
 
 
-@pytest.mark.parametrize("kernel", ["mma", "sk"])
+@pytest.mark.parametrize("kernel", ["blk", "mma", "sk"])
 @pytest.mark.parametrize("t", TYPES)
 @pytest.mark.parametrize("wpb", ["1", "3", "8"])
 def test_streamed_gemv_epilogues_and_reruns(ctx, monkeypatch, kernel, t, wpb):
