@@ -122,7 +122,7 @@ int upload_vec(hd_decoder *d, float **dst, const float *src, size_t n) {
 int linear(hd_decoder *d, const hd_weight *w, const float *x, float *y, int rows, const float *bias, float *residual,
            int prec) {
     hd_ctx *ctx = d->ctx;
-    if (rows <= 16) return hd_qgemv(ctx, w, x, y, rows, bias, residual);
+    if (rows <= 16) return hd_qgemv_pinned(ctx, w, nullptr, x, nullptr, 0.f, y, rows, bias, residual);
     float *out = residual ? d->tmp : y;
     int rc = hd_qgemm(ctx, w, x, out, rows, prec);
     if (rc) return rc;
@@ -136,7 +136,7 @@ int linear(hd_decoder *d, const hd_weight *w, const float *x, float *y, int rows
 }
 
 int ffn_gate_up(hd_decoder *d, const hd_decoder::Layer &l, const float *x, float *a, int rows, int prec) {
-    if (rows <= 16) return hd_qgemv_swiglu(d->ctx, l.wg, l.wu, x, a, rows);
+    if (rows <= 16) return hd_qgemv_pinned(d->ctx, l.wg, l.wu, x, nullptr, 0.f, a, rows, nullptr, nullptr);
     int rc = hd_qgemm(d->ctx, l.wg, x, d->g, rows, prec);
     if (!rc) rc = hd_qgemm(d->ctx, l.wu, x, d->tmp, rows, prec);
     if (!rc) rc = hd_swiglu(d->ctx, d->g, d->tmp, a, (int64_t)rows * d->c.ffn);
@@ -160,7 +160,7 @@ int layer_forward(hd_decoder *d, int li, int rows, const int32_t *pos, const int
         // reading q from the fused rows
         const int64_t ld = l.wqkv->rows;
         if (!rc)
-            rc = gemv ? hd_qgemv_norm(ctx, l.wqkv, nullptr, d->h, l.attn_norm, c.eps, d->qkv, rows, l.bqkv, nullptr)
+            rc = gemv ? hd_qgemv_pinned(ctx, l.wqkv, nullptr, d->h, l.attn_norm, c.eps, d->qkv, rows, l.bqkv, nullptr)
                       : linear(d, l.wqkv, d->xn, d->qkv, rows, l.bqkv, nullptr, prec);
         // decode: RoPE and the cache append run inside the attention kernel
         if (!rc && !lens)
@@ -193,7 +193,7 @@ int layer_forward(hd_decoder *d, int li, int rows, const int32_t *pos, const int
     }
     if (!rc) rc = linear(d, l.wo, d->att, d->h, rows, nullptr, d->h, prec);
     if (gemv) {
-        if (!rc) rc = hd_qgemv_norm(ctx, l.wg, l.wu, d->h, l.ffn_norm, c.eps, d->a, rows, nullptr, nullptr);
+        if (!rc) rc = hd_qgemv_pinned(ctx, l.wg, l.wu, d->h, l.ffn_norm, c.eps, d->a, rows, nullptr, nullptr);
     } else {
         if (!rc) rc = hd_rmsnorm(ctx, d->h, l.ffn_norm, nullptr, d->xn, rows, c.hidden, c.eps);
         if (!rc) rc = ffn_gate_up(d, l, d->xn, d->a, rows, prec);

@@ -590,22 +590,45 @@ int run_gemv_rb(hd_ctx *ctx, const GemvArgs &a, int type, const char *name) {
     return HD_OK;
 }
 
+// Plain GEMVs at batch <= 4 on weights below HACEDLE_GEMV_SMALL_KB kilobytes
+// (default 16 MB) that no large-matrix kernel took go to the small-matrix
+// tensor-core kernel (hd_gemv_small.cu).  Measured on B200 in CUDA-graph
+// chains over weight copies larger than L2, microseconds per launch, against
+// the CTA kernel below: 0.5B-shaped Q5_0 4864 x 896 B=1 2.6 (3.3), B=4 3.2
+// (5.8); Q6_K / Q4_K 896 x 4864 B=4 4.4 / 4.1 (7.3 / 7.3); Q5_0 1152 x 896
+// B=1 2.2 (4.2); Q4_K 3584 x 3584 B=4 9.4 (21; 10.5 on the large-matrix
+// tensor-core kernel).  Q8_0 weights of under 2 MB at batch 2..4 stay on the
+// CTA kernel (896 x 896 B=4 3.5 against 4.3), and batch 5..16 on the tcgen05
+// kernel (its x conversion per CTA costs more there).  HACEDLE_GEMV_SMALL = 0
+// turns it off, = 1 sends every plain GEMV that fits to it (any batch).
+bool small_gemv(const hd_weight *w, int B, int sms, bool pair = false) {
+    const char *v = getenv("HACEDLE_GEMV_SMALL");
+    const int e = v && *v ? atoi(v) : -1;
+    if (e == 0) return false;
+    if (e != 1) {
+        const size_t lim = (size_t)env_int("HACEDLE_GEMV_SMALL_KB", 16384) * 1024;
+        if (B > 4 || w->gguf_bytes >= lim) return false;
+        if (w->type == HD_TYPE_Q8_0 && B >= 2 && w->gguf_bytes < ((size_t)2 << 20)) return false;
+    }
+    return hd_qgemv_small_fits(w, B, sms, pair);
+}
+
 // Plain GEMVs (no norm, no SwiGLU pair) at batch <= 4 on large weights take
 // one of three kernels laid out for streaming (measured on B200 in CUDA-graph
 // chains over weight copies larger than L2, fractions of the HBM copy peak):
 //  - batch 1, weights of HACEDLE_GEMV_BIG_KB kilobytes and more (default
 //    16 MB): the block kernel (hd_gemv_blk.cu; 7B-shaped Q5_0/Q4_K/Q6_K
 //    0.48/0.37/0.46, Q8_0 LM head 0.67, against 0.32/0.26/0.23/0.62 here);
-//  - batch 2..4, weights of HACEDLE_GEMV_MID_KB and more (default 4 MB): the
-//    tensor-core kernel (hd_gemv_mma.cu), whose cost per weight does not grow
-//    with the batch (7B-shaped 0.20-0.24 against 0.09-0.11 here, 3584 x 3584
-//    Q4_K 10.5 against 21.6 us), except Q8_0 weights of 16 MB and more, on
-//    the block kernel.
+//  - batch 2..4, weights of HACEDLE_GEMV_MID_KB and more (default 4 MB) that
+//    the small-matrix kernel does not take: the tensor-core kernel
+//    (hd_gemv_mma.cu), whose cost per weight does not grow with the batch
+//    (7B-shaped 0.20-0.24 against 0.09-0.11 here), except Q8_0 weights of
+//    16 MB and more, on the block kernel.
 // HACEDLE_GEMV_BLK / HACEDLE_GEMV_MMA / HACEDLE_GEMV_SK = 1 send every batch
 // <= 4 GEMV that fits to that kernel (in this order of precedence), = 0 turn
 // it off.  Returns 3 (block), 2 (tensor cores), 1 (streamed CUDA cores) or
 // 0 (the CTA kernel below).
-int big_gemv_kernel(const hd_weight *w, int B) {
+int big_gemv_kernel(const hd_weight *w, int B, int sms) {
     auto env = [](const char *name) { const char *v = getenv(name); return v && *v ? atoi(v) : -1; };
     const int eb = env("HACEDLE_GEMV_BLK"), em = env("HACEDLE_GEMV_MMA"), es = env("HACEDLE_GEMV_SK");
     if (eb == 1 && hd_qgemv_blk_fits(w)) return 3;
@@ -616,16 +639,20 @@ int big_gemv_kernel(const hd_weight *w, int B) {
     const bool blk_ok = eb != 0 && hd_qgemv_blk_fits(w), mma_ok = em != 0 && hd_qgemv_mma_fits(w);
     if (B == 1) return w->gguf_bytes >= big && blk_ok ? 3 : 0;
     if (w->type == HD_TYPE_Q8_0 && w->gguf_bytes >= big && blk_ok) return 3;
-    if (w->gguf_bytes >= mid && mma_ok) return 2;
+    if (w->gguf_bytes >= mid && mma_ok && !small_gemv(w, B, sms)) return 2;
     if (w->gguf_bytes >= big && blk_ok) return 3;
     return 0;
 }
 
+// pinned: the decoder's GEMVs -- the CTA kernel at batch <= 4 and the
+// tcgen05 kernel at 5..16, the kernels its greedy tokens are pinned to (the
+// small-matrix and large-matrix kernels sum in other orders; at a step whose
+// top-2 logits are nearly tied that can change a greedy id).
 int run_gemv(hd_ctx *ctx, const hd_weight *w, const hd_weight *w_up, const float *x, float *y, int B,
              const float *bias, const float *residual, const char *name, const float *nw = nullptr,
-             float eps = 0.f, int32_t *amax = nullptr) {
+             float eps = 0.f, int32_t *amax = nullptr, bool pinned = false) {
     if (amax && (w_up || B > 4)) {  // the fused argmax rides on the CTA kernel at batch <= 4
-        int rc = run_gemv(ctx, w, w_up, x, y, B, bias, residual, name, nw, eps);
+        int rc = run_gemv(ctx, w, w_up, x, y, B, bias, residual, name, nw, eps, nullptr, pinned);
         return rc ? rc : hd_argmax_rows(ctx, y, B, w->rows, amax);
     }
     if (!ctx || !w || !x || !y) return hd_fail(ctx, HD_E_ARG, "%s: null argument", name);
@@ -639,17 +666,24 @@ int run_gemv(hd_ctx *ctx, const hd_weight *w, const hd_weight *w_up, const float
         // pair would hold 2 x 16 accumulators per thread at this batch).
         size_t one = (size_t)B * w->rows;
         int rc = hd_ensure_hbuf(ctx, &ctx->scratch, &ctx->scratch_bytes, 2 * one * sizeof(float));
-        if (!rc) rc = run_gemv(ctx, w, nullptr, x, ctx->scratch, B, nullptr, nullptr, name, nw, eps);
-        if (!rc) rc = run_gemv(ctx, w_up, nullptr, x, ctx->scratch + one, B, nullptr, nullptr, name, nw, eps);
+        if (!rc) rc = run_gemv(ctx, w, nullptr, x, ctx->scratch, B, nullptr, nullptr, name, nw, eps, nullptr, pinned);
+        if (!rc)
+            rc = run_gemv(ctx, w_up, nullptr, x, ctx->scratch + one, B, nullptr, nullptr, name, nw, eps, nullptr, pinned);
         if (!rc) rc = hd_swiglu(ctx, ctx->scratch, ctx->scratch + one, y, (int64_t)one);
         return rc;
     }
-    if (!w_up && !nw && !amax && B <= 4) {
-        const int k = big_gemv_kernel(w, B);
+    if (!w_up && !nw && !amax && !pinned) {
+        const int k = B <= 4 ? big_gemv_kernel(w, B, ctx->sm_count) : 0;
         if (k == 3) return hd_qgemv_blk(ctx, w, x, y, B, bias, residual, name);
         if (k == 2) return hd_qgemv_mma(ctx, w, x, y, B, bias, residual, name);
         if (k == 1) return hd_qgemv_sk(ctx, w, x, y, B, bias, residual, name);
+        if (small_gemv(w, B, ctx->sm_count))
+            return hd_qgemv_small(ctx, w, nullptr, x, y, B, bias, residual, nullptr, 0.f, name);
     }
+    // the fused RMSNorm and the SwiGLU pair (the decoder's projections) on the
+    // small-matrix kernel too, where it takes them
+    if ((w_up || nw) && !amax && !pinned && small_gemv(w, B, ctx->sm_count, w_up != nullptr))
+        return hd_qgemv_small(ctx, w, w_up, x, y, B, bias, residual, nw, eps, name);
     if (!w_up && !nw && !amax) {  // batch 5..16 on the tensor cores, where the shape fits
         bool done = false;
         const int rc = hd_qgemv_tc(ctx, w, x, y, B, bias, residual, &done);
@@ -757,6 +791,12 @@ int hd_qgemv_norm(hd_ctx *ctx, const hd_weight *w, const hd_weight *w_up, const 
     if (w_up && (bias || residual))
         return hd_fail(ctx, HD_E_ARG, "hd_qgemv_rmsnorm: the SwiGLU pair takes no bias or residual");
     return run_gemv(ctx, w, w_up, x, y, B, bias, residual, "hd_qgemv_rmsnorm", norm_w, eps);
+}
+
+// The decoder's GEMVs (see run_gemv: pinned).
+int hd_qgemv_pinned(hd_ctx *ctx, const hd_weight *w, const hd_weight *w_up, const float *x, const float *norm_w,
+                    float eps, float *y, int B, const float *bias, const float *residual) {
+    return run_gemv(ctx, w, w_up, x, y, B, bias, residual, "decoder GEMV", norm_w, eps, nullptr, true);
 }
 
 // LM head and greedy sampling in one launch at batch <= 4 (larger batches:

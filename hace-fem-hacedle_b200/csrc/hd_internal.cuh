@@ -125,11 +125,20 @@ int hd_attention_run(hd_ctx *ctx, const float *q, int64_t qld, const float *kc, 
                      const int32_t *rope_pos = nullptr, bool early_kv = false);
 // Q-GEMV (B <= 16) of rmsnorm(x) with the norm in each CTA's prologue;
 // w_up != null: SwiGLU pair.
+// The decoder's GEMVs: y = W x, W rmsnorm(x) (norm_w) or the SwiGLU pair
+// (w_up), on the kernels its greedy tokens are pinned to (hd_gemv.cu).
+int hd_qgemv_pinned(hd_ctx *ctx, const hd_weight *w, const hd_weight *w_up, const float *x, const float *norm_w,
+                    float eps, float *y, int B, const float *bias, const float *residual);
 int hd_qgemv_norm(hd_ctx *ctx, const hd_weight *w, const hd_weight *w_up, const float *x, const float *norm_w,
                   float eps, float *y, int B, const float *bias, const float *residual);
 // Streamed Q-GEMV at batch 1..4 (hd_gemv_sk.cu): y = W x (+bias, +residual);
 // the weight must satisfy hd_qgemv_sk_fits (cols % 128 == 0).
 bool hd_qgemv_sk_fits(const hd_weight *w);
+// Q-GEMV of a few-MB weight at batch 1..16 on the tensor cores, K parts of a
+// 32-row tile in a thread-block cluster (hd_gemv_small.cu).
+bool hd_qgemv_small_fits(const hd_weight *w, int B, int sms, bool pair = false);
+int hd_qgemv_small(hd_ctx *ctx, const hd_weight *w, const hd_weight *w_up, const float *x, float *y, int B,
+                   const float *bias, const float *residual, const float *norm_w, float eps, const char *name);
 // Q-GEMV at batch 1..4 in 256-row x unit-group blocks (hd_gemv_blk.cu).
 bool hd_qgemv_blk_fits(const hd_weight *w);
 int hd_qgemv_blk(hd_ctx *ctx, const hd_weight *w, const float *x, float *y, int B, const float *bias,
@@ -196,6 +205,30 @@ static inline cudaError_t hd_launch_cluster(hd_ctx *ctx, void (*kern)(KArgs...),
 // ------------------------------------------------------- device utilities
 __device__ __forceinline__ void pdl_wait() { asm volatile("griddepcontrol.wait;" ::: "memory"); }
 __device__ __forceinline__ void pdl_trigger() { asm volatile("griddepcontrol.launch_dependents;" :::); }
+
+// Read-only loads that stay where they are written.  __ldg loads are marked
+// invariant, so the compiler may move them past griddepcontrol.wait to their
+// first use; weight loads meant to overlap the previous kernel use these.
+__device__ __forceinline__ uint32_t ld_pin_u16(const void *p) {
+    unsigned short v;
+    asm volatile("ld.global.nc.u16 %0, [%1];" : "=h"(v) : "l"(p));
+    return v;
+}
+__device__ __forceinline__ uint32_t ld_pin_u32(const void *p) {
+    uint32_t v;
+    asm volatile("ld.global.nc.u32 %0, [%1];" : "=r"(v) : "l"(p));
+    return v;
+}
+__device__ __forceinline__ uint2 ld_pin_v2(const void *p) {
+    uint2 v;
+    asm volatile("ld.global.nc.v2.u32 {%0, %1}, [%2];" : "=r"(v.x), "=r"(v.y) : "l"(p));
+    return v;
+}
+__device__ __forceinline__ uint4 ld_pin_v4(const void *p) {
+    uint4 v;
+    asm volatile("ld.global.nc.v4.u32 {%0, %1, %2, %3}, [%4];" : "=r"(v.x), "=r"(v.y), "=r"(v.z), "=r"(v.w) : "l"(p));
+    return v;
+}
 
 __device__ __forceinline__ float h2f(uint16_t h) {
     return __half2float(__ushort_as_half(h));   // exact, subnormals kept

@@ -17,27 +17,29 @@ struct URegs<HD_TYPE_Q4_K> { uint4 a, m; };
 template <>
 struct URegs<HD_TYPE_Q6_K> { uint4 a, sc; uint2 h; uint32_t d; };
 
+// The loads are pinned (ld_pin_*): issued before griddepcontrol.wait, they
+// overlap the previous kernel instead of being moved to their first use.
 template <int TYPE>
 __device__ __forceinline__ void load_unit(const WView &w, int64_t r, int u, URegs<TYPE> &g) {
     const int64_t ur = (int64_t)u * w.rows + r;
     if constexpr (TYPE == HD_TYPE_Q8_0) {
         const uint4 *p = (const uint4 *)(w.q + ur * 32);
-        g.a = __ldg(p);
-        g.b = __ldg(p + 1);
-        g.d = __ldg((const unsigned short *)w.meta + ur);
+        g.a = ld_pin_v4(p);
+        g.b = ld_pin_v4(p + 1);
+        g.d = ld_pin_u16((const unsigned short *)w.meta + ur);
     } else if constexpr (TYPE == HD_TYPE_Q5_0) {
-        g.a = __ldg((const uint4 *)(w.q + ur * 16));
-        g.qh = __ldg((const unsigned int *)w.aux + ur);
-        g.d = __ldg((const unsigned short *)w.meta + ur);
+        g.a = ld_pin_v4(w.q + ur * 16);
+        g.qh = ld_pin_u32((const unsigned int *)w.aux + ur);
+        g.d = ld_pin_u16((const unsigned short *)w.meta + ur);
     } else if constexpr (TYPE == HD_TYPE_Q4_K) {
-        g.a = __ldg((const uint4 *)(w.q + ur * 16));
-        g.m = __ldg((const uint4 *)(w.meta + ((int64_t)(u >> 3) * w.rows + r) * 16));
+        g.a = ld_pin_v4(w.q + ur * 16);
+        g.m = ld_pin_v4(w.meta + ((int64_t)(u >> 3) * w.rows + r) * 16);
     } else {
         const int64_t sr = (int64_t)(u >> 3) * w.rows + r;
-        g.a = __ldg((const uint4 *)(w.q + ur * 16));
-        g.h = __ldg((const uint2 *)w.aux + ur);
-        g.sc = __ldg((const uint4 *)(w.meta + sr * 16));
-        g.d = __ldg(w.dsb + sr);
+        g.a = ld_pin_v4(w.q + ur * 16);
+        g.h = ld_pin_v2((const uint2 *)w.aux + ur);
+        g.sc = ld_pin_v4(w.meta + sr * 16);
+        g.d = ld_pin_u16(w.dsb + sr);
     }
 }
 
