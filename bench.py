@@ -230,25 +230,26 @@ def run_ours(args, rank, world, local):
                 "gbs": round(case_bytes(t, N, K, B) / (per * 1e-3) / 1e9, 1), "us_per_launch": round(per * 1e3, 3)}
     launches = launches_per_step * args.steps
     achieved = step_bytes * args.steps / (kernel_ms * 1e-3) / 1e9
-    # Batch 1 and 4 run the CUDA-core k_qgemv, batch 16 the tensor-core
-    # k_qgemv_tc (hd_qgemv picks by batch): their shares of the step's time.
+    # Batch 1 and 4 run the small-matrix tensor-core k_qgemv_sm (mma.sync),
+    # batch 16 the tcgen05 k_qgemv_tc (hd_qgemv picks by batch and size):
+    # their shares of the step's time.
     tc_ms = sum(case_ms[(t, B)] for (t, N, K) in CASES for B in BATCHES if B >= 5)
     roofline = {"bound": "hbm", "achieved": round(achieved, 1), "peak": hbm, "unit": "GB/s",
                 "frac": round(achieved / hbm, 4), "traffic": None, "peak_kind": peak_kind,
-                "kernel": "k_qgemv", "algorithmic_bytes_per_step": step_bytes,
-                "kernel_time_share": {"k_qgemv (B=1,4)": round(1 - tc_ms / kernel_ms, 3),
+                "kernel": "k_qgemv_sm", "algorithmic_bytes_per_step": step_bytes,
+                "kernel_time_share": {"k_qgemv_sm (B=1,4)": round(1 - tc_ms / kernel_ms, 3),
                                       "k_qgemv_tc (B=16)": round(tc_ms / kernel_ms, 3)}}
     # DRAM bytes of one captured launch (ncu --set full, Q5_0 batch 1), with its
-    # algorithmic bytes: profiles/qgemv_q5_0_b1_ncu.md.
+    # algorithmic bytes: profiles/qgemv_sm_q5_0_b1_ncu.md.
     # (not measured in this run: copied from that committed capture)
-    trf = os.path.join(ROOT, "profiles", "qgemv_q5_0_b1_ncu.md")
+    trf = os.path.join(ROOT, "profiles", "qgemv_sm_q5_0_b1_ncu.md")
     if os.path.exists(trf):
         kv = dict(ln.split(":", 1) for ln in open(trf) if ln.startswith(("dram_bytes_per_launch", "algorithmic_bytes")))
         if kv:
             roofline["traffic"] = int(kv["dram_bytes_per_launch"])
-            roofline["traffic_kernel"] = "k_qgemv<Q5_0,B=1> on 4864x896"
+            roofline["traffic_kernel"] = "k_qgemv_sm<Q5_0,B=1> on 4864x896"
             roofline["traffic_algorithmic_bytes"] = int(kv["algorithmic_bytes_per_launch"])
-            roofline["traffic_source"] = "copied from profiles/qgemv_q5_0_b1_ncu.md (one ncu capture), not this run"
+            roofline["traffic_source"] = "copied from profiles/qgemv_sm_q5_0_b1_ncu.md (one ncu capture), not this run"
 
     # End to end through the host-buffer C-ABI call.
     e2e = None
