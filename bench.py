@@ -287,6 +287,19 @@ def run_ours(args, rank, world, local):
         "wall_ms_timed_region": round(total_ms, 3),
         "workloads": extra,
     }
+    # The multi-GPU figures at the top level: the row-sharded 7B-shaped layer
+    # (exchange over NVLink included, strong scaling) and the 256-sequence
+    # decode (replicas, sequences sharded over the ranks).
+    l7 = extra.get("layer7b_sharded", {})
+    dq = extra.get("decode_q05b", {}).get("seqs256", {})
+    if "B1" in l7:
+        res["layer7b_B1_gbs"] = l7["B1"].get("gbs")
+        res["layer7b_B1_exchange_ms"] = l7["B1"].get("exchange_ms")
+    if "B512" in l7:
+        res["layer7b_B512_tflops"] = l7["B512"].get("tflops")
+        res["layer7b_B512_exchange_ms"] = l7["B512"].get("exchange_ms")
+    if dq:
+        res["decode_256seq_tokens_per_s"] = dq.get("tokens_per_s_all_gpus")
     if rank == 0:
         print(json.dumps(res), flush=True)
     ctx.close()
@@ -430,10 +443,11 @@ def layer7b_workload(ctx, args, rank, world, reps=5):
     """The seven projections of a Qwen2.5-7B-shaped layer (q/k/v/o and
     gate/up Q4_K, down Q6_K), output rows sharded over the ranks.  Each rank
     computes its rows (GEMV at B=1, tcgen05 GEMM at B=64 and 512), then the
-    outputs are exchanged over NVLink: by default each rank's own kernel writes
-    its slice into every rank's full output (hd_push_columns, IPC-mapped
-    buffers); HACEDLE_EXCHANGE=nccl uses an NCCL all-gather plus
-    hd_gather_columns instead.
+    outputs are exchanged over NVLink: by default one launch of our own kernel
+    writes all seven slices into every rank's full outputs and completes with
+    one handshake (hd_push_columns_multi, IPC-mapped buffers);
+    HACEDLE_EXCHANGE=push1 pushes output by output (seven handshakes),
+    HACEDLE_EXCHANGE=nccl uses an NCCL all-gather plus hd_gather_columns.
     Total work is fixed (strong scaling); times are device times (the work is
     queued behind a device-side spin), max over ranks, after a 256 MB L2 flush
     before every rep."""
@@ -455,6 +469,7 @@ def layer7b_workload(ctx, args, rank, world, reps=5):
     flops_per_tok = sum(2 * N * K for _, t, N, K in mats)
     flush = torch.empty(256 << 20, dtype=torch.uint8, device="cuda")
     use_nccl = os.environ.get("HACEDLE_EXCHANGE", "") == "nccl"
+    one_by_one = os.environ.get("HACEDLE_EXCHANGE", "") == "push1"
     peer = None
     if world > 1 and not use_nccl:
         import torch.distributed as dist
@@ -467,7 +482,10 @@ def layer7b_workload(ctx, args, rank, world, reps=5):
     res = {"scaling": "strong", "ranks": world, "weight_bytes_layer": w_total, "peak_kind": kind,
            "exchange": ("none" if world == 1 else
                         "NCCL all_gather_into_tensor (torch.distributed) + hd_gather_columns" if use_nccl else
-                        "hd_push_columns: P2P stores over NVLink into IPC-mapped outputs, epoch flags")}
+                        "hd_push_columns per output: P2P stores over NVLink into IPC-mapped outputs, "
+                        "one epoch handshake each" if one_by_one else
+                        "hd_push_columns_multi: P2P stores over NVLink into IPC-mapped outputs, all seven "
+                        "outputs in one launch with one epoch handshake")}
     for B in (1, 64, 512):
         xs = {K: torch.from_numpy(S.gen_activations(B, K, 60)).cuda() for K in (H, F)}
         ys = [torch.empty(B, N // world, device="cuda") for _, _, N, _, _ in ws]
@@ -485,6 +503,9 @@ def layer7b_workload(ctx, args, rank, world, reps=5):
 
         def exchange():
             import torch.distributed as dist
+            if peer and not one_by_one:
+                peer.push_all([(i, y, N // world) for i, ((nm, t, N, K, w), y) in enumerate(zip(ws, ys))], B)
+                return
             for i, ((nm, t, N, K, w), y, g, f) in enumerate(zip(ws, ys, gath, full)):
                 if peer:
                     peer.push(i, y, B, N // world)

@@ -9,6 +9,10 @@
 // peer's flag array and waits until every peer's flag for this epoch is up in
 // its own.  A call ends once all G slices are in this rank's F.
 //
+// hd_push_columns_multi does the same for up to HD_PUSH_MAX outputs (the
+// projections of a layer) in one launch with one completion handshake, so the
+// round trip of the flags is paid once per layer instead of once per output.
+//
 // Ordering: after a CTA barrier, one thread of each CTA fences at system scope
 // and takes a ticket; the last CTA fences again and publishes the epoch with a
 // release store, and the
@@ -32,6 +36,39 @@ __device__ __forceinline__ int32_t ld_acquire_sys(const int32_t *p) {
     int32_t v;
     asm volatile("ld.acquire.sys.global.s32 %0, [%1];" : "=r"(v) : "l"(p) : "memory");
     return v;
+}
+
+// The end of a push: the CTA's stores, then one system-scope fence before its
+// ticket; the last CTA publishes the epoch to every peer and waits (bounded)
+// until every peer's epoch has reached this one.
+__device__ __forceinline__ void push_complete(int32_t *const *__restrict__ flags, int world, int rank, int32_t epoch,
+                                              int *tickets, int *err) {
+    // The CTA's stores, then one system-scope fence before its ticket.
+    __syncthreads();
+    __shared__ int last;
+    if (threadIdx.x == 0) {
+        __threadfence_system();
+        last = (atomicAdd(tickets, 1) == (int)gridDim.x - 1);
+    }
+    __syncthreads();
+    if (!last || threadIdx.x != 0) return;
+    *tickets = 0;   // kept zero for the next user
+    __threadfence_system();
+    for (int r = 0; r < world; r++)
+        if (r != rank) st_release_sys(flags[r] + rank, epoch);
+    const int32_t *mine = flags[rank];
+    const long long t0 = clock64();
+    for (int r = 0; r < world; r++) {
+        if (r == rank) continue;
+        // Epochs only grow: a peer already in a later exchange counts as done.
+        while (ld_acquire_sys(mine + r) - epoch < 0) {
+            if (clock64() - t0 > P2P_SPIN_LIMIT) {
+                atomicExch(err, HD_E_TIMEOUT);
+                return;
+            }
+            __nanosleep(64);
+        }
+    }
 }
 
 // Grid-stride over the [B][n / VEC] vectors of y (VEC = 4: float4 copies,
@@ -66,32 +103,52 @@ __global__ void __launch_bounds__(256) k_push_columns(const float *__restrict__ 
             if (dst[u] >= 0)
                 for (int r = 0; r < world; r++) *(V *)(full[r] + dst[u]) = v[u];
     }
-    // The CTA's stores, then one system-scope fence before its ticket.
-    __syncthreads();
-    __shared__ int last;
-    if (threadIdx.x == 0) {
-        __threadfence_system();
-        last = (atomicAdd(tickets, 1) == (int)gridDim.x - 1);
-    }
-    __syncthreads();
-    if (!last || threadIdx.x != 0) return;
-    *tickets = 0;   // kept zero for the next user
-    __threadfence_system();
-    for (int r = 0; r < world; r++)
-        if (r != rank) st_release_sys(flags[r] + rank, epoch);
-    const int32_t *mine = flags[rank];
-    const long long t0 = clock64();
-    for (int r = 0; r < world; r++) {
-        if (r == rank) continue;
-        // Epochs only grow: a peer already in a later exchange counts as done.
-        while (ld_acquire_sys(mine + r) - epoch < 0) {
-            if (clock64() - t0 > P2P_SPIN_LIMIT) {
-                atomicExch(err, HD_E_TIMEOUT);
-                return;
+    push_complete(flags, world, rank, epoch, tickets, err);
+}
+
+// Up to HD_PUSH_MAX outputs in one launch: output i is y[i] [B][n[i]] into
+// full[i][r] [B][world * n[i]]; the same grid-stride walk per output, then
+// one handshake.
+struct PushItems {
+    const float *y[HD_PUSH_MAX];
+    float *const *full[HD_PUSH_MAX];
+    int64_t n[HD_PUSH_MAX];
+    int count;
+};
+
+template <int VEC>
+__global__ void __launch_bounds__(256) k_push_columns_multi(PushItems it, int32_t *const *__restrict__ flags,
+                                                            int world, int rank, int B, int32_t epoch, int *tickets,
+                                                            int *err) {
+    using V = typename std::conditional<VEC == 4, float4, float>::type;
+    pdl_wait();
+    pdl_trigger();
+    const uint32_t stride = gridDim.x * blockDim.x;
+    for (int i = 0; i < it.count; i++) {
+        const int64_t n = it.n[i], ldf = (int64_t)world * n;
+        const float *__restrict__ y = it.y[i];
+        float *const *__restrict__ full = it.full[i];
+        const uint32_t nv = (uint32_t)(n / VEC), total = (uint32_t)B * nv;
+        for (uint32_t e0 = blockIdx.x * blockDim.x + threadIdx.x; e0 < total; e0 += 4 * stride) {
+            V v[4];
+            int64_t dst[4];
+#pragma unroll
+            for (int u = 0; u < 4; u++) {
+                const uint32_t e = e0 + u * stride;
+                dst[u] = -1;
+                if (e < total && e >= e0) {
+                    const uint32_t b = e / nv, j = (e - b * nv) * VEC;
+                    v[u] = __ldg((const V *)(y + (int64_t)b * n + j));
+                    dst[u] = (int64_t)b * ldf + (int64_t)rank * n + j;
+                }
             }
-            __nanosleep(64);
+#pragma unroll
+            for (int u = 0; u < 4; u++)
+                if (dst[u] >= 0)
+                    for (int r = 0; r < world; r++) *(V *)(full[r] + dst[u]) = v[u];
         }
     }
+    push_complete(flags, world, rank, epoch, tickets, err);
 }
 
 }  // namespace
@@ -160,5 +217,43 @@ extern "C" int hd_push_columns(hd_ctx *ctx, const float *y_dev, float *const *fu
     else
         HD_CUDA_TRY(ctx, hd_launch(ctx, k_push_columns<1>, grid, dim3(256), 0, y_dev, full_ptrs_dev, flag_ptrs_dev,
                                    world, rank, B, n, epoch, ctx->tickets, ctx->flag));
+    return HD_OK;
+}
+
+extern "C" int hd_push_columns_multi(hd_ctx *ctx, int count, const float *const *y_devs, float *const *const *full_ptrs_devs,
+                                     const int64_t *ns, int32_t *const *flag_ptrs_dev, int world, int rank, int B,
+                                     int32_t epoch) {
+    if (!ctx || !y_devs || !full_ptrs_devs || !ns || !flag_ptrs_dev)
+        return hd_fail(ctx, HD_E_ARG, "hd_push_columns_multi: null argument");
+    HD_REQUIRE(ctx, count >= 1 && count <= HD_PUSH_MAX, HD_E_ARG, "hd_push_columns_multi: %d outputs (1..%d)", count,
+               HD_PUSH_MAX);
+    HD_REQUIRE(ctx, world >= 1 && rank >= 0 && rank < world && B >= 1 && B <= 65535, HD_E_SHAPE,
+               "hd_push_columns_multi: bad shape (world %d, rank %d, B %d)", world, rank, B);
+    HD_REQUIRE(ctx, epoch > 0, HD_E_ARG, "hd_push_columns_multi: epoch must be positive");
+    PushItems it{};
+    it.count = count;
+    bool v4 = true;
+    int64_t most = 0;
+    for (int i = 0; i < count; i++) {
+        if (!y_devs[i] || !full_ptrs_devs[i]) return hd_fail(ctx, HD_E_ARG, "hd_push_columns_multi: null output %d", i);
+        HD_REQUIRE(ctx, ns[i] >= 1 && (int64_t)B * ns[i] < ((int64_t)1 << 31) - 4 * 4 * 256 * 4 * 148, HD_E_SHAPE,
+                   "hd_push_columns_multi: output %d slice of %lld values", i, (long long)B * ns[i]);
+        it.y[i] = y_devs[i];
+        it.full[i] = full_ptrs_devs[i];
+        it.n[i] = ns[i];
+        v4 = v4 && ns[i] % 4 == 0 && ((uintptr_t)y_devs[i] & 15) == 0;
+        most = most > B * ns[i] ? most : B * ns[i];
+    }
+    int rc = hd_ensure_workspace(ctx, 0, 1);
+    if (rc) return rc;
+    int64_t ctas = ((v4 ? most / 4 : most) + 255) / 256;
+    if (ctas > 4 * (int64_t)ctx->sm_count) ctas = 4 * (int64_t)ctx->sm_count;
+    if (ctas < 1) ctas = 1;
+    if (v4)
+        HD_CUDA_TRY(ctx, hd_launch(ctx, k_push_columns_multi<4>, dim3((unsigned)ctas), dim3(256), 0, it, flag_ptrs_dev,
+                                   world, rank, B, epoch, ctx->tickets, ctx->flag));
+    else
+        HD_CUDA_TRY(ctx, hd_launch(ctx, k_push_columns_multi<1>, dim3((unsigned)ctas), dim3(256), 0, it, flag_ptrs_dev,
+                                   world, rank, B, epoch, ctx->tickets, ctx->flag));
     return HD_OK;
 }

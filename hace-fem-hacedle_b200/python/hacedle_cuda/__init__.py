@@ -35,7 +35,7 @@ EXPORTS = [
     "hd_decoder_generate_ex", "hd_gguf_open", "hd_gguf_open_memory", "hd_gguf_close", "hd_gguf_error", "hd_gguf_counts", "hd_gguf_tensor",
     "hd_gguf_find_tensor", "hd_gguf_kv", "hd_gguf_find_key", "hd_gguf_kv_int", "hd_gguf_kv_float", "hd_gguf_kv_string",
     "hd_gguf_kv_array", "hd_gguf_upload", "hd_logits_process", "hd_sample_rows",
-    "hd_xbuf_alloc", "hd_xbuf_free", "hd_ipc_handle", "hd_ipc_open", "hd_ipc_close", "hd_push_columns",
+    "hd_xbuf_alloc", "hd_xbuf_free", "hd_ipc_handle", "hd_ipc_open", "hd_ipc_close", "hd_push_columns", "hd_push_columns_multi",
     "hd_kv_arena_create", "hd_kv_arena_free", "hd_kv_layer", "hd_kv_allocate", "hd_kv_release", "hd_kv_session",
     "hd_kv_advance", "hd_kv_soul_sessions", "hd_kv_snapshot", "hd_kv_restore", "hd_kv_snapshot_free",
     "hd_kv_append_slots", "hd_attention_decode_slots", "hd_quantize_q8_1", "hd_qgemv_q8_1",
@@ -83,6 +83,7 @@ def lib() -> C.CDLL:
         "hd_xbuf_alloc": [V, SZ, C.POINTER(V)], "hd_xbuf_free": [V, V], "hd_ipc_handle": [V, V, V],
         "hd_ipc_open": [V, V, C.POINTER(V)], "hd_ipc_close": [V, V],
         "hd_push_columns": [V, V, V, V, I, I, I, I64, I],
+        "hd_push_columns_multi": [V, I, V, V, V, V, I, I, I, I],
         "hd_kv_append": [V, V, V, V, V, V, I, I, I, I, I],
         "hd_attention_decode": [V, V, V, V, V, I, I, I, I, I, V],
         "hd_attention_prefill": [V, V, V, V, I, I, I, I, I, I, V],

@@ -131,6 +131,32 @@ class PeerExchange:
         self.ctx._check(lib().hd_push_columns(self.ctx.h, y.data_ptr(), self.full_ptrs[i][k].data_ptr(),
                                               self.flag_ptrs.data_ptr(), self.world, self.rank, B, n, self.epoch))
 
+    def push_all(self, items, B: int):
+        """One exchange of several outputs: items = [(i, y, n), ...], each as
+        push(i, y, B, n), in one launch with one completion handshake
+        (hd_push_columns_multi).  Every rank makes the same calls."""
+        import ctypes as C
+
+        from . import lib
+        if not 1 <= len(items) <= 16:
+            raise ValueError("push_all takes 1..16 outputs")
+        ys, fulls, ns = [], [], []
+        for i, y, n in items:
+            Bmax, N = self.shapes[i]
+            if B > Bmax or n * self.world != N:
+                raise ValueError(f"slice [{B}][{n}] does not fit output {i} [{Bmax}][{N}] over {self.world} ranks")
+        self.epoch += 1
+        for i, y, n in items:
+            k = self.uses[i] % 2
+            self.uses[i] += 1
+            ys.append(y.data_ptr())
+            fulls.append(self.full_ptrs[i][k].data_ptr())
+            ns.append(n)
+        cnt = len(items)
+        self.ctx._check(lib().hd_push_columns_multi(self.ctx.h, cnt, (C.c_void_p * cnt)(*ys),
+                                                    (C.c_void_p * cnt)(*fulls), (C.c_int64 * cnt)(*ns),
+                                                    self.flag_ptrs.data_ptr(), self.world, self.rank, B, self.epoch))
+
     def close(self):
         import torch
 

@@ -248,6 +248,16 @@ int hd_ipc_open(hd_ctx *ctx, const void *handle, void **peer_ptr);
 int hd_ipc_close(hd_ctx *ctx, void *peer_ptr);
 int hd_push_columns(hd_ctx *ctx, const float *y_dev, float *const *full_ptrs_dev, int32_t *const *flag_ptrs_dev,
                     int world, int rank, int B, int64_t n, int32_t epoch);
+/* hd_push_columns_multi: the same for `count` (1..HD_PUSH_MAX) outputs of one
+ * layer in one launch with one completion handshake: output i is y_devs[i]
+ * [B][ns[i]] into the full buffers of DEVICE pointer array full_ptrs_devs[i]
+ * ([B][world*ns[i]] each).  y_devs, full_ptrs_devs and ns are HOST arrays of
+ * `count` entries.  One epoch covers all the outputs; the reuse rule above
+ * applies per output. */
+#define HD_PUSH_MAX 16
+int hd_push_columns_multi(hd_ctx *ctx, int count, const float *const *y_devs, float *const *const *full_ptrs_devs,
+                          const int64_t *ns, int32_t *const *flag_ptrs_dev, int world, int rank, int B,
+                          int32_t epoch);
 
 /* ------------------------------------------------------- KV and attention */
 /* Device KV cache (KvCache::append, core/ops/block.rs:268-282, KvArena

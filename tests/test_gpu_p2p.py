@@ -3,7 +3,9 @@ hacedle_cuda.shard.PeerExchange) on 2 GPUs, one process per GPU: every rank
 ends with every rank's slice, bit-exact, in the final [B][G*n] layout, for
 the float4 and the one-float paths and for repeated exchanges (growing
 epochs); many exchanges with a device consumer between them and no host
-synchronization; and the bounded wait expiring when a rank skips an exchange
+synchronization; several outputs in one launch with one handshake
+(hd_push_columns_multi, PeerExchange.push_all), mixed with single pushes;
+and the bounded wait expiring when a rank skips an exchange
 (the context reports HD_E_TIMEOUT and stays usable).  Skipped on machines
 with fewer than two GPUs.  Host messages go over gloo; no NCCL, no NVLS."""
 import multiprocessing as mp
@@ -120,6 +122,64 @@ def _rank_pipelined(rank, world, port, q):
         q.put((rank, False, f"{type(e).__name__}: {e}"))
 
 
+def _rank_multi(rank, world, port, q):
+    """push_all: the outputs of a layer (shapes of both vector widths) in one
+    launch, back to back with a slow consumer on rank 1, alternating with
+    single pushes of the same outputs."""
+    import sys
+    sys.path[:0] = [ROOT, os.path.join(ROOT, "hace-fem-hacedle_b200", "python")]
+    try:
+        import datetime
+
+        import torch
+        import torch.distributed as dist
+
+        torch.cuda.set_device(rank)
+        dist.init_process_group("gloo", init_method=f"tcp://127.0.0.1:{port}", rank=rank, world_size=world,
+                                timeout=datetime.timedelta(seconds=60))
+        import hacedle_cuda as hc
+        from hacedle_cuda import shard
+
+        def ago(obj):
+            out = [None] * world
+            dist.all_gather_object(out, obj)
+            return out
+
+        ctx = hc.Context(rank)
+        for cases in ([(4, 1792), (4, 256), (4, 9472)], [(3, 33), (3, 100), (3, 5)]):   # float4 / one-float paths
+            B = cases[0][0]
+            ex = shard.PeerExchange(ctx, world, rank, [(B, n * world) for _, n in cases], ago)
+            E = 8
+            ys = {(e, i): [np.random.default_rng(1000 * e + 10 * i + r).standard_normal((B, n), dtype=np.float32)
+                           for r in range(world)] for e in range(E) for i, (_, n) in enumerate(cases)}
+            dev = {k: torch.from_numpy(v[rank]).cuda() for k, v in ys.items()}
+            outs = {k: torch.empty(B, cases[k[1]][1] * world, device="cuda") for k in ys}
+            torch.cuda.synchronize()
+            dist.barrier()
+            for e in range(E):
+                if e % 3 == 2:   # every third exchange output by output
+                    for i, (_, n) in enumerate(cases):
+                        ex.push(i, dev[(e, i)], B, n)
+                else:
+                    ex.push_all([(i, dev[(e, i)], n) for i, (_, n) in enumerate(cases)], B)
+                if rank == 1:
+                    torch.cuda._sleep(200000)   # a slow consumer
+                for i in range(len(cases)):
+                    outs[(e, i)].copy_(ex.full(i, B))
+            torch.cuda.synchronize()
+            ctx.check_device_errors()
+            ok = all(np.array_equal(outs[k].cpu().numpy(), np.concatenate(v, axis=1)) for k, v in ys.items())
+            dist.barrier()
+            ex.close()
+            if not ok:
+                break
+        ctx.close()
+        dist.destroy_process_group()
+        q.put((rank, ok, ""))
+    except Exception as e:  # reported to the parent
+        q.put((rank, False, f"{type(e).__name__}: {e}"))
+
+
 def _rank_timeout(rank, world, port, q):
     """Rank 1 skips an exchange: rank 0's bounded wait for its flag runs out
     (about 1 s) and the context reports HD_E_TIMEOUT; the GPU stays usable."""
@@ -196,6 +256,10 @@ def _run(target):
 
 def test_push_columns_pipelined_two_gpus():
     _run(_rank_pipelined)
+
+
+def test_push_columns_multi_two_gpus():
+    _run(_rank_multi)
 
 
 def test_push_columns_bounded_wait_times_out_two_gpus():
