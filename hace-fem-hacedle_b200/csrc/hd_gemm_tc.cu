@@ -1289,6 +1289,287 @@ __global__ void __launch_bounds__(TC4_THREADS, 1)
     }
 }
 
+// ------------------------------------------------------------------- v5
+// The two-pass GEMM with each MMA across an SM pair (bf16 mode):
+// tcgen05.mma.cta_group::2 with M = 256.  A CTA pair (a cluster of two) owns
+// a tile of 256 weight rows x BT tokens: CTA r of the pair loads weight rows
+// 128 r .. 128 r + 127 of the tile and tokens BT/2 r .. BT/2 r + BT/2 - 1
+// into the same shared-memory offsets, and the leader's (rank 0) single MMA
+// thread issues MMAs that read both CTAs' halves; each CTA's tensor memory
+// receives its 128 rows x BT tokens of the product.
+// Why.  In the one-SM kernel each 64-deep K-step moves (128 + BT) x 128 bytes
+// through an SM's shared memory twice (TMA write, MMA read): at BT = 192,
+// 80 KB against 384 cycles of MMA, so shared memory (~128 B per cycle), not
+// the tensor pipe, set the pace.  Split across the pair, an SM moves
+// (128 + BT/2) x 128 bytes per step for the same 2 BT cycles of MMA per SM:
+// at BT = 256, 64 KB against 512 cycles.
+// Protocol (per stage s): each CTA's producer waits for its own empty[s]
+// (released by the leader's tcgen05.commit multicast to both CTAs), the
+// leader's producer posts the transaction bytes of both halves on the
+// leader's full[s], and both CTAs' TMA loads (cta_group::2, no multicast)
+// complete on the leader's full[s]; the leader's MMA thread waits for
+// full[s].  The accumulators: acc_full[b] in both CTAs (multicast commit),
+// acc_empty[b] in the leader with 256 arrivals (the 128 epilogue threads of
+// each CTA, the peer's arriving remotely).  Tensor memory is allocated and
+// freed by warp 4 of both CTAs (cta_group::2).  Cluster barriers after the
+// barrier initialisation and before the end keep either CTA from signalling
+// or reading a partner that has not started or has already left.  Waits are
+// bounded as in v4.
+constexpr int TC5_MAX_STG = 12;
+__host__ __device__ inline int tc5_stage_bytes(int bt) { return (128 + bt / 2) * BK * 2; }
+__host__ __device__ inline int tc5_stages(int bt) {
+    const int n = (TC4_SMEM_MAX - 2048 - TC4_EPI_BYTES) / tc5_stage_bytes(bt);
+    return n > TC5_MAX_STG ? TC5_MAX_STG : n;
+}
+// Instruction descriptor: fp32 accumulate, bf16 A and B, both K-major, M = 256 (the pair), N = bt.
+__host__ __device__ constexpr uint32_t idesc_bf16_pair(int n) {
+    return (1u << 4) | (1u << 7) | (1u << 10) | ((uint32_t)(n >> 3) << 17) | ((uint32_t)(256 >> 4) << 24);
+}
+__device__ __forceinline__ uint32_t tc5_rank() {
+    uint32_t r;
+    asm volatile("mov.u32 %0, %%cluster_ctarank;" : "=r"(r));
+    return r;
+}
+__device__ __forceinline__ void tc5_cluster_sync() {
+    asm volatile("barrier.cluster.arrive.release.aligned;" ::: "memory");
+    asm volatile("barrier.cluster.wait.acquire.aligned;" ::: "memory");
+}
+__device__ __forceinline__ uint32_t tc5_mapa(uint32_t addr, uint32_t rank) {
+    uint32_t r;
+    asm volatile("mapa.shared::cluster.u32 %0, %1, %2;" : "=r"(r) : "r"(addr), "r"(rank));
+    return r;
+}
+// A 2D tile load of one CTA of the pair, completing on the barrier at the
+// cluster address bar (the leader's).
+__device__ __forceinline__ void tma_2d_pair(uint32_t dst, const CUtensorMap *tm, int x, int y, uint32_t bar) {
+    asm volatile(
+        "cp.async.bulk.tensor.2d.cta_group::2.shared::cluster.global.mbarrier::complete_tx::bytes [%0], [%1, {%2, "
+        "%3}], [%4];" ::"r"(dst),
+        "l"((uint64_t)tm), "r"(x), "r"(y), "r"(bar)
+        : "memory");
+}
+__device__ __forceinline__ void mbar_arrive_cluster(uint32_t bar) {
+    asm volatile("mbarrier.arrive.shared::cluster.b64 _, [%0];" ::"r"(bar) : "memory");
+}
+// Completion of the leader's MMAs issued so far, as one arrival on the
+// barrier at this offset in both CTAs of the pair.
+__device__ __forceinline__ void commit_pair(uint32_t bar) {
+    asm volatile(
+        "tcgen05.commit.cta_group::2.mbarrier::arrive::one.shared::cluster.multicast::cluster.b64 [%0], %1;" ::"r"(bar),
+        "h"((uint16_t)3)
+        : "memory");
+}
+
+__global__ void __launch_bounds__(TC4_THREADS, 1)
+    k_gemm_tc5(const __grid_constant__ CUtensorMap tmw, const __grid_constant__ CUtensorMap tmx,
+               const __grid_constant__ CUtensorMap tmy, float *__restrict__ Y, int T, int N, int BT, int ntm2,
+               int ntiles, int ksteps, int ytma, int *flag) {
+    extern __shared__ uint8_t smem_raw[];
+    __shared__ __align__(8) uint64_t full[TC5_MAX_STG], empty[TC5_MAX_STG];
+    __shared__ __align__(8) uint64_t acc_full[2], acc_empty[2], fin_bar;
+    __shared__ uint32_t tmem_base_sh;
+
+    const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+    const uint32_t rank = tc5_rank();   // 0: the leader, which issues the MMAs
+    const int pair = blockIdx.x >> 1, npairs = gridDim.x >> 1;
+    const int SB = tc5_stage_bytes(BT), STG = tc5_stages(BT);
+    const int AB = 128 * BK * 2, HB = BT / 2;
+    uint8_t *base = (uint8_t *)(((uintptr_t)smem_raw + 1023) & ~(uintptr_t)1023);
+
+    if (threadIdx.x == 0) {
+        for (int s = 0; s < STG; s++) {
+            mbar_init(smem_u32(&full[s]), 1);
+            mbar_init(smem_u32(&empty[s]), 1);
+        }
+        for (int i = 0; i < 2; i++) {
+            mbar_init(smem_u32(&acc_full[i]), 1);
+            mbar_init(smem_u32(&acc_empty[i]), 256);
+        }
+        mbar_init(smem_u32(&fin_bar), 1);
+        asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
+        asm volatile("prefetch.tensormap [%0];" ::"l"((uint64_t)&tmw) : "memory");
+        asm volatile("prefetch.tensormap [%0];" ::"l"((uint64_t)&tmx) : "memory");
+        if (ytma) asm volatile("prefetch.tensormap [%0];" ::"l"((uint64_t)&tmy) : "memory");
+    }
+    if (warp == TC4_MMA) {
+        asm volatile("tcgen05.alloc.cta_group::2.sync.aligned.shared::cta.b32 [%0], %1;" ::"r"(smem_u32(&tmem_base_sh)),
+                     "r"(512));
+        asm volatile("tcgen05.relinquish_alloc_permit.cta_group::2.sync.aligned;");
+    }
+    tc_fence_before();
+    __syncthreads();
+    tc5_cluster_sync();   // both CTAs' barriers initialised before any remote arrival
+    tc_fence_after();
+    const uint32_t tmem = tmem_base_sh;
+    pdl_wait();
+    pdl_trigger();
+
+    if (warp < TC4_PW) {
+        // ---- TMA producers (both CTAs), steps dealt to the warps in turn as in v4
+        const int npw = STG < TC4_PW ? STG : TC4_PW;
+        if (warp < npw) {
+            const uint32_t full0 = tc5_mapa(smem_u32(&full[0]), 0);   // the leader's full[0]
+            int g = 0, s = 0, turn = 0;
+            uint32_t ph = 0;
+            bool alive = true;
+            for (int item = pair; item < ntiles && alive; item += npairs) {
+                const int row0 = (item % ntm2) * 256 + (int)rank * 128, t0 = (item / ntm2) * BT + (int)rank * HB;
+                for (int ks = 0; ks < ksteps; ks++) {
+                    if (turn == warp) {
+                        if (!mbar_wait_warp(smem_u32(&empty[s]), ph ^ 1, flag, 64)) { alive = false; break; }
+                        if (lane == 0) {
+                            const uint32_t st = smem_u32(base + s * SB), bar = full0 + 8u * (uint32_t)s;
+                            if (rank == 0) mbar_expect_tx(smem_u32(&full[s]), 2 * SB);
+                            tma_2d_pair(st, &tmw, ks * BK, row0, bar);
+                            tma_2d_pair(st + AB, &tmx, ks * BK, t0, bar);
+                        }
+                        __syncwarp();
+                    }
+                    g++;
+                    if (++s == STG) { s = 0; ph ^= 1; }
+                    if (++turn == npw) turn = 0;
+                }
+            }
+            // After a timeout the loads in flight complete on the leader's
+            // barrier; give them time to land in this CTA's stages.
+            if (!alive) __nanosleep(100000);
+        }
+    } else if (warp == TC4_MMA) {
+        if (rank == 0) {
+            // ---- MMA issuer (the leader's one thread)
+            const uint32_t idesc = idesc_bf16_pair(BT);
+            int s = 0, li = 0;
+            uint32_t ph = 0;
+            bool alive = true;
+            for (int item = pair; item < ntiles && alive; item += npairs, li++) {
+                const int buf = li & 1;
+                if (!mbar_wait_warp(smem_u32(&acc_empty[buf]), ((li >> 1) & 1) ^ 1, flag)) break;
+                tc_fence_after();
+                const uint32_t d = tmem + (uint32_t)(buf * BT);
+                for (int ks = 0; ks < ksteps;) {
+                    const bool two = STG >= 4 && ks + 1 < ksteps;
+                    const int s1 = s + 1 == STG ? 0 : s + 1;
+                    const uint32_t ph1 = s + 1 == STG ? ph ^ 1 : ph;
+                    bool ok = mbar_wait(smem_u32(&full[s]), ph, flag);
+                    if (two) ok = ok && mbar_wait(smem_u32(&full[s1]), ph1, flag);
+                    if (!__all_sync(0xffffffffu, ok)) { alive = false; break; }
+                    if (lane == 0) {
+#pragma unroll
+                        for (int h = 0; h < 2; h++) {
+                            if (h == 1 && !two) break;
+                            const uint32_t a0 = smem_u32(base + (h ? s1 : s) * SB), b0 = a0 + AB;
+#pragma unroll
+                            for (int kk = 0; kk < BK / 16; kk++) {
+                                const uint64_t ad = sw128_desc(a0 + kk * 32), bd = sw128_desc(b0 + kk * 32);
+                                const uint32_t acc = (ks > 0 || h > 0 || kk > 0) ? 1u : 0u;
+                                asm volatile(
+                                    "{\n .reg .pred p;\n setp.ne.b32 p, %4, 0;\n"
+                                    " tcgen05.mma.cta_group::2.kind::f16 [%0], %1, %2, %3, p;\n}\n" ::"r"(d),
+                                    "l"(ad), "l"(bd), "r"(idesc), "r"(acc));
+                            }
+                        }
+                        commit_pair(smem_u32(&empty[s]));
+                        if (two) commit_pair(smem_u32(&empty[s1]));
+                    }
+                    __syncwarp();
+                    if (two) {
+                        s = s1 + 1 == STG ? 0 : s1 + 1;
+                        ph = s1 + 1 == STG ? ph1 ^ 1 : ph1;
+                    } else {
+                        s = s1;
+                        ph = ph1;
+                    }
+                    ks += two ? 2 : 1;
+                }
+                if (alive && lane == 0) commit_pair(smem_u32(&acc_full[buf]));
+                __syncwarp();
+            }
+            // Completion of this commit covers every MMA issued above (in both
+            // CTAs' tensor memory); awaited also after a timeout.
+            if (lane == 0) commit_pair(smem_u32(&fin_bar));
+            __syncwarp();
+        }
+        mbar_wait_quiet(smem_u32(&fin_bar), 0);
+    } else {
+        // ---- epilogue (both CTAs): this CTA's 128 rows of the tile
+        const int q = warp & 3, et = threadIdx.x - TC4_EPI * 32;
+        float *ebuf = (float *)(base + STG * SB);
+        const uint32_t ae0 = tc5_mapa(smem_u32(&acc_empty[0]), 0);   // the leader's acc_empty[0]
+        int li = 0, ch = 0;
+        for (int item = pair; item < ntiles; item += npairs, li++) {
+            const int buf = li & 1;
+            const int row0 = (item % ntm2) * 256 + (int)rank * 128;
+            const int64_t n = (int64_t)row0 + 32 * q + lane;
+            const int t0 = (item / ntm2) * BT;
+            const bool ok = epi_all(mbar_wait(smem_u32(&acc_full[buf]), (li >> 1) & 1, flag, 128));
+            tc_fence_after();
+            // (the peer's rows of the last tile may all lie past N: nothing to store)
+            for (int c0 = 0; ok && row0 < N && c0 < BT && t0 + c0 < T; c0 += TC4_ECH, ch++) {
+                uint32_t rr[16];
+                const uint32_t taddr = tmem + ((uint32_t)(32 * q) << 16) + (uint32_t)(buf * BT + c0);
+                asm volatile(
+                    "tcgen05.ld.sync.aligned.32x32b.x16.b32 {%0,%1,%2,%3,%4,%5,%6,%7,%8,%9,%10,%11,%12,%13,%14,%15}, "
+                    "[%16];"
+                    : "=r"(rr[0]), "=r"(rr[1]), "=r"(rr[2]), "=r"(rr[3]), "=r"(rr[4]), "=r"(rr[5]), "=r"(rr[6]),
+                      "=r"(rr[7]), "=r"(rr[8]), "=r"(rr[9]), "=r"(rr[10]), "=r"(rr[11]), "=r"(rr[12]), "=r"(rr[13]),
+                      "=r"(rr[14]), "=r"(rr[15])
+                    : "r"(taddr));
+                asm volatile("tcgen05.wait::ld.sync.aligned;" ::: "memory");
+                float v[16];
+#pragma unroll
+                for (int j = 0; j < 16; j++) v[j] = __uint_as_float(rr[j]);
+                if (ytma) {
+                    float *sb = ebuf + (ch & 1) * (TC4_ECH * 128);
+                    if (et == 0) bulk_wait_read1();
+                    epi_sync();
+#pragma unroll
+                    for (int j = 0; j < 16; j++) sb[j * 128 + 32 * q + lane] = v[j];
+                    fence_async_smem();
+                    epi_sync();
+                    if (et == 0) {
+                        tma_store_2d(&tmy, smem_u32(sb), row0, t0 + c0);
+                        bulk_commit();
+                    }
+                } else if (n < N) {
+#pragma unroll
+                    for (int j = 0; j < 16; j++)
+                        if (t0 + c0 + j < T) Y[(int64_t)(t0 + c0 + j) * N + n] = v[j];
+                }
+            }
+            tc_fence_before();
+            mbar_arrive_cluster(ae0 + 8u * (uint32_t)buf);
+            if (!ok) break;
+        }
+        if (et == 0) bulk_wait_all();
+    }
+    tc_fence_before();
+    __syncthreads();
+    tc5_cluster_sync();   // neither CTA leaves while its partner may still signal it or read its stages
+    if (warp == TC4_MMA) {
+        tc_fence_after();
+        asm volatile("tcgen05.dealloc.cta_group::2.sync.aligned.b32 %0, %1;" ::"r"(tmem), "r"(512));
+    }
+}
+
+// Token tile of the pair GEMM: a multiple of 32 (64..256) minimising rounds
+// of tiles per pair x cycles per K-step (the larger of its MMA time, 2 BT per
+// SM, and the shared-memory traffic of one SM's halves, written once and read
+// once at ~128 B per cycle).
+int tc5_pick_bt(int64_t mt2, int T, int pairs) {
+    int best_bt = 64;
+    double best = 1e30;
+    for (int bt = 64; bt <= 256; bt += 32) {
+        if (bt > 64 && T <= bt - 32) break;
+        if (tc5_stages(bt) < 3) continue;
+        const int64_t tiles = mt2 * ((T + bt - 1) / bt);
+        const double rounds = (double)((tiles + pairs - 1) / pairs);
+        const double mma = 2.0 * bt, smem = 2.0 * tc5_stage_bytes(bt) / 128.0;
+        const double cost = rounds * ((mma > smem ? mma : smem) + 64.0);
+        if (cost < best - 1e-9) { best = cost; best_bt = bt; }
+    }
+    return best_bt;
+}
+
 template <int TYPE, int BT, int EX>
 cudaError_t launch_tc3(hd_ctx *ctx, const hd_weight *w, const CUtensorMap &tmx, const CUtensorMap &tmx_lo, float *Y,
                        int T, int ks, const int *rowshift) {
@@ -1328,8 +1609,57 @@ int tc4_pick_bt(int64_t mt, int T, int sms, int ex) {
     return best_bt;
 }
 
+// The pair GEMM (k_gemm_tc5) on the prepared bf16 operands wb [N][K] and
+// xb [T][K]: clusters of two CTAs, one pair per two SMs.
+int launch_tc5(hd_ctx *ctx, const uint8_t *wb, const uint8_t *xb, int64_t N, int64_t K, int T, float *Y, int ksteps) {
+    const int64_t mt2 = (N + 255) / 256;
+    const int pairs_max = ctx->sm_count / 2;
+    int bt = tc5_pick_bt(mt2, T, pairs_max);
+    if (const char *env = getenv("HACEDLE_TC_BT")) {
+        const int b = atoi(env);
+        if (b >= 64 && b <= 256 && b % 32 == 0) bt = b;
+    }
+    EncodeTiledFn enc = encode_tiled();
+    if (!enc) return hd_fail(ctx, HD_E_CUDA, "hd_qgemm: cuTensorMapEncodeTiled is not available");
+    auto make = [&](CUtensorMap *m, const void *ptr, int64_t rows, int box_rows) {
+        cuuint64_t dims[2] = {(cuuint64_t)K, (cuuint64_t)rows};
+        cuuint64_t strides[1] = {(cuuint64_t)K * 2};
+        cuuint32_t box[2] = {(cuuint32_t)BK, (cuuint32_t)box_rows};
+        cuuint32_t estr[2] = {1, 1};
+        return enc(m, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 2, const_cast<void *>(ptr), dims, strides, box, estr,
+                   CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
+                   CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+    };
+    CUtensorMap tw, tx, ty;
+    CUresult cr = make(&tw, wb, N, 128);
+    if (cr == CUDA_SUCCESS) cr = make(&tx, xb, T, bt / 2);
+    int ytma = 0;
+    if (cr == CUDA_SUCCESS && N % 4 == 0 && getenv("HACEDLE_TC4_DIRECT_STORE") == nullptr) {
+        cuuint64_t dims[2] = {(cuuint64_t)N, (cuuint64_t)T};
+        cuuint64_t strides[1] = {(cuuint64_t)N * 4};
+        cuuint32_t box[2] = {128, (cuuint32_t)TC4_ECH};
+        cuuint32_t estr[2] = {1, 1};
+        cr = enc(&ty, CU_TENSOR_MAP_DATA_TYPE_FLOAT32, 2, Y, dims, strides, box, estr, CU_TENSOR_MAP_INTERLEAVE_NONE,
+                 CU_TENSOR_MAP_SWIZZLE_NONE, CU_TENSOR_MAP_L2_PROMOTION_NONE, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+        ytma = 1;
+    } else {
+        ty = tx;
+    }
+    if (cr != CUDA_SUCCESS) return hd_fail(ctx, HD_E_CUDA, "hd_qgemm: cuTensorMapEncodeTiled failed (%d)", (int)cr);
+    const size_t smem = (size_t)tc5_stages(bt) * tc5_stage_bytes(bt) + TC4_EPI_BYTES + 1024;
+    const int ntm2 = (int)mt2, ntiles = ntm2 * ((T + bt - 1) / bt);
+    const int pairs = ntiles < pairs_max ? ntiles : pairs_max;
+    cudaError_t e = cudaFuncSetAttribute(k_gemm_tc5, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
+    if (e == cudaSuccess)
+        e = hd_launch_cluster(ctx, k_gemm_tc5, dim3(2 * pairs), dim3(TC4_THREADS), smem, 2, tw, tx, ty, Y, T, (int)N, bt,
+                              ntm2, ntiles, ksteps, ytma, ctx->flag);
+    if (e != cudaSuccess) return hd_fail(ctx, HD_E_CUDA, "hd_qgemm (tcgen05 pair GEMM): %s", cudaGetErrorString(e));
+    return HD_OK;
+}
+
 // The two-pass path (see k_gemm_tc4).  Activations as for v3; the weight is
-// dequantized into ctx->wbf first.
+// dequantized into ctx->wbf first.  The bf16 mode runs the pair GEMM
+// (k_gemm_tc5) where its tiles fill the SM pairs.
 int qgemm_tc4(hd_ctx *ctx, const hd_weight *w, const float *X, float *Y, int T, int exact) {
     const int64_t N = w->rows, K = w->cols;
     const size_t plane = ((size_t)T * K * 2 + 255) & ~(size_t)255;
@@ -1355,6 +1685,18 @@ int qgemm_tc4(hd_ctx *ctx, const hd_weight *w, const float *X, float *Y, int T, 
                           (uint16_t *)nullptr, 0, nrb, nw, X, T, (uint16_t *)xb, (uint16_t *)nullptr, (int *)nullptr);
     });
     if (e != cudaSuccess) return hd_fail(ctx, HD_E_CUDA, "hd_qgemm (operand preparation): %s", cudaGetErrorString(e));
+    if (!exact) {
+        // The pair GEMM where its 256-row tiles fill the SM pairs (measured on
+        // B200, prep + GEMM: 18944 x 3584 Q4_K at T = 512 716 against 616
+        // TFLOP/s, 3584 x 3584 at T = 2048 837 against 798, 4864 x 896 Q5_0
+        // 644 against 637); with fewer tiles (896 x 4864: 44 tiles for 74
+        // pairs) the one-SM kernel, 466 against 424.  HACEDLE_TC5 = 1 / 0
+        // forces it on / off.
+        const char *v5 = getenv("HACEDLE_TC5");
+        const int64_t tiles2 = ((N + 255) / 256) * ((T + 191) / 192);
+        const bool pair = v5 && *v5 ? *v5 != '0' : tiles2 >= ctx->sm_count / 2;
+        if (pair) return launch_tc5(ctx, wb, xb, N, K, T, Y, (int)((w->units + 1) / 2));
+    }
 
     const int64_t mt = (N + 127) / 128;
     int bt = tc4_pick_bt(mt, T, ctx->sm_count, exact);

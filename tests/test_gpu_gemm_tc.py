@@ -204,3 +204,43 @@ def test_qgemm_fp32_two_pass_any_rows(ctx, monkeypatch, t, N, K, T):
     ctx.qgemm(w, Xd, Y2, precision=0)
     torch.cuda.synchronize()
     assert torch.equal(Y, Y2)
+
+
+@pytest.mark.parametrize("t,N,K,T", [(S.GGML_Q5_0, 100, 96, 1), (S.GGML_Q5_0, 257, 160, 70), (S.GGML_Q4_K, 896, 512, 33),
+                                     (S.GGML_Q6_K, 1000, 256, 300), (S.GGML_Q8_0, 4864, 896, 129),
+                                     (S.GGML_Q4_K, 1152, 1024, 2048)])
+@pytest.mark.parametrize("bt", ["", "64", "160", "256"])
+def test_qgemm_pair_gemm(ctx, monkeypatch, t, N, K, T, bt):
+    """The bf16 two-pass GEMM on SM pairs (k_gemm_tc5: tcgen05.mma.cta_group::2,
+    M = 256 over two CTAs of a cluster, each CTA loading half of the token
+    tile): any row count (a peer whose 128 rows lie past N stores nothing),
+    token tails, token tiles 64..256; NaN-filled outputs fully written; equal
+    to the one-SM kernel's result within the bf16 contract, reruns bitwise
+    equal."""
+    import torch
+    monkeypatch.setenv("HACEDLE_TC4_MIN_T", "1")
+    monkeypatch.setenv("HACEDLE_TC5", "1")
+    if bt:
+        monkeypatch.setenv("HACEDLE_TC_BT", bt)
+    raw = S.gen_weight(t, N, K, 160 + N)
+    X = S.gen_activations(T, K, 161)
+    w = ctx.weight(t, raw, N, K)
+    Xd = torch.from_numpy(X).cuda()
+    outs = []
+    for _ in range(2):
+        Y = torch.full((T, N), float("nan"), device="cuda")
+        ctx.qgemm(w, Xd, Y, precision=1)
+        ctx.check_device_errors()
+        outs.append(Y.cpu().numpy())
+    monkeypatch.setenv("HACEDLE_TC5", "0")
+    Y1 = torch.full((T, N), float("nan"), device="cuda")
+    ctx.qgemm(w, Xd, Y1, precision=1)
+    ctx.check_device_errors()
+    ref = X @ O.dequantize(t, raw, N * K).reshape(N, K).T
+    got = outs[0]
+    assert np.isfinite(got).all()
+    assert np.abs(got - ref).max() / np.abs(ref).max() <= TOL
+    assert np.array_equal(outs[0].view(np.uint32), outs[1].view(np.uint32))
+    one_sm = Y1.cpu().numpy()
+    assert np.abs(got - one_sm).max() <= 1e-6 * np.abs(ref).max()
+    w.free()
