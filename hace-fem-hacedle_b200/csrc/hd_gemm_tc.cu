@@ -1315,11 +1315,34 @@ __global__ void __launch_bounds__(TC4_THREADS, 1)
 // barrier initialisation and before the end keep either CTA from signalling
 // or reading a partner that has not started or has already left.  Waits are
 // bounded as in v4.
+// The issuing thread sets the pace: a tcgen05.mma costs it ~100 cycles to
+// issue whatever its N (clock64 traces of the leader's MMA thread), and a
+// barrier wait ~190 cycles even when the stage has landed.  So stages go in
+// pairs with one (full, empty) barrier pair per two K-steps, one wait and
+// one commit per 8 MMAs, and the thread's loop is lean: descriptors are one
+// add from per-kernel bases.  Measured (prep + GEMM, B200): Q5_0 4864 x 896
+// at T = 2048 26.2 us (682 TFLOP/s; one-SM kernel 28.0), Q4_K 3584 x 3584
+// 57.8 us (911; 65.6), Q4_K 18944 x 3584 at T = 512 96.5 us (721; 112.9).
 constexpr int TC5_MAX_STG = 12;
+constexpr int TC5_EPI_WARPS = 8;                          // two per TMEM lane quarter, each half the columns
+constexpr int TC5_THREADS = (TC4_EPI + TC5_EPI_WARPS) * 32;
+constexpr int TC5_EPI_BYTES = 2 * TC4_EPI_BYTES;          // two output chunk buffers per column half
 __host__ __device__ inline int tc5_stage_bytes(int bt) { return (128 + bt / 2) * BK * 2; }
 __host__ __device__ inline int tc5_stages(int bt) {
-    const int n = (TC4_SMEM_MAX - 2048 - TC4_EPI_BYTES) / tc5_stage_bytes(bt);
+    const int n = (TC4_SMEM_MAX - 2048 - TC5_EPI_BYTES) / tc5_stage_bytes(bt);
     return n > TC5_MAX_STG ? TC5_MAX_STG : n;
+}
+// Named barrier 1 + h of the 128 epilogue threads of column half h, and a
+// vote over them.
+__device__ __forceinline__ void epi5_sync(int h) { asm volatile("bar.sync %0, 128;" ::"r"(1 + h) : "memory"); }
+__device__ __forceinline__ bool epi5_all(int h, bool v) {
+    uint32_t r;
+    asm volatile(
+        "{\n .reg .pred p, q;\n setp.ne.u32 p, %1, 0;\n bar.red.and.pred q, %2, 128, p;\n selp.u32 %0, 1, 0, q;\n}\n"
+        : "=r"(r)
+        : "r"((uint32_t)v), "r"(1 + h)
+        : "memory");
+    return r != 0;
 }
 // Instruction descriptor: fp32 accumulate, bf16 A and B, both K-major, M = 256 (the pair), N = bt.
 __host__ __device__ constexpr uint32_t idesc_bf16_pair(int n) {
@@ -1360,7 +1383,7 @@ __device__ __forceinline__ void commit_pair(uint32_t bar) {
         : "memory");
 }
 
-__global__ void __launch_bounds__(TC4_THREADS, 1)
+__global__ void __launch_bounds__(TC5_THREADS, 1)
     k_gemm_tc5(const __grid_constant__ CUtensorMap tmw, const __grid_constant__ CUtensorMap tmx,
                const __grid_constant__ CUtensorMap tmy, float *__restrict__ Y, int T, int N, int BT, int ntm2,
                int ntiles, int ksteps, int ytma, int *flag) {
@@ -1372,18 +1395,18 @@ __global__ void __launch_bounds__(TC4_THREADS, 1)
     const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
     const uint32_t rank = tc5_rank();   // 0: the leader, which issues the MMAs
     const int pair = blockIdx.x >> 1, npairs = gridDim.x >> 1;
-    const int SB = tc5_stage_bytes(BT), STG = tc5_stages(BT);
-    const int AB = 128 * BK * 2, HB = BT / 2;
+    const int SB = tc5_stage_bytes(BT), STG = tc5_stages(BT) & ~1, NP = STG / 2;   // stage pairs
+    const int AB = 128 * BK * 2, HB = BT / 2, kpairs = (ksteps + 1) / 2;
     uint8_t *base = (uint8_t *)(((uintptr_t)smem_raw + 1023) & ~(uintptr_t)1023);
 
     if (threadIdx.x == 0) {
-        for (int s = 0; s < STG; s++) {
+        for (int s = 0; s < NP; s++) {
             mbar_init(smem_u32(&full[s]), 1);
             mbar_init(smem_u32(&empty[s]), 1);
         }
         for (int i = 0; i < 2; i++) {
             mbar_init(smem_u32(&acc_full[i]), 1);
-            mbar_init(smem_u32(&acc_empty[i]), 256);
+            mbar_init(smem_u32(&acc_empty[i]), 2 * TC5_EPI_WARPS * 32);
         }
         mbar_init(smem_u32(&fin_bar), 1);
         asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
@@ -1405,28 +1428,36 @@ __global__ void __launch_bounds__(TC4_THREADS, 1)
     pdl_trigger();
 
     if (warp < TC4_PW) {
-        // ---- TMA producers (both CTAs), steps dealt to the warps in turn as in v4
-        const int npw = STG < TC4_PW ? STG : TC4_PW;
+        // ---- TMA producers (both CTAs).  Stages go in pairs: one barrier
+        // pair (full, empty) per two K-steps, so that the MMA thread waits and
+        // commits once per 8 MMAs.  Pairs of steps are dealt to the warps in
+        // turn as the steps are in v4.
+        const int npw = NP < TC4_PW ? NP : TC4_PW;
         if (warp < npw) {
             const uint32_t full0 = tc5_mapa(smem_u32(&full[0]), 0);   // the leader's full[0]
-            int g = 0, s = 0, turn = 0;
+            int g = 0, sp = 0, turn = 0;
             uint32_t ph = 0;
             bool alive = true;
             for (int item = pair; item < ntiles && alive; item += npairs) {
                 const int row0 = (item % ntm2) * 256 + (int)rank * 128, t0 = (item / ntm2) * BT + (int)rank * HB;
-                for (int ks = 0; ks < ksteps; ks++) {
+                for (int kp = 0; kp < kpairs; kp++) {
                     if (turn == warp) {
-                        if (!mbar_wait_warp(smem_u32(&empty[s]), ph ^ 1, flag, 64)) { alive = false; break; }
+                        if (!mbar_wait_warp(smem_u32(&empty[sp]), ph ^ 1, flag, 64)) { alive = false; break; }
                         if (lane == 0) {
-                            const uint32_t st = smem_u32(base + s * SB), bar = full0 + 8u * (uint32_t)s;
-                            if (rank == 0) mbar_expect_tx(smem_u32(&full[s]), 2 * SB);
-                            tma_2d_pair(st, &tmw, ks * BK, row0, bar);
-                            tma_2d_pair(st + AB, &tmx, ks * BK, t0, bar);
+                            const int nst = 2 * kp + 1 < ksteps ? 2 : 1;
+                            const uint32_t bar = full0 + 8u * (uint32_t)sp;
+                            if (rank == 0) mbar_expect_tx(smem_u32(&full[sp]), 2 * nst * SB);
+                            for (int j = 0; j < nst; j++) {
+                                const uint32_t st = smem_u32(base + (2 * sp + j) * SB);
+                                const int ks = 2 * kp + j;
+                                tma_2d_pair(st, &tmw, ks * BK, row0, bar);
+                                tma_2d_pair(st + AB, &tmx, ks * BK, t0, bar);
+                            }
                         }
                         __syncwarp();
                     }
                     g++;
-                    if (++s == STG) { s = 0; ph ^= 1; }
+                    if (++sp == NP) { sp = 0; ph ^= 1; }
                     if (++turn == npw) turn = 0;
                 }
             }
@@ -1435,76 +1466,67 @@ __global__ void __launch_bounds__(TC4_THREADS, 1)
             if (!alive) __nanosleep(100000);
         }
     } else if (warp == TC4_MMA) {
-        if (rank == 0) {
-            // ---- MMA issuer (the leader's one thread)
+        if (rank == 0 && lane == 0) {
+            // ---- MMA issuer: the leader's lane 0 alone (the rest of the warp
+            // waits below).  The issuing thread's own instructions set the
+            // pace of short MMAs, so its loop is lean: descriptors are one
+            // add from per-kernel bases (stages are contiguous, a descriptor
+            // holds the address / 16), and the waits are its own.
             const uint32_t idesc = idesc_bf16_pair(BT);
-            int s = 0, li = 0;
+            const uint64_t adesc0 = sw128_desc(smem_u32(base)), bdesc0 = sw128_desc(smem_u32(base) + AB);
+            const uint32_t sstep = (uint32_t)(SB >> 4);
+            int sp = 0, li = 0;
             uint32_t ph = 0;
             bool alive = true;
             for (int item = pair; item < ntiles && alive; item += npairs, li++) {
                 const int buf = li & 1;
-                if (!mbar_wait_warp(smem_u32(&acc_empty[buf]), ((li >> 1) & 1) ^ 1, flag)) break;
+                if (!mbar_wait(smem_u32(&acc_empty[buf]), ((li >> 1) & 1) ^ 1, flag)) break;
                 tc_fence_after();
                 const uint32_t d = tmem + (uint32_t)(buf * BT);
-                for (int ks = 0; ks < ksteps;) {
-                    const bool two = STG >= 4 && ks + 1 < ksteps;
-                    const int s1 = s + 1 == STG ? 0 : s + 1;
-                    const uint32_t ph1 = s + 1 == STG ? ph ^ 1 : ph;
-                    bool ok = mbar_wait(smem_u32(&full[s]), ph, flag);
-                    if (two) ok = ok && mbar_wait(smem_u32(&full[s1]), ph1, flag);
-                    if (!__all_sync(0xffffffffu, ok)) { alive = false; break; }
-                    if (lane == 0) {
+                for (int kp = 0; kp < kpairs; kp++) {
+                    if (!mbar_wait(smem_u32(&full[sp]), ph, flag)) { alive = false; break; }
+                    const int nst = 2 * kp + 1 < ksteps ? 2 : 1;
+                    for (int j = 0; j < nst; j++) {
+                        const uint32_t off = (uint32_t)(2 * sp + j) * sstep;
+                        const uint64_t ad = adesc0 + off, bd = bdesc0 + off;
 #pragma unroll
-                        for (int h = 0; h < 2; h++) {
-                            if (h == 1 && !two) break;
-                            const uint32_t a0 = smem_u32(base + (h ? s1 : s) * SB), b0 = a0 + AB;
-#pragma unroll
-                            for (int kk = 0; kk < BK / 16; kk++) {
-                                const uint64_t ad = sw128_desc(a0 + kk * 32), bd = sw128_desc(b0 + kk * 32);
-                                const uint32_t acc = (ks > 0 || h > 0 || kk > 0) ? 1u : 0u;
-                                asm volatile(
-                                    "{\n .reg .pred p;\n setp.ne.b32 p, %4, 0;\n"
-                                    " tcgen05.mma.cta_group::2.kind::f16 [%0], %1, %2, %3, p;\n}\n" ::"r"(d),
-                                    "l"(ad), "l"(bd), "r"(idesc), "r"(acc));
-                            }
+                        for (int kk = 0; kk < BK / 16; kk++) {
+                            const uint32_t acc = (kp > 0 || j > 0 || kk > 0) ? 1u : 0u;
+                            asm volatile(
+                                "{\n .reg .pred p;\n setp.ne.b32 p, %4, 0;\n"
+                                " tcgen05.mma.cta_group::2.kind::f16 [%0], %1, %2, %3, p;\n}\n" ::"r"(d),
+                                "l"(ad + 2 * kk), "l"(bd + 2 * kk), "r"(idesc), "r"(acc));
                         }
-                        commit_pair(smem_u32(&empty[s]));
-                        if (two) commit_pair(smem_u32(&empty[s1]));
                     }
-                    __syncwarp();
-                    if (two) {
-                        s = s1 + 1 == STG ? 0 : s1 + 1;
-                        ph = s1 + 1 == STG ? ph1 ^ 1 : ph1;
-                    } else {
-                        s = s1;
-                        ph = ph1;
-                    }
-                    ks += two ? 2 : 1;
+                    commit_pair(smem_u32(&empty[sp]));
+                    if (++sp == NP) { sp = 0; ph ^= 1; }
                 }
-                if (alive && lane == 0) commit_pair(smem_u32(&acc_full[buf]));
-                __syncwarp();
+                if (alive) commit_pair(smem_u32(&acc_full[buf]));
             }
             // Completion of this commit covers every MMA issued above (in both
             // CTAs' tensor memory); awaited also after a timeout.
-            if (lane == 0) commit_pair(smem_u32(&fin_bar));
-            __syncwarp();
+            commit_pair(smem_u32(&fin_bar));
         }
+        __syncwarp();
         mbar_wait_quiet(smem_u32(&fin_bar), 0);
     } else {
-        // ---- epilogue (both CTAs): this CTA's 128 rows of the tile
-        const int q = warp & 3, et = threadIdx.x - TC4_EPI * 32;
-        float *ebuf = (float *)(base + STG * SB);
+        // ---- epilogue (both CTAs): this CTA's 128 rows of the tile; warp
+        // w reads TMEM lanes 32 (w % 4).. (rows) and column half h of the
+        // tile's BT token columns, 16 columns at a time.
+        const int ew = warp - TC4_EPI, q = warp & 3, h = ew >> 2, et = threadIdx.x - (TC4_EPI + 4 * h) * 32;
+        float *ebuf = (float *)(base + STG * SB) + h * (2 * TC4_ECH * 128);
         const uint32_t ae0 = tc5_mapa(smem_u32(&acc_empty[0]), 0);   // the leader's acc_empty[0]
+        const int c_lo = h * (BT / 2), c_hi = c_lo + BT / 2;
         int li = 0, ch = 0;
         for (int item = pair; item < ntiles; item += npairs, li++) {
             const int buf = li & 1;
             const int row0 = (item % ntm2) * 256 + (int)rank * 128;
             const int64_t n = (int64_t)row0 + 32 * q + lane;
             const int t0 = (item / ntm2) * BT;
-            const bool ok = epi_all(mbar_wait(smem_u32(&acc_full[buf]), (li >> 1) & 1, flag, 128));
+            const bool ok = epi5_all(h, mbar_wait(smem_u32(&acc_full[buf]), (li >> 1) & 1, flag, 128));
             tc_fence_after();
             // (the peer's rows of the last tile may all lie past N: nothing to store)
-            for (int c0 = 0; ok && row0 < N && c0 < BT && t0 + c0 < T; c0 += TC4_ECH, ch++) {
+            for (int c0 = c_lo; ok && row0 < N && c0 < c_hi && t0 + c0 < T; c0 += TC4_ECH, ch++) {
                 uint32_t rr[16];
                 const uint32_t taddr = tmem + ((uint32_t)(32 * q) << 16) + (uint32_t)(buf * BT + c0);
                 asm volatile(
@@ -1521,11 +1543,11 @@ __global__ void __launch_bounds__(TC4_THREADS, 1)
                 if (ytma) {
                     float *sb = ebuf + (ch & 1) * (TC4_ECH * 128);
                     if (et == 0) bulk_wait_read1();
-                    epi_sync();
+                    epi5_sync(h);
 #pragma unroll
                     for (int j = 0; j < 16; j++) sb[j * 128 + 32 * q + lane] = v[j];
                     fence_async_smem();
-                    epi_sync();
+                    epi5_sync(h);
                     if (et == 0) {
                         tma_store_2d(&tmy, smem_u32(sb), row0, t0 + c0);
                         bulk_commit();
@@ -1560,7 +1582,7 @@ int tc5_pick_bt(int64_t mt2, int T, int pairs) {
     double best = 1e30;
     for (int bt = 64; bt <= 256; bt += 32) {
         if (bt > 64 && T <= bt - 32) break;
-        if (tc5_stages(bt) < 3) continue;
+        if (tc5_stages(bt) < 4) continue;   // two stage pairs at least
         const int64_t tiles = mt2 * ((T + bt - 1) / bt);
         const double rounds = (double)((tiles + pairs - 1) / pairs);
         const double mma = 2.0 * bt, smem = 2.0 * tc5_stage_bytes(bt) / 128.0;
@@ -1646,12 +1668,12 @@ int launch_tc5(hd_ctx *ctx, const uint8_t *wb, const uint8_t *xb, int64_t N, int
         ty = tx;
     }
     if (cr != CUDA_SUCCESS) return hd_fail(ctx, HD_E_CUDA, "hd_qgemm: cuTensorMapEncodeTiled failed (%d)", (int)cr);
-    const size_t smem = (size_t)tc5_stages(bt) * tc5_stage_bytes(bt) + TC4_EPI_BYTES + 1024;
+    const size_t smem = (size_t)tc5_stages(bt) * tc5_stage_bytes(bt) + TC5_EPI_BYTES + 1024;
     const int ntm2 = (int)mt2, ntiles = ntm2 * ((T + bt - 1) / bt);
     const int pairs = ntiles < pairs_max ? ntiles : pairs_max;
     cudaError_t e = cudaFuncSetAttribute(k_gemm_tc5, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
     if (e == cudaSuccess)
-        e = hd_launch_cluster(ctx, k_gemm_tc5, dim3(2 * pairs), dim3(TC4_THREADS), smem, 2, tw, tx, ty, Y, T, (int)N, bt,
+        e = hd_launch_cluster(ctx, k_gemm_tc5, dim3(2 * pairs), dim3(TC5_THREADS), smem, 2, tw, tx, ty, Y, T, (int)N, bt,
                               ntm2, ntiles, ksteps, ytma, ctx->flag);
     if (e != cudaSuccess) return hd_fail(ctx, HD_E_CUDA, "hd_qgemm (tcgen05 pair GEMM): %s", cudaGetErrorString(e));
     return HD_OK;
@@ -1687,9 +1709,9 @@ int qgemm_tc4(hd_ctx *ctx, const hd_weight *w, const float *X, float *Y, int T, 
     if (e != cudaSuccess) return hd_fail(ctx, HD_E_CUDA, "hd_qgemm (operand preparation): %s", cudaGetErrorString(e));
     if (!exact) {
         // The pair GEMM where its 256-row tiles fill the SM pairs (measured on
-        // B200, prep + GEMM: 18944 x 3584 Q4_K at T = 512 716 against 616
-        // TFLOP/s, 3584 x 3584 at T = 2048 837 against 798, 4864 x 896 Q5_0
-        // 644 against 637); with fewer tiles (896 x 4864: 44 tiles for 74
+        // B200, prep + GEMM: 18944 x 3584 Q4_K at T = 512 721 against 616
+        // TFLOP/s, 3584 x 3584 at T = 2048 911 against 798, 4864 x 896 Q5_0
+        // 682 against 637); with fewer tiles (896 x 4864: 44 tiles for 74
         // pairs) the one-SM kernel, 466 against 424.  HACEDLE_TC5 = 1 / 0
         // forces it on / off.
         const char *v5 = getenv("HACEDLE_TC5");
