@@ -1712,7 +1712,7 @@ int qgemm_tc4(hd_ctx *ctx, const hd_weight *w, const float *X, float *Y, int T, 
         // B200, prep + GEMM: 18944 x 3584 Q4_K at T = 512 721 against 616
         // TFLOP/s, 3584 x 3584 at T = 2048 911 against 798, 4864 x 896 Q5_0
         // 682 against 637); with fewer tiles (896 x 4864: 44 tiles for 74
-        // pairs) the one-SM kernel, 466 against 424.  HACEDLE_TC5 = 1 / 0
+        // pairs) the one-SM kernel, 466 against 459.  HACEDLE_TC5 = 1 / 0
         // forces it on / off.
         const char *v5 = getenv("HACEDLE_TC5");
         const int64_t tiles2 = ((N + 255) / 256) * ((T + 191) / 192);
