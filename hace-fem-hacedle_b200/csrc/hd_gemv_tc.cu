@@ -176,9 +176,15 @@ __global__ void __launch_bounds__(TV_THREADS, 1) k_qgemv_tc(TvArgs a) {
     URegs<TYPE> reg[TV_ROUNDS];
     float4 xv[TV_XI][2];
 
-    // Activations first (after the dependency wait), then every weight unit
-    // of the thread: the activation loads are then not queued behind the
-    // weight misses.
+    // Every weight unit of the thread before the dependency wait (the
+    // weights are not written by the previous kernel; their loads, pinned in
+    // place, run while it finishes), then the activations after it.
+#pragma unroll
+    for (int i = 0; i < TV_ROUNDS; i++) {
+        const int u = 4 * i + js;
+        if (dq && u < U && row < a.N) load_unit<TYPE>(a.w, row, u0 + u, reg[i]);
+        else zero_unit<TYPE>(reg[i]);
+    }
     pdl_trigger();
     pdl_wait();
 #pragma unroll
@@ -193,12 +199,6 @@ __global__ void __launch_bounds__(TV_THREADS, 1) k_qgemv_tc(TvArgs a) {
                 xv[k][1] = __ldg(p + 1);
             }
         }
-    }
-#pragma unroll
-    for (int i = 0; i < TV_ROUNDS; i++) {
-        const int u = 4 * i + js;
-        if (dq && u < U && row < a.N) load_unit<TYPE>(a.w, row, u0 + u, reg[i]);
-        else zero_unit<TYPE>(reg[i]);
     }
     tc_fence_before();
     __syncthreads();
