@@ -631,14 +631,18 @@ bool small_gemv(const hd_weight *w, int B, int sms, bool pair = false) {
 int big_gemv_kernel(const hd_weight *w, int B, int sms) {
     auto env = [](const char *name) { const char *v = getenv(name); return v && *v ? atoi(v) : -1; };
     const int eb = env("HACEDLE_GEMV_BLK"), em = env("HACEDLE_GEMV_MMA"), es = env("HACEDLE_GEMV_SK");
+    if (env("HACEDLE_GEMV_ST") == 1 && hd_qgemv_stream_fits(w, B, sms)) return 4;
     if (eb == 1 && hd_qgemv_blk_fits(w)) return 3;
     if (em == 1 && hd_qgemv_mma_fits(w)) return 2;
     if (es == 1 && hd_qgemv_sk_fits(w)) return 1;
     const size_t big = (size_t)env_int("HACEDLE_GEMV_BIG_KB", 16384) * 1024;
     const size_t mid = (size_t)env_int("HACEDLE_GEMV_MID_KB", 4096) * 1024;
     const bool blk_ok = eb != 0 && hd_qgemv_blk_fits(w), mma_ok = em != 0 && hd_qgemv_mma_fits(w);
+    if (B >= 3 && env("HACEDLE_GEMV_ST") != 0 && w->type != HD_TYPE_Q6_K && w->gguf_bytes >= big &&
+        hd_qgemv_stream_fits(w, B, sms))
+        return 4;
     if (B == 1) return w->gguf_bytes >= big && blk_ok ? 3 : 0;
-    if (w->type == HD_TYPE_Q8_0 && w->gguf_bytes >= big && blk_ok) return 3;
+    if ((B == 2 || w->type == HD_TYPE_Q8_0) && w->gguf_bytes >= big && blk_ok) return 3;
     if (w->gguf_bytes >= mid && mma_ok && !small_gemv(w, B, sms)) return 2;
     if (w->gguf_bytes >= big && blk_ok) return 3;
     return 0;
@@ -674,6 +678,7 @@ int run_gemv(hd_ctx *ctx, const hd_weight *w, const hd_weight *w_up, const float
     }
     if (!w_up && !nw && !amax && !pinned) {
         const int k = B <= 4 ? big_gemv_kernel(w, B, ctx->sm_count) : 0;
+        if (k == 4) return hd_qgemv_stream(ctx, w, x, y, B, bias, residual, name);
         if (k == 3) return hd_qgemv_blk(ctx, w, x, y, B, bias, residual, name);
         if (k == 2) return hd_qgemv_mma(ctx, w, x, y, B, bias, residual, name);
         if (k == 1) return hd_qgemv_sk(ctx, w, x, y, B, bias, residual, name);

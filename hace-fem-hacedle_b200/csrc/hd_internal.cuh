@@ -139,6 +139,11 @@ bool hd_qgemv_sk_fits(const hd_weight *w);
 bool hd_qgemv_small_fits(const hd_weight *w, int B, int sms, bool pair = false);
 int hd_qgemv_small(hd_ctx *ctx, const hd_weight *w, const hd_weight *w_up, const float *x, float *y, int B,
                    const float *bias, const float *residual, const float *norm_w, float eps, const char *name);
+// Streamed Q-GEMV of a large weight at batch 1..4 on the tensor cores:
+// 128-row blocks walking K in lockstep, a cp.async ring (hd_gemv_stream.cu).
+bool hd_qgemv_stream_fits(const hd_weight *w, int B, int sms);
+int hd_qgemv_stream(hd_ctx *ctx, const hd_weight *w, const float *x, float *y, int B, const float *bias,
+                    const float *residual, const char *name);
 // Q-GEMV at batch 1..4 in 256-row x unit-group blocks (hd_gemv_blk.cu).
 bool hd_qgemv_blk_fits(const hd_weight *w);
 int hd_qgemv_blk(hd_ctx *ctx, const hd_weight *w, const float *x, float *y, int B, const float *bias,

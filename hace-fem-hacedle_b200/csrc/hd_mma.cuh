@@ -23,6 +23,20 @@ template <int N>
 __device__ __forceinline__ void cp_wait() {
     asm volatile("cp.async.wait_group %0;" ::"n"(N) : "memory");
 }
+// cp.async.wait_group with a run-time count (0..8; larger counts wait for all).
+__device__ __forceinline__ void cp_wait_dyn(int n) {
+    switch (n) {
+    case 1: cp_wait<1>(); break;
+    case 2: cp_wait<2>(); break;
+    case 3: cp_wait<3>(); break;
+    case 4: cp_wait<4>(); break;
+    case 5: cp_wait<5>(); break;
+    case 6: cp_wait<6>(); break;
+    case 7: cp_wait<7>(); break;
+    case 8: cp_wait<8>(); break;
+    default: cp_wait<0>(); break;
+    }
+}
 __device__ __forceinline__ void ldsm4(uint32_t addr, uint32_t (&r)[4]) {
     asm volatile("ldmatrix.sync.aligned.m8n8.x4.shared.b16 {%0, %1, %2, %3}, [%4];"
                  : "=r"(r[0]), "=r"(r[1]), "=r"(r[2]), "=r"(r[3])
