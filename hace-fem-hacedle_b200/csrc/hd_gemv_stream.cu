@@ -11,17 +11,20 @@
 //    K in the same order, 8 units (one K-quant super-block) per stage, so
 //    that at any moment the grid reads the same few units of all rows: one
 //    near-contiguous stream through the unit-major layout;
-//  - a stage (a 2-4 KB contiguous run per unit and its side bytes, scales
-//    and super-block headers) arrives by cp.async into a ring of NS stages,
-//    NS - 1 stages ahead of use (the first ones before griddepcontrol.wait);
+//  - a stage (per unit a 2-4 KB contiguous run of quants, its side bytes
+//    and scales, then the super-block headers) arrives by bulk copies that
+//    one copy warp issues into a ring of NS stages, each completing on the
+//    stage's mbarrier; the consumer warps release a stage through a second
+//    mbarrier, so no CTA-wide barrier paces the walk (the first NS stages go
+//    out before griddepcontrol.wait);
 //  - the products run on the tensor cores (mma.sync m16n8k16, exact fp16
 //    quants against x split into fp16 hi/lo, as hd_gemv_small.cu), about
 //    0.07 instructions per weight;
 //  - when the row blocks alone leave SMs idle, the K parts of a block form a
 //    thread-block cluster whose partial sums meet in the first CTA through
 //    distributed shared memory.
-// Warp w takes the 32-row tile w % 4 of the block and units 2 (w / 4),
-// 2 (w / 4) + 1 of every stage; the four quarters meet in shared memory at
+// Consumer warp w takes the 32-row tile w % 4 of the block and units
+// 2 (w / 4), 2 (w / 4) + 1 of every stage; the four quarters meet in shared memory at
 // the end of a block, in a fixed order (as the K parts), so results are
 // bitwise reproducible.
 #include <cstdlib>
@@ -31,8 +34,9 @@
 
 namespace {
 
-constexpr int ST_WARPS = 16;     // 4 tiles of 32 rows x 4 unit quarters of a stage
-constexpr int ST_THREADS = 32 * ST_WARPS;
+constexpr int ST_CWARPS = 16;    // consumers: 4 tiles of 32 rows x 4 unit quarters of a stage
+constexpr int ST_CTHREADS = 32 * ST_CWARPS;
+constexpr int ST_THREADS = ST_CTHREADS + 32;   // and one copy warp
 constexpr int ST_UG = 8;          // units per stage
 constexpr int ST_RB = 128;        // rows per CTA (4 tiles of 32)
 constexpr int ST_SMAX = 8;        // K parts (cluster size), at most
@@ -73,6 +77,7 @@ struct StArgs {
     int NS;                 // stages
     int upc;                // units per K part, at most
     int nblk;               // row blocks
+    int *flag;              // the context's error word (HD_E_TIMEOUT from a wait)
 };
 
 // Shared memory (byte offsets, all multiples of 128):
@@ -80,7 +85,7 @@ struct StArgs {
 //   row sums [4 quarters][4 tiles][NB][32] float; K-part sums [S][NB][128];
 //   per-warp scales [16][2 units][NSC][32] float; NS stages.
 struct StLayout {
-    int img, xs, red, part, scl, stage, total;
+    int img, xs, red, part, scl, bar, stage, total;
 };
 template <int TYPE>
 __host__ __device__ inline StLayout st_layout(int NB, int upc, int S, int NS) {
@@ -90,19 +95,71 @@ __host__ __device__ inline StLayout st_layout(int NB, int upc, int S, int NS) {
     L.red = L.xs + ((upc * NB * 8 + 127) & ~127);
     L.part = L.red + 4 * 4 * NB * 32 * 4;
     L.scl = L.part + ((S > 1 ? S * NB * ST_RB * 4 : 0) + 127) / 128 * 128;
-    L.stage = L.scl + ST_WARPS * 2 * St<TYPE>::NSC * 32 * 4;
+    L.bar = L.scl + ST_CWARPS * 2 * St<TYPE>::NSC * 32 * 4;
+    L.stage = L.bar + 2 * 8 * ST_NSMAX + 96;   // full[NS], empty[NS] (stages stay 128-aligned)
     L.total = L.stage + NS * StL<TYPE>::STAGE;
     return L;
 }
+
+// mbarriers and bulk copies (waits bounded by time: HD_E_TIMEOUT in the
+// context's flag word, and every other waiter gives up once it is set)
+constexpr long long ST_SPIN = 2000000000;   // clock64 cycles (~1 s)
+__device__ __forceinline__ void st_bar_init(uint32_t bar, uint32_t count) {
+    asm volatile("mbarrier.init.shared::cta.b64 [%0], %1;" ::"r"(bar), "r"(count));
+}
+__device__ __forceinline__ void st_arrive(uint32_t bar) {
+    asm volatile("{\n .reg .b64 st;\n mbarrier.arrive.shared::cta.b64 st, [%0];\n}\n" ::"r"(bar) : "memory");
+}
+__device__ __forceinline__ void st_expect(uint32_t bar, uint32_t bytes) {
+    asm volatile("mbarrier.arrive.expect_tx.shared::cta.b64 _, [%0], %1;" ::"r"(bar), "r"(bytes) : "memory");
+}
+__device__ __forceinline__ bool st_try(uint32_t bar, uint32_t parity) {
+    uint32_t ok;
+    asm volatile(
+        "{\n .reg .pred p;\n mbarrier.try_wait.parity.shared::cta.b64 p, [%1], %2;\n selp.u32 %0, 1, 0, p;\n}\n"
+        : "=r"(ok)
+        : "r"(bar), "r"(parity)
+        : "memory");
+    return ok != 0;
+}
+__device__ __forceinline__ bool st_wait(uint32_t bar, uint32_t parity, int *flag, unsigned sleep_ns = 0) {
+    if (st_try(bar, parity)) return true;
+    const long long t0 = clock64();
+    for (unsigned it = 1;; it++) {
+        if (sleep_ns) __nanosleep(sleep_ns);
+        if (st_try(bar, parity)) return true;
+        if ((it & 63) == 0) {
+            if (*(volatile int *)flag) return false;
+            if (clock64() - t0 > ST_SPIN) {
+                atomicExch(flag, HD_E_TIMEOUT);
+                return false;
+            }
+        }
+    }
+}
+__device__ __forceinline__ void st_wait_quiet(uint32_t bar, uint32_t parity) {
+    const long long t0 = clock64();
+    while (!st_try(bar, parity))
+        if (clock64() - t0 > ST_SPIN) return;
+}
+// global -> this CTA's shared memory, completing on an mbarrier of this CTA
+__device__ __forceinline__ void st_bulk(uint32_t dst, const void *src, uint32_t bytes, uint32_t bar) {
+    asm volatile("cp.async.bulk.shared::cluster.global.mbarrier::complete_tx::bytes [%0], [%1], %2, [%3];" ::"r"(dst),
+                 "l"(src), "r"(bytes), "r"(bar)
+                 : "memory");
+}
+// the 512 consumer threads (named barrier 1; the copy warp does not take part)
+__device__ __forceinline__ void st_csync() { asm volatile("bar.sync 1, %0;" ::"n"(ST_CTHREADS) : "memory"); }
 
 template <int TYPE, int NB>
 __global__ void __launch_bounds__(ST_THREADS, 1) k_qgemv_st(StArgs a) {
     using P = St<TYPE>;
     constexpr int USTR = StL<TYPE>::USTR, STAGE = StL<TYPE>::STAGE;
     constexpr int ROWB = P::QB / ST_RB;   // quant bytes per row
+    constexpr int SR = P::SIDE / ST_RB;   // side bytes per row
     extern __shared__ __align__(128) unsigned char st_sm[];
     const int lane = threadIdx.x & 31, wib = threadIdx.x >> 5;
-    const int g = lane >> 2, t = lane & 3, tw = wib & 3, uh = wib >> 2;
+    const int g = lane >> 2, t = lane & 3, tw = wib & 3, uh = (wib >> 2) & 3;
     const int S = a.S, NS = a.NS;
     const int part = S > 1 ? (int)mm_cluster_rank() : 0;
     const int rows = a.N, units = a.units;
@@ -114,9 +171,10 @@ __global__ void __launch_bounds__(ST_THREADS, 1) k_qgemv_st(StArgs a) {
     uint4 *img = (uint4 *)(st_sm + L.img);
     float2 *xs2 = (float2 *)(st_sm + L.xs);
     float *red = (float *)(st_sm + L.red);
-    float *scl = (float *)(st_sm + L.scl) + wib * (2 * P::NSC * 32);
+    float *scl = (float *)(st_sm + L.scl) + (wib & 15) * (2 * P::NSC * 32);
     unsigned char *stg = st_sm + L.stage;
     const uint32_t stg_s = smem_u32(stg);
+    const uint32_t full0 = smem_u32(st_sm + L.bar), empty0 = full0 + 8 * ST_NSMAX;
     const WView w = a.w;
     const int gi_lane = (lane & 7) * 4 + (lane >> 3);
 
@@ -125,51 +183,71 @@ __global__ void __launch_bounds__(ST_THREADS, 1) k_qgemv_st(StArgs a) {
     const int nitems = blk0 < a.nblk ? (a.nblk - blk0 + bstride - 1) / bstride : 0;
     const int nsteps = nitems * ngroups;
 
-    // Copies of step j (item j / ngroups, group j % ngroups) into buffer j % NS.
-    auto issue = [&](int j) {
-        const int it = j / ngroups, gr = j - it * ngroups;
-        const int r0 = (blk0 + it * bstride) * ST_RB;
-        const int u0 = cu0 + gr * ST_UG, nk = min(ST_UG, cu1 - u0);
-        const uint32_t s0 = stg_s + (uint32_t)(j % NS) * STAGE;
-        // units: quants, side bytes, scales, in 16-byte chunks (rows past N
-        // are not copied: their sums are not stored)
-        constexpr int CQ = P::QB / 16, CS = P::SIDE / 16, CD = P::DB / 16, CU = CQ + CS + CD;
-        for (int c = threadIdx.x; c < nk * CU; c += ST_THREADS) {
-            const int k = c / CU, cc = c - k * CU, u = u0 + k;
-            const uint32_t ur = (uint32_t)u * (uint32_t)rows + (uint32_t)r0;
-            const uint32_t dst = s0 + k * USTR;
-            if (cc < CQ) {
-                if (r0 + cc * 16 / ROWB < rows) cp16(dst + cc * 16, w.q + (size_t)ur * ROWB + cc * 16);
-            } else if (cc < CQ + CS) {
-                if constexpr (P::SIDE > 0) {
-                    constexpr int SR = P::SIDE / ST_RB, RPC = 16 / SR;   // side bytes per row, rows per chunk
-                    const int c2 = cc - CQ;
-                    if (r0 + c2 * RPC < rows) cp16(dst + P::QB + c2 * 16, w.aux + (size_t)ur * SR + c2 * 16);
-                }
-            } else {
-                const int c3 = cc - CQ - CS;
-                if (r0 + c3 * 8 < rows) cp16(dst + P::QB + P::SIDE + c3 * 16, w.meta + (size_t)ur * 2 + c3 * 16);
-            }
+    if (threadIdx.x == 0) {
+        for (int i = 0; i < NS; i++) {
+            st_bar_init(full0 + 8 * i, 1);
+            st_bar_init(empty0 + 8 * i, ST_CTHREADS);
         }
-        if constexpr (P::HDR > 0) {   // one super-block per stage
-            const uint32_t sr = (uint32_t)(u0 >> 3) * (uint32_t)rows + (uint32_t)r0;
-            const uint32_t dst = s0 + ST_UG * USTR;
-            for (int c = threadIdx.x; c < (P::HDR + P::DSB) / 16; c += ST_THREADS) {
-                if (c < P::HDR / 16) {
-                    if (r0 + c < rows) cp16(dst + c * 16, w.meta + (size_t)sr * 16 + c * 16);
-                } else {
-                    const int c4 = c - P::HDR / 16;
-                    if (r0 + c4 * 8 < rows) cp16(dst + P::HDR + c4 * 16, (const unsigned char *)w.dsb + (size_t)sr * 2 + c4 * 16);
-                }
-            }
-        }
-    };
-
-    for (int j = 0; j < NS - 1; j++) {
-        if (j < nsteps) issue(j);
-        cp_commit();
+        asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
     }
+    __syncthreads();
     if (S > 1) mm_cluster_arrive_relaxed();   // waited on before the first remote store
+
+    if (wib == ST_CWARPS) {
+        // ---- copy warp: step j into stage j % NS once the consumers have
+        // released the stage's previous use; lane c issues copy c of the step
+        // (per unit the quants, side bytes and scales of the block's rows,
+        // each one contiguous run; then the super-block header and scale).
+        // Weights do not depend on the previous kernel: the first NS stages
+        // go out before the consumers' dependency wait.
+        constexpr int CPU = 1 + (P::SIDE > 0) + (P::DB > 0);
+        bool ok = true;
+        int issued = 0;
+        for (int j = 0; j < nsteps && ok; j++) {
+            const int sidx = j % NS;
+            if (j >= NS) {
+                if (lane == 0) ok = st_wait(empty0 + 8 * sidx, ((j / NS) - 1) & 1, a.flag, 20);
+                ok = __shfl_sync(0xffffffffu, ok, 0);
+                if (!ok) break;
+            }
+            const int it = j / ngroups, gr = j - it * ngroups;
+            const int r0 = (blk0 + it * bstride) * ST_RB, nr = min(ST_RB, rows - r0);
+            const int u0 = cu0 + gr * ST_UG, nk = min(ST_UG, cu1 - u0);
+            const uint32_t s0 = stg_s + (uint32_t)sidx * STAGE, bar = full0 + 8 * sidx;
+            const uint32_t tx = (uint32_t)nr * ((uint32_t)nk * (ROWB + SR + (P::DB > 0 ? 2 : 0)) +
+                                                (P::HDR > 0 ? 16 : 0) + (P::DSB > 0 ? 2 : 0));
+            if (lane == 0) st_expect(bar, tx);
+            __syncwarp();
+            const int ncp = nk * CPU + (P::HDR > 0) + (P::DSB > 0);
+            if (lane < ncp) {
+                if (lane < nk * CPU) {
+                    const int k = lane / CPU, c = lane - k * CPU;
+                    const uint32_t ur = (uint32_t)(u0 + k) * (uint32_t)rows + (uint32_t)r0;
+                    const uint32_t dst = s0 + k * USTR;
+                    if (c == 0) st_bulk(dst, w.q + (size_t)ur * ROWB, nr * ROWB, bar);
+                    else if (P::SIDE > 0 && c == 1) st_bulk(dst + P::QB, w.aux + (size_t)ur * SR, nr * SR, bar);
+                    else st_bulk(dst + P::QB + P::SIDE, w.meta + (size_t)ur * 2, nr * 2, bar);
+                } else {
+                    const uint32_t sr = (uint32_t)(u0 >> 3) * (uint32_t)rows + (uint32_t)r0;
+                    const uint32_t dst = s0 + ST_UG * USTR;
+                    if (lane == nk * CPU && P::HDR > 0) st_bulk(dst, w.meta + (size_t)sr * 16, nr * 16, bar);
+                    else st_bulk(dst + P::HDR, (const unsigned char *)w.dsb + (size_t)sr * 2, nr * 2, bar);
+                }
+            }
+            issued = j + 1;
+        }
+        // the CTA exits only after its copies have landed (also after an error)
+        if (lane == 0)
+            for (int j = issued > NS ? issued - NS : 0; j < issued; j++) st_wait_quiet(full0 + 8 * (j % NS), (j / NS) & 1);
+        __syncwarp();
+        if (S > 1) {   // the cluster barrier counts every thread: the consumers' two phases
+            mm_cluster_wait();
+            mm_cluster_arrive_release();
+            mm_cluster_wait();
+        }
+        return;
+    }
+
     pdl_trigger();
     pdl_wait();
 
@@ -179,11 +257,11 @@ __global__ void __launch_bounds__(ST_THREADS, 1) k_qgemv_st(StArgs a) {
     {
         constexpr int XR = 8;
         const int ntask = nu * NB * 8;
-        for (int base = 0; base < ntask; base += XR * ST_THREADS) {
+        for (int base = 0; base < ntask; base += XR * ST_CTHREADS) {
             float4 v[XR];
 #pragma unroll
             for (int r = 0; r < XR; r++) {
-                const int task = base + r * ST_THREADS + threadIdx.x;
+                const int task = base + r * ST_CTHREADS + threadIdx.x;
                 const int q = task & 7, lb = task >> 3, l = lb / NB, b = lb - l * NB;
                 v[r] = make_float4(0.f, 0.f, 0.f, 0.f);
                 if (task < ntask && b < a.B)
@@ -191,8 +269,8 @@ __global__ void __launch_bounds__(ST_THREADS, 1) k_qgemv_st(StArgs a) {
             }
 #pragma unroll
             for (int r = 0; r < XR; r++) {
-                if (base + r * ST_THREADS >= ntask) break;   // warp-uniform
-                const int task = base + r * ST_THREADS + threadIdx.x;
+                if (base + r * ST_CTHREADS >= ntask) break;   // warp-uniform
+                const int task = base + r * ST_CTHREADS + threadIdx.x;
                 const bool live = task < ntask;
                 const int q = task & 7, lb = task >> 3, l = lb / NB, b = lb - l * NB;
                 const float4 xv4 = v[r];
@@ -227,115 +305,120 @@ __global__ void __launch_bounds__(ST_THREADS, 1) k_qgemv_st(StArgs a) {
             }
         }
     }
+    st_csync();
 
     float *pt = (float *)(st_sm + L.part);
     float acc[4] = {0.f, 0.f, 0.f, 0.f};   // rows g + 8 i of tile tw, batch row t
+    bool ok = true;
     for (int j = 0; j < nsteps; j++) {
-        cp_wait_dyn(NS - 2);
-        __syncthreads();   // step j landed everywhere; every warp is done with step j - 1
-        if (j + NS - 1 < nsteps) issue(j + NS - 1);
-        cp_commit();
+        const int sidx = j % NS;
+        ok = ok && st_wait(full0 + 8 * sidx, (j / NS) & 1, a.flag);
+        __syncwarp();   // this warp's reads of its scale slots of step j - 1 are done
         const int it = j / ngroups, gr = j - it * ngroups;
         const int u0 = cu0 + gr * ST_UG, nk = min(ST_UG, cu1 - u0);
-        const unsigned char *st = stg + (j % NS) * STAGE;
-        const uint32_t st_s = stg_s + (uint32_t)(j % NS) * STAGE;
+        const unsigned char *st = stg + sidx * STAGE;
+        const uint32_t st_s = stg_s + (uint32_t)sidx * STAGE;
         const int row_l = tw * 32 + lane;   // this lane's row in the block (scale decode)
 
-        // scales of this warp's units (lane = row), (g, i) slot order
+        if (ok) {
+            // scales of this warp's units (lane = row), (g, i) slot order
 #pragma unroll
-        for (int k4 = 0; k4 < 2; k4++) {
-            const int k = uh * 2 + k4;
-            if (k < nk) {
-                const int u = u0 + k;
-                const unsigned char *su = st + k * USTR;
-                if constexpr (TYPE == HD_TYPE_Q5_0 || TYPE == HD_TYPE_Q8_0) {
-                    scl[k4 * 32 + gi_lane] = h2f(*(const uint16_t *)(su + P::QB + P::SIDE + row_l * 2));
-                } else if constexpr (TYPE == HD_TYPE_Q4_K) {
-                    const uint4 hd = *(const uint4 *)(st + ST_UG * USTR + row_l * 16);
-                    const float d = h2f((uint16_t)(hd.x & 0xFFFF)), dmin = h2f((uint16_t)(hd.x >> 16));
-                    int sc, m;
-                    q4k_sm_regs(u & 7, hd.y, hd.z, hd.w, sc, m);
-                    scl[(k4 * 2) * 32 + gi_lane] = __fmul_rn(d, (float)sc);
-                    scl[(k4 * 2 + 1) * 32 + gi_lane] = __fmul_rn(dmin, (float)m);
-                } else {
-                    const int8_t *sc = (const int8_t *)(st + ST_UG * USTR + row_l * 16);
-                    const float d = h2f(*(const uint16_t *)(st + ST_UG * USTR + P::HDR + row_l * 2));
-                    const int s0 = 2 * (u & 7);
-                    scl[(k4 * 2) * 32 + gi_lane] = __fmul_rn(d, (float)sc[s0]);
-                    scl[(k4 * 2 + 1) * 32 + gi_lane] = __fmul_rn(d, (float)sc[s0 + 1]);
-                }
-            }
-        }
-        __syncwarp();
-#pragma unroll
-        for (int k4 = 0; k4 < 2; k4++) {
-            const int k = uh * 2 + k4;
-            if (k < nk) {   // warp-uniform
-                const int l = u0 + k - cu0;
-                const uint32_t su_s = st_s + k * USTR;
-                const unsigned char *su = st + k * USTR;
-                uint32_t r[4], r2[4];
-                if constexpr (TYPE == HD_TYPE_Q8_0) {
-                    // rows of 32 bytes: the quant halves are 16 bytes apart
-                    ldsm4(su_s + tw * 1024 + lane * 32, r);
-                    ldsm4(su_s + tw * 1024 + lane * 32 + 16, r2);
-                } else {
-                    ldsm4(su_s + tw * 512 + lane * 16, r);
-                }
-                uint32_t ex[4][2];
-#pragma unroll
-                for (int i = 0; i < 4; i++) ex[i][0] = ex[i][1] = 0;
-                if constexpr (TYPE == HD_TYPE_Q5_0) {
-                    const uint32_t *qh = (const uint32_t *)(su + P::QB) + tw * 32 + g;
-#pragma unroll
-                    for (int i = 0; i < 4; i++) ex[i][0] = qh[8 * i] >> t;
-                } else if constexpr (TYPE == HD_TYPE_Q6_K) {
-                    const uint2 *hb = (const uint2 *)(su + P::QB) + tw * 32 + g;
-#pragma unroll
-                    for (int i = 0; i < 4; i++) {
-                        const uint2 h = hb[8 * i];
-                        ex[i][0] = h.x >> (2 * t);
-                        ex[i][1] = h.y >> (2 * t);
-                    }
-                }
-                const float4 d4 = *(const float4 *)(scl + (k4 * P::NSC) * 32 + g * 4);
-                float4 e4 = make_float4(0.f, 0.f, 0.f, 0.f);
-                if constexpr (P::NSC == 2) e4 = *(const float4 *)(scl + (k4 * 2 + 1) * 32 + g * 4);
-                const float dv[4] = {d4.x, d4.y, d4.z, d4.w}, ev[4] = {e4.x, e4.y, e4.z, e4.w};
-                uint4 bf = make_uint4(0, 0, 0, 0);
-                if (NB >= 4 || g < 2 * NB) bf = img[l * 8 * NB + lane];
-                const float2 ps = t < NB ? xs2[l * NB + t] : make_float2(0.f, 0.f);
-                const float z[4] = {0.f, 0.f, 0.f, 0.f};
-#pragma unroll
-                for (int m = 0; m < 2; m++) {
-                    uint32_t A0[4], A1[4];   // rows g + 16 m, g + 8 + 16 m
-                    unpack_word<TYPE>(r[2 * m], ex[2 * m][0], ex[2 * m][1], A0);
-                    unpack_word<TYPE>(r[2 * m + 1], ex[2 * m + 1][0], ex[2 * m + 1][1], A1);
-                    float e0[4], e1[4];
-                    mma16816(e0, A0[0], A1[0], A0[1], A1[1], bf.x, bf.y, z);
-                    if constexpr (TYPE == HD_TYPE_Q8_0) {
-                        uint32_t B0[4], B1[4];
-                        unpack_word<TYPE>(r2[2 * m], 0, 0, B0);
-                        unpack_word<TYPE>(r2[2 * m + 1], 0, 0, B1);
-                        mma16816(e0, B0[0], B1[0], B0[1], B1[1], bf.z, bf.w, e0);
-                    } else if constexpr (TYPE == HD_TYPE_Q6_K) {
-                        mma16816(e1, A0[2], A1[2], A0[3], A1[3], bf.z, bf.w, z);
+            for (int k4 = 0; k4 < 2; k4++) {
+                const int k = uh * 2 + k4;
+                if (k < nk) {
+                    const int u = u0 + k;
+                    const unsigned char *su = st + k * USTR;
+                    if constexpr (TYPE == HD_TYPE_Q5_0 || TYPE == HD_TYPE_Q8_0) {
+                        scl[k4 * 32 + gi_lane] = h2f(*(const uint16_t *)(su + P::QB + P::SIDE + row_l * 2));
+                    } else if constexpr (TYPE == HD_TYPE_Q4_K) {
+                        const uint4 hd = *(const uint4 *)(st + ST_UG * USTR + row_l * 16);
+                        const float d = h2f((uint16_t)(hd.x & 0xFFFF)), dmin = h2f((uint16_t)(hd.x >> 16));
+                        int sc, m;
+                        q4k_sm_regs(u & 7, hd.y, hd.z, hd.w, sc, m);
+                        scl[(k4 * 2) * 32 + gi_lane] = __fmul_rn(d, (float)sc);
+                        scl[(k4 * 2 + 1) * 32 + gi_lane] = __fmul_rn(dmin, (float)m);
                     } else {
-                        mma16816(e0, A0[2], A1[2], A0[3], A1[3], bf.z, bf.w, e0);
+                        const int8_t *sc = (const int8_t *)(st + ST_UG * USTR + row_l * 16);
+                        const float d = h2f(*(const uint16_t *)(st + ST_UG * USTR + P::HDR + row_l * 2));
+                        const int s0 = 2 * (u & 7);
+                        scl[(k4 * 2) * 32 + gi_lane] = __fmul_rn(d, (float)sc[s0]);
+                        scl[(k4 * 2 + 1) * 32 + gi_lane] = __fmul_rn(d, (float)sc[s0 + 1]);
                     }
+                }
+            }
+            __syncwarp();
 #pragma unroll
-                    for (int h = 0; h < 2; h++) {
-                        const int i = 2 * m + h;
-                        acc[i] = fmaf(dv[i] * ps.x, e0[2 * h] + e0[2 * h + 1], acc[i]);
-                        if constexpr (TYPE == HD_TYPE_Q6_K) acc[i] = fmaf(ev[i] * ps.x, e1[2 * h] + e1[2 * h + 1], acc[i]);
-                        if constexpr (TYPE == HD_TYPE_Q4_K) acc[i] = fmaf(-ev[i], ps.y, acc[i]);
+            for (int k4 = 0; k4 < 2; k4++) {
+                const int k = uh * 2 + k4;
+                if (k < nk) {   // warp-uniform
+                    const int l = u0 + k - cu0;
+                    const uint32_t su_s = st_s + k * USTR;
+                    const unsigned char *su = st + k * USTR;
+                    uint32_t r[4], r2[4];
+                    if constexpr (TYPE == HD_TYPE_Q8_0) {
+                        // rows of 32 bytes: the quant halves are 16 bytes apart
+                        ldsm4(su_s + tw * 1024 + lane * 32, r);
+                        ldsm4(su_s + tw * 1024 + lane * 32 + 16, r2);
+                    } else {
+                        ldsm4(su_s + tw * 512 + lane * 16, r);
+                    }
+                    uint32_t ex[4][2];
+#pragma unroll
+                    for (int i = 0; i < 4; i++) ex[i][0] = ex[i][1] = 0;
+                    if constexpr (TYPE == HD_TYPE_Q5_0) {
+                        const uint32_t *qh = (const uint32_t *)(su + P::QB) + tw * 32 + g;
+#pragma unroll
+                        for (int i = 0; i < 4; i++) ex[i][0] = qh[8 * i] >> t;
+                    } else if constexpr (TYPE == HD_TYPE_Q6_K) {
+                        const uint2 *hb = (const uint2 *)(su + P::QB) + tw * 32 + g;
+#pragma unroll
+                        for (int i = 0; i < 4; i++) {
+                            const uint2 h = hb[8 * i];
+                            ex[i][0] = h.x >> (2 * t);
+                            ex[i][1] = h.y >> (2 * t);
+                        }
+                    }
+                    const float4 d4 = *(const float4 *)(scl + (k4 * P::NSC) * 32 + g * 4);
+                    float4 e4 = make_float4(0.f, 0.f, 0.f, 0.f);
+                    if constexpr (P::NSC == 2) e4 = *(const float4 *)(scl + (k4 * 2 + 1) * 32 + g * 4);
+                    const float dv[4] = {d4.x, d4.y, d4.z, d4.w}, ev[4] = {e4.x, e4.y, e4.z, e4.w};
+                    uint4 bf = make_uint4(0, 0, 0, 0);
+                    if (NB >= 4 || g < 2 * NB) bf = img[l * 8 * NB + lane];
+                    const float2 ps = t < NB ? xs2[l * NB + t] : make_float2(0.f, 0.f);
+                    const float z[4] = {0.f, 0.f, 0.f, 0.f};
+#pragma unroll
+                    for (int m = 0; m < 2; m++) {
+                        uint32_t A0[4], A1[4];   // rows g + 16 m, g + 8 + 16 m
+                        unpack_word<TYPE>(r[2 * m], ex[2 * m][0], ex[2 * m][1], A0);
+                        unpack_word<TYPE>(r[2 * m + 1], ex[2 * m + 1][0], ex[2 * m + 1][1], A1);
+                        float e0[4], e1[4];
+                        mma16816(e0, A0[0], A1[0], A0[1], A1[1], bf.x, bf.y, z);
+                        if constexpr (TYPE == HD_TYPE_Q8_0) {
+                            uint32_t B0[4], B1[4];
+                            unpack_word<TYPE>(r2[2 * m], 0, 0, B0);
+                            unpack_word<TYPE>(r2[2 * m + 1], 0, 0, B1);
+                            mma16816(e0, B0[0], B1[0], B0[1], B1[1], bf.z, bf.w, e0);
+                        } else if constexpr (TYPE == HD_TYPE_Q6_K) {
+                            mma16816(e1, A0[2], A1[2], A0[3], A1[3], bf.z, bf.w, z);
+                        } else {
+                            mma16816(e0, A0[2], A1[2], A0[3], A1[3], bf.z, bf.w, e0);
+                        }
+#pragma unroll
+                        for (int h = 0; h < 2; h++) {
+                            const int i = 2 * m + h;
+                            acc[i] = fmaf(dv[i] * ps.x, e0[2 * h] + e0[2 * h + 1], acc[i]);
+                            if constexpr (TYPE == HD_TYPE_Q6_K)
+                                acc[i] = fmaf(ev[i] * ps.x, e1[2 * h] + e1[2 * h + 1], acc[i]);
+                            if constexpr (TYPE == HD_TYPE_Q4_K) acc[i] = fmaf(-ev[i], ps.y, acc[i]);
+                        }
                     }
                 }
             }
         }
+        st_arrive(empty0 + 8 * sidx);   // this thread's reads of the stage are done
 
         if (gr == ngroups - 1) {
-            // ---- the block is done: its row sums (unit halves added in
+            // ---- the block is done: its row sums (unit quarters added in
             // order), across the K parts of the cluster, then stored
             const int r0 = (blk0 + it * bstride) * ST_RB;
             if (t < NB) {
@@ -344,23 +427,26 @@ __global__ void __launch_bounds__(ST_THREADS, 1) k_qgemv_st(StArgs a) {
             }
 #pragma unroll
             for (int i = 0; i < 4; i++) acc[i] = 0.f;
-            __syncthreads();
+            st_csync();
             const int ntask = ST_RB * a.B;
             if (S == 1) {
-                for (int task = threadIdx.x; task < ntask; task += ST_THREADS) {
-                    const int rr = task & (ST_RB - 1), b = task >> 7, row = r0 + rr;
-                    if (row < rows) {
-                        const int ti = rr >> 5, ri = rr & 31;
-                        float o = (red[((0 * 4 + ti) * NB + b) * 32 + ri] + red[((1 * 4 + ti) * NB + b) * 32 + ri]) +
-                                  (red[((2 * 4 + ti) * NB + b) * 32 + ri] + red[((3 * 4 + ti) * NB + b) * 32 + ri]);
-                        if (a.bias) o = o + a.bias[row];
-                        if (a.residual) o = a.residual[(int64_t)b * rows + row] + o;
-                        a.y[(int64_t)b * rows + row] = o;
+                if (ok) {
+                    for (int task = threadIdx.x; task < ntask; task += ST_CTHREADS) {
+                        const int rr = task & (ST_RB - 1), b = task >> 7, row = r0 + rr;
+                        if (row < rows) {
+                            const int ti = rr >> 5, ri = rr & 31;
+                            float o = (red[((0 * 4 + ti) * NB + b) * 32 + ri] + red[((1 * 4 + ti) * NB + b) * 32 + ri]) +
+                                      (red[((2 * 4 + ti) * NB + b) * 32 + ri] + red[((3 * 4 + ti) * NB + b) * 32 + ri]);
+                            if (a.bias) o = o + a.bias[row];
+                            if (a.residual) o = a.residual[(int64_t)b * rows + row] + o;
+                            a.y[(int64_t)b * rows + row] = o;
+                        }
                     }
                 }
+                if (it + 1 < nitems) st_csync();   // red is rewritten at the next block's end
             } else {
                 mm_cluster_wait();   // every CTA of the cluster runs: its shared memory may be written
-                for (int task = threadIdx.x; task < ntask; task += ST_THREADS) {
+                for (int task = threadIdx.x; task < ntask; task += ST_CTHREADS) {
                     const int rr = task & (ST_RB - 1), b = task >> 7, ti = rr >> 5, ri = rr & 31;
                     const float o = (red[((0 * 4 + ti) * NB + b) * 32 + ri] + red[((1 * 4 + ti) * NB + b) * 32 + ri]) +
                                     (red[((2 * 4 + ti) * NB + b) * 32 + ri] + red[((3 * 4 + ti) * NB + b) * 32 + ri]);
@@ -368,8 +454,8 @@ __global__ void __launch_bounds__(ST_THREADS, 1) k_qgemv_st(StArgs a) {
                 }
                 mm_cluster_arrive_release();
                 mm_cluster_wait();
-                if (part == 0) {
-                    for (int task = threadIdx.x; task < ntask; task += ST_THREADS) {
+                if (part == 0 && ok && !*(volatile int *)a.flag) {
+                    for (int task = threadIdx.x; task < ntask; task += ST_CTHREADS) {
                         const int rr = task & (ST_RB - 1), b = task >> 7, row = r0 + rr;
                         if (row < rows) {
                             float o = pt[b * ST_RB + rr];
@@ -381,10 +467,8 @@ __global__ void __launch_bounds__(ST_THREADS, 1) k_qgemv_st(StArgs a) {
                     }
                 }
             }
-            // (the next step's barrier orders these reads of red before its rewrite)
         }
     }
-    cp_wait_dyn(0);
 }
 
 int st_env(const char *name, int dflt) {
@@ -494,6 +578,8 @@ int launch_st(hd_ctx *ctx, StArgs a, const char *name) {
 bool hd_qgemv_stream_fits(const hd_weight *w, int B, int sms) {
     if (B < 1 || B > 4 || !hd_type_supported(w->type) || w->rows % 8 != 0) return false;
     if ((int64_t)w->units * w->rows >= ((int64_t)1 << 31) / 32) return false;
+    // bulk copies: 16-byte aligned sources
+    if (((uintptr_t)w->q | (uintptr_t)w->aux | (uintptr_t)w->meta | (uintptr_t)w->dsb) & 15) return false;
     const int nb = B <= 1 ? 1 : B <= 2 ? 2 : 4;
     bool ok = false;
     HD_TYPE_SWITCH(w->type, TT, ok = st_plan<TT>((int)w->rows, w->units, nb, sms).ok);
@@ -515,6 +601,7 @@ int hd_qgemv_stream(hd_ctx *ctx, const hd_weight *w, const float *x, float *y, i
     a.K = (int)w->cols;
     a.units = w->units;
     a.S = a.NS = a.upc = a.nblk = 1;
+    a.flag = ctx->flag;
     const int nb = B <= 1 ? 1 : B <= 2 ? 2 : 4;
     int rc = HD_E_TYPE;
     HD_TYPE_SWITCH(w->type, TT, {
