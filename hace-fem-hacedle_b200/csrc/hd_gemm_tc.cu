@@ -935,6 +935,7 @@ EncodeTiledFn encode_tiled() {
 // (f16_split_row).
 constexpr int PREP_RS = 32 * 16 + 16;  // staged row stride in bytes (conflict-free)
 
+constexpr int PREP_XV = 4;   // bf16 mode: groups of 8 activations per thread
 template <int TYPE, int EX>
 __global__ void __launch_bounds__(256) k_prep(WView w, uint16_t *__restrict__ whi, uint16_t *__restrict__ wlo,
                                               int wshift, int nrb, int nw, const float *__restrict__ X, int T,
@@ -998,11 +999,24 @@ __global__ void __launch_bounds__(256) k_prep(WView w, uint16_t *__restrict__ wh
     if constexpr (EX) {
         f16_split_row(X, (int)K, (__half *)xhi, (__half *)xlo, rowshift, xb, red);
     } else {
-        const int64_t i = ((int64_t)xb * 256 + threadIdx.x) * 8;
-        if (i < (int64_t)T * K) {
-            const float4 a = *(const float4 *)(X + i), b = *(const float4 *)(X + i + 4);
-            *(uint4 *)(xhi + i) = make_uint4(pack_bf16(a.x, a.y), pack_bf16(a.z, a.w), pack_bf16(b.x, b.y),
-                                             pack_bf16(b.z, b.w));
+        // PREP_XV groups of 8 values per thread, a block's groups 8 x 256
+        // apart (coalesced), every load issued before the first store
+        const int64_t n8 = (int64_t)T * K / 8;
+        float4 a[PREP_XV], b[PREP_XV];
+#pragma unroll
+        for (int r = 0; r < PREP_XV; r++) {
+            const int64_t gi = ((int64_t)xb * PREP_XV + r) * 256 + threadIdx.x;
+            if (gi < n8) {
+                a[r] = __ldcs((const float4 *)(X + 8 * gi));
+                b[r] = __ldcs((const float4 *)(X + 8 * gi + 4));
+            }
+        }
+#pragma unroll
+        for (int r = 0; r < PREP_XV; r++) {
+            const int64_t gi = ((int64_t)xb * PREP_XV + r) * 256 + threadIdx.x;
+            if (gi < n8)
+                *(uint4 *)(xhi + 8 * gi) = make_uint4(pack_bf16(a[r].x, a[r].y), pack_bf16(a[r].z, a[r].w),
+                                                      pack_bf16(b[r].x, b[r].y), pack_bf16(b[r].z, b[r].w));
         }
     }
 }
@@ -1042,6 +1056,13 @@ __device__ __forceinline__ bool epi_all(bool v) {
 }
 __device__ __forceinline__ void tma_store_2d(const CUtensorMap *tm, uint32_t src, int x, int y) {
     asm volatile("cp.async.bulk.tensor.2d.global.shared::cta.bulk_group [%0, {%2, %3}], [%1];" ::"l"((uint64_t)tm),
+                 "r"(src), "r"(x), "r"(y)
+                 : "memory");
+}
+// The same tile added element-wise to global memory (fp32, in L2).
+__device__ __forceinline__ void tma_add_2d(const CUtensorMap *tm, uint32_t src, int x, int y) {
+    asm volatile("cp.reduce.async.bulk.tensor.2d.global.shared::cta.add.bulk_group [%0, {%2, %3}], [%1];" ::"l"(
+                     (uint64_t)tm),
                  "r"(src), "r"(x), "r"(y)
                  : "memory");
 }
@@ -1386,7 +1407,7 @@ __device__ __forceinline__ void commit_pair(uint32_t bar) {
 __global__ void __launch_bounds__(TC5_THREADS, 1)
     k_gemm_tc5(const __grid_constant__ CUtensorMap tmw, const __grid_constant__ CUtensorMap tmx,
                const __grid_constant__ CUtensorMap tmy, float *__restrict__ Y, int T, int N, int BT, int ntm2,
-               int ntiles, int ksteps, int ytma, int *flag) {
+               int ntiles, int ksteps, int ytma, int ksplit, int *flag) {
     extern __shared__ uint8_t smem_raw[];
     __shared__ __align__(8) uint64_t full[TC5_MAX_STG], empty[TC5_MAX_STG];
     __shared__ __align__(8) uint64_t acc_full[2], acc_empty[2], fin_bar;
@@ -1397,6 +1418,11 @@ __global__ void __launch_bounds__(TC5_THREADS, 1)
     const int pair = blockIdx.x >> 1, npairs = gridDim.x >> 1;
     const int SB = tc5_stage_bytes(BT), STG = tc5_stages(BT) & ~1, NP = STG / 2;   // stage pairs
     const int AB = 128 * BK * 2, HB = BT / 2, kpairs = (ksteps + 1) / 2;
+    // Items: ksplit parts of K (contiguous runs of step pairs) of every tile,
+    // part-major; with ksplit = 2 each part adds its sums into Y (zeroed
+    // before the launch): two addends onto zero give the same bits in either
+    // order.
+    const int nitems = ntiles * ksplit;
     uint8_t *base = (uint8_t *)(((uintptr_t)smem_raw + 1023) & ~(uintptr_t)1023);
 
     if (threadIdx.x == 0) {
@@ -1438,9 +1464,11 @@ __global__ void __launch_bounds__(TC5_THREADS, 1)
             int g = 0, sp = 0, turn = 0;
             uint32_t ph = 0;
             bool alive = true;
-            for (int item = pair; item < ntiles && alive; item += npairs) {
-                const int row0 = (item % ntm2) * 256 + (int)rank * 128, t0 = (item / ntm2) * BT + (int)rank * HB;
-                for (int kp = 0; kp < kpairs; kp++) {
+            for (int item = pair; item < nitems && alive; item += npairs) {
+                const int tile = item % ntiles, part = item / ntiles;
+                const int row0 = (tile % ntm2) * 256 + (int)rank * 128, t0 = (tile / ntm2) * BT + (int)rank * HB;
+                const int kp0 = part * kpairs / ksplit, kp1 = (part + 1) * kpairs / ksplit;
+                for (int kp = kp0; kp < kp1; kp++) {
                     if (turn == warp) {
                         if (!mbar_wait_warp(smem_u32(&empty[sp]), ph ^ 1, flag, 64)) { alive = false; break; }
                         if (lane == 0) {
@@ -1478,12 +1506,13 @@ __global__ void __launch_bounds__(TC5_THREADS, 1)
             int sp = 0, li = 0;
             uint32_t ph = 0;
             bool alive = true;
-            for (int item = pair; item < ntiles && alive; item += npairs, li++) {
-                const int buf = li & 1;
+            for (int item = pair; item < nitems && alive; item += npairs, li++) {
+                const int buf = li & 1, part = item / ntiles;
+                const int kp0 = part * kpairs / ksplit, kp1 = (part + 1) * kpairs / ksplit;
                 if (!mbar_wait(smem_u32(&acc_empty[buf]), ((li >> 1) & 1) ^ 1, flag)) break;
                 tc_fence_after();
                 const uint32_t d = tmem + (uint32_t)(buf * BT);
-                for (int kp = 0; kp < kpairs; kp++) {
+                for (int kp = kp0; kp < kp1; kp++) {
                     if (!mbar_wait(smem_u32(&full[sp]), ph, flag)) { alive = false; break; }
                     const int nst = 2 * kp + 1 < ksteps ? 2 : 1;
                     for (int j = 0; j < nst; j++) {
@@ -1491,7 +1520,7 @@ __global__ void __launch_bounds__(TC5_THREADS, 1)
                         const uint64_t ad = adesc0 + off, bd = bdesc0 + off;
 #pragma unroll
                         for (int kk = 0; kk < BK / 16; kk++) {
-                            const uint32_t acc = (kp > 0 || j > 0 || kk > 0) ? 1u : 0u;
+                            const uint32_t acc = (kp > kp0 || j > 0 || kk > 0) ? 1u : 0u;
                             asm volatile(
                                 "{\n .reg .pred p;\n setp.ne.b32 p, %4, 0;\n"
                                 " tcgen05.mma.cta_group::2.kind::f16 [%0], %1, %2, %3, p;\n}\n" ::"r"(d),
@@ -1518,11 +1547,11 @@ __global__ void __launch_bounds__(TC5_THREADS, 1)
         const uint32_t ae0 = tc5_mapa(smem_u32(&acc_empty[0]), 0);   // the leader's acc_empty[0]
         const int c_lo = h * (BT / 2), c_hi = c_lo + BT / 2;
         int li = 0, ch = 0;
-        for (int item = pair; item < ntiles; item += npairs, li++) {
-            const int buf = li & 1;
-            const int row0 = (item % ntm2) * 256 + (int)rank * 128;
+        for (int item = pair; item < nitems; item += npairs, li++) {
+            const int buf = li & 1, tile = item % ntiles;
+            const int row0 = (tile % ntm2) * 256 + (int)rank * 128;
             const int64_t n = (int64_t)row0 + 32 * q + lane;
-            const int t0 = (item / ntm2) * BT;
+            const int t0 = (tile / ntm2) * BT;
             const bool ok = epi5_all(h, mbar_wait(smem_u32(&acc_full[buf]), (li >> 1) & 1, flag, 128));
             tc_fence_after();
             // (the peer's rows of the last tile may all lie past N: nothing to store)
@@ -1549,7 +1578,10 @@ __global__ void __launch_bounds__(TC5_THREADS, 1)
                     fence_async_smem();
                     epi5_sync(h);
                     if (et == 0) {
-                        tma_store_2d(&tmy, smem_u32(sb), row0, t0 + c0);
+                        if (ksplit > 1)
+                            tma_add_2d(&tmy, smem_u32(sb), row0, t0 + c0);
+                        else
+                            tma_store_2d(&tmy, smem_u32(sb), row0, t0 + c0);
                         bulk_commit();
                     }
                 } else if (n < N) {
@@ -1573,22 +1605,31 @@ __global__ void __launch_bounds__(TC5_THREADS, 1)
     }
 }
 
-// Token tile of the pair GEMM: a multiple of 32 (64..256) minimising rounds
-// of tiles per pair x cycles per K-step (the larger of its MMA time, 2 BT per
-// SM, and the shared-memory traffic of one SM's halves, written once and read
-// once at ~128 B per cycle).
-int tc5_pick_bt(int64_t mt2, int T, int pairs) {
-    int best_bt = 64;
+// Token tile (a multiple of 32, 64..256) and K parts (1 or 2) of the pair
+// GEMM, minimising rounds of items per pair x (K-steps per item x cycles per
+// step + ~1000 cycles of tile turnover); a step costs the larger of its MMA
+// time (2 BT per SM) and the shared-memory traffic of one SM's halves
+// (written once, read once, ~128 B per cycle).  Two K parts add ~3e-3 cycles
+// per output element (Y zeroed, then two additions in L2): worth it when the
+// tiles alone leave pairs idle (896 x 4864 at T = 2048: 44 tiles, 74 pairs).
+int tc5_pick(int64_t mt2, int T, int pairs, int ksteps, int64_t N, bool can_split, int *ks_out) {
+    int best_bt = 64, best_ks = 1;
     double best = 1e30;
-    for (int bt = 64; bt <= 256; bt += 32) {
-        if (bt > 64 && T <= bt - 32) break;
-        if (tc5_stages(bt) < 4) continue;   // two stage pairs at least
-        const int64_t tiles = mt2 * ((T + bt - 1) / bt);
-        const double rounds = (double)((tiles + pairs - 1) / pairs);
-        const double mma = 2.0 * bt, smem = 2.0 * tc5_stage_bytes(bt) / 128.0;
-        const double cost = rounds * ((mma > smem ? mma : smem) + 64.0);
-        if (cost < best - 1e-9) { best = cost; best_bt = bt; }
+    const int kpairs = (ksteps + 1) / 2;
+    for (int ks = 1; ks <= (can_split && kpairs >= 2 ? 2 : 1); ks++) {
+        for (int bt = 64; bt <= 256; bt += 32) {
+            if (bt > 64 && T <= bt - 32) break;
+            if (tc5_stages(bt) < 4) continue;   // two stage pairs at least
+            const int64_t items = mt2 * ((T + bt - 1) / bt) * ks;
+            const double rounds = (double)((items + pairs - 1) / pairs);
+            const double mma = 2.0 * bt, smem = 2.0 * tc5_stage_bytes(bt) / 128.0;
+            const double steps = 2.0 * ((kpairs + ks - 1) / ks);
+            double cost = rounds * (steps * ((mma > smem ? mma : smem) + 64.0) + 1000.0);
+            if (ks > 1) cost += 3e-3 * (double)T * (double)N;
+            if (cost < best - 1e-9) { best = cost; best_bt = bt; best_ks = ks; }
+        }
     }
+    *ks_out = best_ks;
     return best_bt;
 }
 
@@ -1636,10 +1677,16 @@ int tc4_pick_bt(int64_t mt, int T, int sms, int ex) {
 int launch_tc5(hd_ctx *ctx, const uint8_t *wb, const uint8_t *xb, int64_t N, int64_t K, int T, float *Y, int ksteps) {
     const int64_t mt2 = (N + 255) / 256;
     const int pairs_max = ctx->sm_count / 2;
-    int bt = tc5_pick_bt(mt2, T, pairs_max);
+    const bool ytma_ok = N % 4 == 0 && getenv("HACEDLE_TC4_DIRECT_STORE") == nullptr;
+    int ks = 1;
+    int bt = tc5_pick(mt2, T, pairs_max, ksteps, N, ytma_ok, &ks);
     if (const char *env = getenv("HACEDLE_TC_BT")) {
         const int b = atoi(env);
         if (b >= 64 && b <= 256 && b % 32 == 0) bt = b;
+    }
+    if (const char *env = getenv("HACEDLE_TC5_KS")) {   // K parts: 1, or 2 where the output goes by TMA
+        const int k = atoi(env);
+        if (k == 1 || (k == 2 && ytma_ok && ksteps >= 3)) ks = k;
     }
     EncodeTiledFn enc = encode_tiled();
     if (!enc) return hd_fail(ctx, HD_E_CUDA, "hd_qgemm: cuTensorMapEncodeTiled is not available");
@@ -1656,7 +1703,7 @@ int launch_tc5(hd_ctx *ctx, const uint8_t *wb, const uint8_t *xb, int64_t N, int
     CUresult cr = make(&tw, wb, N, 128);
     if (cr == CUDA_SUCCESS) cr = make(&tx, xb, T, bt / 2);
     int ytma = 0;
-    if (cr == CUDA_SUCCESS && N % 4 == 0 && getenv("HACEDLE_TC4_DIRECT_STORE") == nullptr) {
+    if (cr == CUDA_SUCCESS && ytma_ok) {
         cuuint64_t dims[2] = {(cuuint64_t)N, (cuuint64_t)T};
         cuuint64_t strides[1] = {(cuuint64_t)N * 4};
         cuuint32_t box[2] = {128, (cuuint32_t)TC4_ECH};
@@ -1670,11 +1717,13 @@ int launch_tc5(hd_ctx *ctx, const uint8_t *wb, const uint8_t *xb, int64_t N, int
     if (cr != CUDA_SUCCESS) return hd_fail(ctx, HD_E_CUDA, "hd_qgemm: cuTensorMapEncodeTiled failed (%d)", (int)cr);
     const size_t smem = (size_t)tc5_stages(bt) * tc5_stage_bytes(bt) + TC5_EPI_BYTES + 1024;
     const int ntm2 = (int)mt2, ntiles = ntm2 * ((T + bt - 1) / bt);
-    const int pairs = ntiles < pairs_max ? ntiles : pairs_max;
-    cudaError_t e = cudaFuncSetAttribute(k_gemm_tc5, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
+    const int pairs = ntiles * ks < pairs_max ? ntiles * ks : pairs_max;
+    cudaError_t e = cudaSuccess;
+    if (ks > 1) e = cudaMemsetAsync(Y, 0, (size_t)T * (size_t)N * sizeof(float), ctx->stream);
+    if (e == cudaSuccess) e = cudaFuncSetAttribute(k_gemm_tc5, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
     if (e == cudaSuccess)
         e = hd_launch_cluster(ctx, k_gemm_tc5, dim3(2 * pairs), dim3(TC5_THREADS), smem, 2, tw, tx, ty, Y, T, (int)N, bt,
-                              ntm2, ntiles, ksteps, ytma, ctx->flag);
+                              ntm2, ntiles, ksteps, ytma, ks, ctx->flag);
     if (e != cudaSuccess) return hd_fail(ctx, HD_E_CUDA, "hd_qgemm (tcgen05 pair GEMM): %s", cudaGetErrorString(e));
     return HD_OK;
 }
@@ -1695,7 +1744,7 @@ int qgemm_tc4(hd_ctx *ctx, const hd_weight *w, const float *X, float *Y, int T, 
     int *rowshift = exact ? (int *)(xb + 2 * plane) : nullptr;
     const WView v = wview(w);
     const int nrb = (int)((N + 31) / 32), nw = nrb * ((w->units + 7) / 8);
-    const int nx = exact ? T : (int)(((int64_t)T * K / 8 + 255) / 256);
+    const int nx = exact ? T : (int)(((int64_t)T * K / 8 + 256 * PREP_XV - 1) / (256 * PREP_XV));
     cudaError_t e = cudaSuccess;
     HD_TYPE_SWITCH(w->type, TT, {
         if (exact)
@@ -1715,7 +1764,7 @@ int qgemm_tc4(hd_ctx *ctx, const hd_weight *w, const float *X, float *Y, int T, 
         // pairs) the one-SM kernel, 466 against 459.  HACEDLE_TC5 = 1 / 0
         // forces it on / off.
         const char *v5 = getenv("HACEDLE_TC5");
-        const int64_t tiles2 = ((N + 255) / 256) * ((T + 191) / 192);
+        const int64_t tiles2 = ((N + 255) / 256) * ((T + 191) / 192) * (N % 4 == 0 && w->units >= 6 ? 2 : 1);
         const bool pair = v5 && *v5 ? *v5 != '0' : tiles2 >= ctx->sm_count / 2;
         if (pair) return launch_tc5(ctx, wb, xb, N, K, T, Y, (int)((w->units + 1) / 2));
     }

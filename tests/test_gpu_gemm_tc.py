@@ -244,3 +244,39 @@ def test_qgemm_pair_gemm(ctx, monkeypatch, t, N, K, T, bt):
     one_sm = Y1.cpu().numpy()
     assert np.abs(got - one_sm).max() <= 1e-6 * np.abs(ref).max()
     w.free()
+
+
+@pytest.mark.parametrize("t,N,K,T", [(S.GGML_Q5_0, 260, 160, 70), (S.GGML_Q4_K, 896, 4864, 2048),
+                                     (S.GGML_Q6_K, 1000, 768, 300), (S.GGML_Q8_0, 4864, 896, 129),
+                                     (S.GGML_Q4_K, 896, 512, 33)])
+@pytest.mark.parametrize("bt", ["", "64", "256"])
+@pytest.mark.parametrize("forced", [True, False])
+def test_qgemm_pair_gemm_two_k_parts(ctx, monkeypatch, t, N, K, T, bt, forced):
+    """The pair GEMM with K in two parts (HACEDLE_TC5_KS=2, or the cost
+    model's choice where the tiles leave SM pairs idle, as on the 896 x 4864
+    Q4_K weight at T = 2048): Y zeroed, each part's sums added by TMA; any row
+    count, token tails, an odd number of K-step pairs; equal to the oracle
+    within the bf16 contract and reruns bitwise equal (two addends onto zero
+    sum the same in either order)."""
+    import torch
+    monkeypatch.setenv("HACEDLE_TC4_MIN_T", "1")
+    if forced:
+        monkeypatch.setenv("HACEDLE_TC5", "1")
+        monkeypatch.setenv("HACEDLE_TC5_KS", "2")
+    if bt:
+        monkeypatch.setenv("HACEDLE_TC_BT", bt)
+    raw = S.gen_weight(t, N, K, 170 + N)
+    X = S.gen_activations(T, K, 171)
+    w = ctx.weight(t, raw, N, K)
+    Xd = torch.from_numpy(X).cuda()
+    outs = []
+    for _ in range(2):
+        Y = torch.full((T, N), float("nan"), device="cuda")
+        ctx.qgemm(w, Xd, Y, precision=1)
+        ctx.check_device_errors()
+        outs.append(Y.cpu().numpy())
+    ref = X @ O.dequantize(t, raw, N * K).reshape(N, K).T
+    assert np.isfinite(outs[0]).all()
+    assert np.abs(outs[0] - ref).max() / np.abs(ref).max() <= TOL
+    assert np.array_equal(outs[0].view(np.uint32), outs[1].view(np.uint32))
+    w.free()
