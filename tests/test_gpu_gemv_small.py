@@ -26,6 +26,7 @@ def _rel_err(y, ref):
 
 
 def _small(monkeypatch, s="", w=""):
+    monkeypatch.setenv("HACEDLE_GEMV_ST", "0")
     monkeypatch.setenv("HACEDLE_GEMV_BLK", "0")
     monkeypatch.setenv("HACEDLE_GEMV_MMA", "0")
     monkeypatch.setenv("HACEDLE_GEMV_SK", "0")

@@ -31,7 +31,9 @@ def _weight_with_tie(V, K, seed):
 def test_lm_head_argmax_matches_gemv_and_oracle(ctx, monkeypatch, B, norm):
     import torch
     # the plain reference GEMV on the CTA kernel (the one the fused argmax rides
-    # on), not the block, tensor-core or stream-K kernels large weights take
+    # on), not the block, tensor-core, streamed or stream-K kernels large
+    # weights take
+    monkeypatch.setenv("HACEDLE_GEMV_ST", "0")
     monkeypatch.setenv("HACEDLE_GEMV_BLK", "0")
     monkeypatch.setenv("HACEDLE_GEMV_MMA", "0")
     monkeypatch.setenv("HACEDLE_GEMV_SK", "0")
