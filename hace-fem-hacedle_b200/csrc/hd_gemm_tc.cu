@@ -935,7 +935,11 @@ EncodeTiledFn encode_tiled() {
 // (f16_split_row).
 constexpr int PREP_RS = 32 * 16 + 16;  // staged row stride in bytes (conflict-free)
 
-constexpr int PREP_XV = 4;   // bf16 mode: groups of 8 activations per thread
+constexpr int PREP_XV = 4;   // bf16 mode: groups of 8 activations per thread, at most
+// From this many groups on, one group per thread (more blocks in flight);
+// below, PREP_XV (fewer blocks to launch).  Measured on B200, prep + GEMM:
+// Q5_0 4864 x 896 T = 128 / 512 +9 % / +4 % with 4, T = 2048 +2 % with 1.
+constexpr int64_t PREP_XV_BIG = 131072;
 template <int TYPE, int EX>
 __global__ void __launch_bounds__(256) k_prep(WView w, uint16_t *__restrict__ whi, uint16_t *__restrict__ wlo,
                                               int wshift, int nrb, int nw, const float *__restrict__ X, int T,
@@ -999,22 +1003,23 @@ __global__ void __launch_bounds__(256) k_prep(WView w, uint16_t *__restrict__ wh
     if constexpr (EX) {
         f16_split_row(X, (int)K, (__half *)xhi, (__half *)xlo, rowshift, xb, red);
     } else {
-        // PREP_XV groups of 8 values per thread, a block's groups 8 x 256
-        // apart (coalesced), every load issued before the first store
+        // xv (1 or PREP_XV) groups of 8 values per thread, a block's groups
+        // 8 x 256 apart (coalesced), every load issued before the first store
         const int64_t n8 = (int64_t)T * K / 8;
+        const int xv = n8 >= PREP_XV_BIG ? 1 : PREP_XV;
         float4 a[PREP_XV], b[PREP_XV];
 #pragma unroll
         for (int r = 0; r < PREP_XV; r++) {
-            const int64_t gi = ((int64_t)xb * PREP_XV + r) * 256 + threadIdx.x;
-            if (gi < n8) {
+            const int64_t gi = ((int64_t)xb * xv + r) * 256 + threadIdx.x;
+            if (r < xv && gi < n8) {
                 a[r] = __ldcs((const float4 *)(X + 8 * gi));
                 b[r] = __ldcs((const float4 *)(X + 8 * gi + 4));
             }
         }
 #pragma unroll
         for (int r = 0; r < PREP_XV; r++) {
-            const int64_t gi = ((int64_t)xb * PREP_XV + r) * 256 + threadIdx.x;
-            if (gi < n8)
+            const int64_t gi = ((int64_t)xb * xv + r) * 256 + threadIdx.x;
+            if (r < xv && gi < n8)
                 *(uint4 *)(xhi + 8 * gi) = make_uint4(pack_bf16(a[r].x, a[r].y), pack_bf16(a[r].z, a[r].w),
                                                       pack_bf16(b[r].x, b[r].y), pack_bf16(b[r].z, b[r].w));
         }
@@ -1744,7 +1749,9 @@ int qgemm_tc4(hd_ctx *ctx, const hd_weight *w, const float *X, float *Y, int T, 
     int *rowshift = exact ? (int *)(xb + 2 * plane) : nullptr;
     const WView v = wview(w);
     const int nrb = (int)((N + 31) / 32), nw = nrb * ((w->units + 7) / 8);
-    const int nx = exact ? T : (int)(((int64_t)T * K / 8 + 256 * PREP_XV - 1) / (256 * PREP_XV));
+    const int64_t n8 = (int64_t)T * K / 8;
+    const int xv = n8 >= PREP_XV_BIG ? 1 : PREP_XV;
+    const int nx = exact ? T : (int)((n8 + 256 * xv - 1) / (256 * xv));
     cudaError_t e = cudaSuccess;
     HD_TYPE_SWITCH(w->type, TT, {
         if (exact)
@@ -1764,7 +1771,8 @@ int qgemm_tc4(hd_ctx *ctx, const hd_weight *w, const float *X, float *Y, int T, 
         // pairs) the one-SM kernel, 466 against 459.  HACEDLE_TC5 = 1 / 0
         // forces it on / off.
         const char *v5 = getenv("HACEDLE_TC5");
-        const int64_t tiles2 = ((N + 255) / 256) * ((T + 191) / 192) * (N % 4 == 0 && w->units >= 6 ? 2 : 1);
+        // (K in two parts counts double: taken on long K only)
+        const int64_t tiles2 = ((N + 255) / 256) * ((T + 191) / 192) * (N % 4 == 0 && K >= 2048 ? 2 : 1);
         const bool pair = v5 && *v5 ? *v5 != '0' : tiles2 >= ctx->sm_count / 2;
         if (pair) return launch_tc5(ctx, wb, xb, N, K, T, Y, (int)((w->units + 1) / 2));
     }
