@@ -36,12 +36,13 @@ namespace {
 
 constexpr int ST_CWARPS = 16;    // consumers: 4 tiles of 32 rows x 4 unit quarters of a stage
 constexpr int ST_CTHREADS = 32 * ST_CWARPS;
-constexpr int ST_THREADS = ST_CTHREADS + 32;   // and one copy warp
+constexpr int ST_CPW = 4;        // copy warps (one warp's bulk copies are processed one after another)
+constexpr int ST_THREADS = ST_CTHREADS + 32 * ST_CPW;
 constexpr int ST_UG = 8;          // units per stage
 constexpr int ST_RB = 128;        // rows per CTA (4 tiles of 32)
 constexpr int ST_SMAX = 8;        // K parts (cluster size), at most
 constexpr int ST_NSMAX = 10;      // stages, at most
-constexpr int ST_SMEM = 227 * 1024;
+constexpr int ST_SMEM = 226 * 1024;   // dynamic; the copy warps keep a few static bytes
 constexpr int ST_MAX_DEV = 64;
 
 // Per unit of a 128-row block in a stage: quants (rows x 16 bytes; Q8_0 32),
@@ -193,17 +194,26 @@ __global__ void __launch_bounds__(ST_THREADS, 1) k_qgemv_st(StArgs a) {
     __syncthreads();
     if (S > 1) mm_cluster_arrive_relaxed();   // waited on before the first remote store
 
-    if (wib == ST_CWARPS) {
-        // ---- copy warp: step j into stage j % NS once the consumers have
+    if (wib >= ST_CWARPS) {
+        // ---- copy warps: warp c takes steps c, c + ST_CPW, ... (the copies
+        // of one warp are processed one after another, those of different
+        // warps overlap): step j into stage j % NS once the consumers have
         // released the stage's previous use; lane c issues copy c of the step
         // (per unit the quants, side bytes and scales of the block's rows,
         // each one contiguous run; then the super-block header and scale).
         // Weights do not depend on the previous kernel: the first NS stages
         // go out before the consumers' dependency wait.
+        // At most NS copy warps take part: a warp at step j has issued step
+        // j - ncw, after the consumers released step j - ncw - NS, so the
+        // release of step j - 2 NS it waits beyond is done and the parity of
+        // the phase it waits for cannot alias an older one (with more warps
+        // than stages it could).
         constexpr int CPU = 1 + (P::SIDE > 0) + (P::DB > 0);
+        const int cw = wib - ST_CWARPS, ncw = NS < ST_CPW ? NS : ST_CPW;
+        __shared__ int st_issued[ST_CPW];   // per copy warp: one past its last issued step
         bool ok = true;
         int issued = 0;
-        for (int j = 0; j < nsteps && ok; j++) {
+        for (int j = cw; j < nsteps && ok && cw < ncw; j += ncw) {
             const int sidx = j % NS;
             if (j >= NS) {
                 if (lane == 0) ok = st_wait(empty0 + 8 * sidx, ((j / NS) - 1) & 1, a.flag, 20);
@@ -236,9 +246,15 @@ __global__ void __launch_bounds__(ST_THREADS, 1) k_qgemv_st(StArgs a) {
             }
             issued = j + 1;
         }
-        // the CTA exits only after its copies have landed (also after an error)
+        // The CTA exits only after its copies have landed (also after an
+        // error): each warp waits for those of its steps that are the latest
+        // use of their stage (step j + NS not issued; a step is issued iff it
+        // lies below its warp's count).
+        if (lane == 0) st_issued[cw] = issued;
+        asm volatile("bar.sync 2, %0;" ::"n"(32 * ST_CPW) : "memory");
         if (lane == 0)
-            for (int j = issued > NS ? issued - NS : 0; j < issued; j++) st_wait_quiet(full0 + 8 * (j % NS), (j / NS) & 1);
+            for (int j = cw; j < issued; j += ncw)
+                if (j + NS >= st_issued[(j + NS) % ncw]) st_wait_quiet(full0 + 8 * (j % NS), (j / NS) & 1);
         __syncwarp();
         if (S > 1) {   // the cluster barrier counts every thread: the consumers' two phases
             mm_cluster_wait();
