@@ -13,10 +13,10 @@
 //    near-contiguous stream through the unit-major layout;
 //  - a stage (per unit a 2-4 KB contiguous run of quants, its side bytes
 //    and scales, then the super-block headers) arrives by bulk copies that
-//    one copy warp issues into a ring of NS stages, each completing on the
-//    stage's mbarrier; the consumer warps release a stage through a second
-//    mbarrier, so no CTA-wide barrier paces the walk (the first NS stages go
-//    out before griddepcontrol.wait);
+//    the copy warps issue, taking the steps in turn, into a ring of NS
+//    stages, each completing on the stage's mbarrier; the consumer warps
+//    release a stage through a second mbarrier, so no CTA-wide barrier paces
+//    the walk (the first NS stages go out before griddepcontrol.wait);
 //  - the products run on the tensor cores (mma.sync m16n8k16, exact fp16
 //    quants against x split into fp16 hi/lo, as hd_gemv_small.cu), about
 //    0.07 instructions per weight;
