@@ -337,11 +337,15 @@ __global__ void __launch_bounds__(ST_THREADS, 1) k_qgemv_st(StArgs a) {
         const int row_l = tw * 32 + lane;   // this lane's row in the block (scale decode)
 
         if (ok) {
-            // scales of this warp's units (lane = row), (g, i) slot order
+            // scales of this warp's units (lane = row), (g, i) slot order.
+            // A unit past the K part's end (the last stage of a part) is
+            // computed from the stage's stale bytes, which stay in bounds,
+            // with x and the scales zeroed: no branch, so that the two
+            // units' chains interleave.
 #pragma unroll
             for (int k4 = 0; k4 < 2; k4++) {
                 const int k = uh * 2 + k4;
-                if (k < nk) {
+                {
                     const int u = u0 + k;
                     const unsigned char *su = st + k * USTR;
                     if constexpr (TYPE == HD_TYPE_Q5_0 || TYPE == HD_TYPE_Q8_0) {
@@ -366,8 +370,9 @@ __global__ void __launch_bounds__(ST_THREADS, 1) k_qgemv_st(StArgs a) {
 #pragma unroll
             for (int k4 = 0; k4 < 2; k4++) {
                 const int k = uh * 2 + k4;
-                if (k < nk) {   // warp-uniform
-                    const int l = u0 + k - cu0;
+                const bool live = k < nk;
+                {
+                    const int l = live ? u0 + k - cu0 : 0;
                     const uint32_t su_s = st_s + k * USTR;
                     const unsigned char *su = st + k * USTR;
                     uint32_t r[4], r2[4];
@@ -394,13 +399,14 @@ __global__ void __launch_bounds__(ST_THREADS, 1) k_qgemv_st(StArgs a) {
                             ex[i][1] = h.y >> (2 * t);
                         }
                     }
-                    const float4 d4 = *(const float4 *)(scl + (k4 * P::NSC) * 32 + g * 4);
+                    float4 d4 = *(const float4 *)(scl + (k4 * P::NSC) * 32 + g * 4);
                     float4 e4 = make_float4(0.f, 0.f, 0.f, 0.f);
                     if constexpr (P::NSC == 2) e4 = *(const float4 *)(scl + (k4 * 2 + 1) * 32 + g * 4);
+                    if (!live) d4 = e4 = make_float4(0.f, 0.f, 0.f, 0.f);
                     const float dv[4] = {d4.x, d4.y, d4.z, d4.w}, ev[4] = {e4.x, e4.y, e4.z, e4.w};
                     uint4 bf = make_uint4(0, 0, 0, 0);
-                    if (NB >= 4 || g < 2 * NB) bf = img[l * 8 * NB + lane];
-                    const float2 ps = t < NB ? xs2[l * NB + t] : make_float2(0.f, 0.f);
+                    if (live && (NB >= 4 || g < 2 * NB)) bf = img[l * 8 * NB + lane];
+                    const float2 ps = live && t < NB ? xs2[l * NB + t] : make_float2(0.f, 0.f);
                     const float z[4] = {0.f, 0.f, 0.f, 0.f};
 #pragma unroll
                     for (int m = 0; m < 2; m++) {
