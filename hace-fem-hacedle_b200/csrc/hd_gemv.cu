@@ -616,18 +616,20 @@ bool small_gemv(const hd_weight *w, int B, int sms, bool pair = false) {
 // Plain GEMVs (no norm, no SwiGLU pair) at batch <= 4 on large weights take
 // one of four kernels laid out for streaming (measured on B200 in CUDA-graph
 // chains over weight copies larger than L2, fractions of the HBM copy peak):
-//  - batch 1 and 2, weights of HACEDLE_GEMV_BIG_KB kilobytes and more
-//    (default 16 MB): the block kernel (hd_gemv_blk.cu; 7B-shaped
-//    Q5_0/Q4_K/Q6_K at batch 1 0.48/0.38/0.47, Q8_0 LM head 0.69; batch 2
-//    Q6_K 0.32, Q8_0 0.55);
-//  - batch 3..4 on weights of HACEDLE_GEMV_MID_KB and more (default 4 MB),
-//    and Q5_0 / Q4_K at batch 2 on the large ones: the streamed tensor-core
-//    kernel (hd_gemv_stream.cu), whose time does not grow with the batch
-//    (batch 4 Q5_0/Q4_K/Q6_K/Q8_0 0.34/0.29/0.28/0.56 against
-//    0.23/0.20/0.24/0.36 on the others; Q4_K 3584 x 3584 7.6 against 9.1 us;
-//    batch 2 Q5_0 0.36 against 0.33, Q4_K 0.30 against 0.27);
-//  - batch 2 otherwise, weights of HACEDLE_GEMV_MID_KB and more that the
-//    small-matrix kernel does not take: the mma.sync kernel (hd_gemv_mma.cu).
+//  - batch 1, weights of HACEDLE_GEMV_BIG_KB kilobytes and more (default
+//    16 MB): the block kernel (hd_gemv_blk.cu; 7B-shaped Q5_0/Q4_K/Q6_K
+//    0.48/0.38/0.47, Q8_0 LM head 0.69; the streamed kernel below
+//    0.40/0.35/0.35/0.65);
+//  - batch 2..4 on weights of HACEDLE_GEMV_MID_KB and more (default 4 MB),
+//    and batch 1 from there up to HACEDLE_GEMV_BIG_KB: the streamed
+//    tensor-core kernel (hd_gemv_stream.cu), whose time barely grows with
+//    the batch (batch 4 Q5_0/Q4_K/Q6_K/Q8_0 0.38/0.33/0.32/0.68 against
+//    0.23/0.20/0.24/0.36 on the others, batch 2 0.40/0.34/0.33/0.66 against
+//    0.33/0.27/0.32/0.55; Q4_K 3584 x 3584 6.6-6.7 us at batch 1..4 against
+//    7.7-9.1 on the small-matrix kernel);
+//  - otherwise at batch 2..4, weights of HACEDLE_GEMV_MID_KB and more that
+//    the small-matrix kernel does not take: the mma.sync kernel
+//    (hd_gemv_mma.cu).
 // HACEDLE_GEMV_ST / HACEDLE_GEMV_BLK / HACEDLE_GEMV_MMA / HACEDLE_GEMV_SK = 1
 // send every batch <= 4 GEMV that fits to that kernel (in this order of
 // precedence), = 0 turn it off.  Returns 4 (streamed tensor cores), 3
@@ -642,9 +644,8 @@ int big_gemv_kernel(const hd_weight *w, int B, int sms) {
     const size_t big = (size_t)env_int("HACEDLE_GEMV_BIG_KB", 16384) * 1024;
     const size_t mid = (size_t)env_int("HACEDLE_GEMV_MID_KB", 4096) * 1024;
     const bool blk_ok = eb != 0 && hd_qgemv_blk_fits(w), mma_ok = em != 0 && hd_qgemv_mma_fits(w);
-    if (env("HACEDLE_GEMV_ST") != 0 && hd_qgemv_stream_fits(w, B, sms) &&
-        ((B >= 3 && w->gguf_bytes >= mid) ||
-         (B == 2 && (w->type == HD_TYPE_Q4_K || w->type == HD_TYPE_Q5_0) && w->gguf_bytes >= big)))
+    if (env("HACEDLE_GEMV_ST") != 0 && hd_qgemv_stream_fits(w, B, sms) && w->gguf_bytes >= mid &&
+        (B >= 2 || w->gguf_bytes < big))
         return 4;
     if (B == 1) return w->gguf_bytes >= big && blk_ok ? 3 : 0;
     if ((B == 2 || w->type == HD_TYPE_Q8_0) && w->gguf_bytes >= big && blk_ok) return 3;

@@ -213,14 +213,16 @@ __global__ void __launch_bounds__(ST_THREADS, 1) k_qgemv_st(StArgs a) {
         __shared__ int st_issued[ST_CPW];   // per copy warp: one past its last issued step
         bool ok = true;
         int issued = 0;
+        // step j = cw + i ncw as (stage, use of the stage, item, group),
+        // advanced by additions (no division per step)
+        int sidx = cw, use = 0, it = 0, gr = cw;
+        while (gr >= ngroups) { gr -= ngroups; it++; }
         for (int j = cw; j < nsteps && ok && cw < ncw; j += ncw) {
-            const int sidx = j % NS;
             if (j >= NS) {
-                if (lane == 0) ok = st_wait(empty0 + 8 * sidx, ((j / NS) - 1) & 1, a.flag, 20);
+                if (lane == 0) ok = st_wait(empty0 + 8 * sidx, (use - 1) & 1, a.flag, 20);
                 ok = __shfl_sync(0xffffffffu, ok, 0);
                 if (!ok) break;
             }
-            const int it = j / ngroups, gr = j - it * ngroups;
             const int r0 = (blk0 + it * bstride) * ST_RB, nr = min(ST_RB, rows - r0);
             const int u0 = cu0 + gr * ST_UG, nk = min(ST_UG, cu1 - u0);
             const uint32_t s0 = stg_s + (uint32_t)sidx * STAGE, bar = full0 + 8 * sidx;
@@ -245,6 +247,10 @@ __global__ void __launch_bounds__(ST_THREADS, 1) k_qgemv_st(StArgs a) {
                 }
             }
             issued = j + 1;
+            sidx += ncw;
+            if (sidx >= NS) { sidx -= NS; use++; }
+            gr += ncw;
+            while (gr >= ngroups) { gr -= ngroups; it++; }
         }
         // The CTA exits only after its copies have landed (also after an
         // error): each warp waits for those of its steps that are the latest
@@ -326,11 +332,10 @@ __global__ void __launch_bounds__(ST_THREADS, 1) k_qgemv_st(StArgs a) {
     float *pt = (float *)(st_sm + L.part);
     float acc[4] = {0.f, 0.f, 0.f, 0.f};   // rows g + 8 i of tile tw, batch row t
     bool ok = true;
+    int sidx = 0, use = 0, it = 0, gr = 0;   // step j as (stage, use of the stage, item, group)
     for (int j = 0; j < nsteps; j++) {
-        const int sidx = j % NS;
-        ok = ok && st_wait(full0 + 8 * sidx, (j / NS) & 1, a.flag);
+        ok = ok && st_wait(full0 + 8 * sidx, use & 1, a.flag);
         __syncwarp();   // this warp's reads of its scale slots of step j - 1 are done
-        const int it = j / ngroups, gr = j - it * ngroups;
         const int u0 = cu0 + gr * ST_UG, nk = min(ST_UG, cu1 - u0);
         const unsigned char *st = stg + sidx * STAGE;
         const uint32_t st_s = stg_s + (uint32_t)sidx * STAGE;
@@ -490,6 +495,8 @@ __global__ void __launch_bounds__(ST_THREADS, 1) k_qgemv_st(StArgs a) {
                 }
             }
         }
+        if (++sidx == NS) { sidx = 0; use++; }
+        if (++gr == ngroups) { gr = 0; it++; }
     }
 }
 
