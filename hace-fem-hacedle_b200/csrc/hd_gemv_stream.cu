@@ -219,7 +219,7 @@ __global__ void __launch_bounds__(ST_THREADS, 1) k_qgemv_st(StArgs a) {
         while (gr >= ngroups) { gr -= ngroups; it++; }
         for (int j = cw; j < nsteps && ok && cw < ncw; j += ncw) {
             if (j >= NS) {
-                if (lane == 0) ok = st_wait(empty0 + 8 * sidx, (use - 1) & 1, a.flag, 20);
+                if (lane == 0) ok = st_wait(empty0 + 8 * sidx, (use - 1) & 1, a.flag, 200);
                 ok = __shfl_sync(0xffffffffu, ok, 0);
                 if (!ok) break;
             }
