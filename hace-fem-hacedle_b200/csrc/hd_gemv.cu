@@ -654,6 +654,23 @@ int big_gemv_kernel(const hd_weight *w, int B, int sms) {
     return 0;
 }
 
+// Batch 5..16 on the streamed tensor-core kernel (weights of
+// HACEDLE_GEMV_MID_KB and more whose x fragments fit its shared memory)
+// instead of the tcgen05 or register-blocked kernels.  Measured on B200 in
+// CUDA-graph chains, us per launch: batch 8 Q5_0 / Q4_K 18944 x 3584 24.7 /
+// 21.7 against 49.3 / 51.4, Q8_0 151936 x 896 41.3 against 126.3 (batch 16
+// 59.0 against 220.8), Q4_K 3584 x 3584 8.7 against 20.0 (batch 16 12.6
+// against 30.4); on the 3 MB decode-sweep weights the tcgen05 kernel stays
+// (batch 16 7.0-8.5 against 7.9-11.7).  HACEDLE_GEMV_ST = 1 forces it, = 0
+// turns it off.
+bool stream_gemv_b16(const hd_weight *w, int B, int sms) {
+    const char *v = getenv("HACEDLE_GEMV_ST");
+    const int e = v && *v ? atoi(v) : -1;
+    if (e == 0) return false;
+    if (e != 1 && w->gguf_bytes < (size_t)env_int("HACEDLE_GEMV_MID_KB", 4096) * 1024) return false;
+    return hd_qgemv_stream_fits(w, B, sms);
+}
+
 // pinned: the decoder's GEMVs -- the CTA kernel at batch <= 4 and the
 // tcgen05 kernel at 5..16, the kernels its greedy tokens are pinned to (the
 // small-matrix and large-matrix kernels sum in other orders; at a step whose
@@ -695,6 +712,8 @@ int run_gemv(hd_ctx *ctx, const hd_weight *w, const hd_weight *w_up, const float
     // small-matrix kernel too, where it takes them
     if ((w_up || nw) && !amax && !pinned && small_gemv(w, B, ctx->sm_count, w_up != nullptr))
         return hd_qgemv_small(ctx, w, w_up, x, y, B, bias, residual, nw, eps, name);
+    if (!w_up && !nw && !amax && !pinned && B > 4 && stream_gemv_b16(w, B, ctx->sm_count))
+        return hd_qgemv_stream(ctx, w, x, y, B, bias, residual, name);
     if (!w_up && !nw && !amax) {  // batch 5..16 on the tensor cores, where the shape fits
         bool done = false;
         const int rc = hd_qgemv_tc(ctx, w, x, y, B, bias, residual, &done);

@@ -1,4 +1,4 @@
-// hd_gemv_stream.cu -- decode Q-GEMV for large weights at batch 1..4,
+// hd_gemv_stream.cu -- decode Q-GEMV at batch 1..16 on the tensor cores,
 // streamed: y[b] = W x[b] (+bias, +residual), fp32 accumulation.
 //
 // Why.  A 38-150 MB weight is a bandwidth problem, and two things kept the
@@ -83,7 +83,8 @@ struct StArgs {
 
 // Shared memory (byte offsets, all multiples of 128):
 //   x fragments [upc][8 NB] uint4; x scales [upc][NB] float2;
-//   row sums [4 quarters][4 tiles][NB][32] float; K-part sums [S][NB][128];
+//   row sums [4 quarters][4 tiles][NB][32] float; K-part sums [S][NB][128]
+//   (batch 8 and 16: over the stage ring once it is idle);
 //   per-warp scales [16][2 units][NSC][32] float; NS stages.
 struct StLayout {
     int img, xs, red, part, scl, bar, stage, total;
@@ -94,11 +95,17 @@ __host__ __device__ inline StLayout st_layout(int NB, int upc, int S, int NS) {
     L.img = 0;
     L.xs = L.img + upc * 8 * NB * 16;
     L.red = L.xs + ((upc * NB * 8 + 127) & ~127);
-    L.part = L.red + 4 * 4 * NB * 32 * 4;
-    L.scl = L.part + ((S > 1 ? S * NB * ST_RB * 4 : 0) + 127) / 128 * 128;
+    L.part = L.red + 4 * 4 * NB * 32 * 4;   // batch <= 4; above, over the stage ring
+    const int psum = S > 1 ? S * NB * ST_RB * 4 : 0;
+    L.scl = L.part + (NB <= 4 ? (psum + 127) / 128 * 128 : 0);
     L.bar = L.scl + ST_CWARPS * 2 * St<TYPE>::NSC * 32 * 4;
     L.stage = L.bar + 2 * 8 * ST_NSMAX + 96;   // full[NS], empty[NS] (stages stay 128-aligned)
-    L.total = L.stage + NS * StL<TYPE>::STAGE;
+    // Batch 8 and 16: the K-part sums (S > 1: one block per CTA, summed
+    // after every CTA of the cluster has consumed its last stage) reuse the
+    // stage ring.
+    const int ring = NS * StL<TYPE>::STAGE;
+    if (NB > 4) L.part = L.stage;
+    L.total = L.stage + (NB > 4 && psum > ring ? psum : ring);
     return L;
 }
 
@@ -155,6 +162,7 @@ __device__ __forceinline__ void st_csync() { asm volatile("bar.sync 1, %0;" ::"n
 template <int TYPE, int NB>
 __global__ void __launch_bounds__(ST_THREADS, 1) k_qgemv_st(StArgs a) {
     using P = St<TYPE>;
+    constexpr int NBLK = NB <= 4 ? 1 : NB / 4;   // MMA n-blocks of 8 columns (hi, lo of 4 batch rows)
     constexpr int USTR = StL<TYPE>::USTR, STAGE = StL<TYPE>::STAGE;
     constexpr int ROWB = P::QB / ST_RB;   // quant bytes per row
     constexpr int SR = P::SIDE / ST_RB;   // side bytes per row
@@ -192,7 +200,12 @@ __global__ void __launch_bounds__(ST_THREADS, 1) k_qgemv_st(StArgs a) {
         asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
     }
     __syncthreads();
-    if (S > 1) mm_cluster_arrive_relaxed();   // waited on before the first remote store
+    // Cluster barrier, first phase: at batch <= 4 every thread arrives here
+    // and waits before its first remote store (the partner runs); above, the
+    // K-part sums overwrite the first CTA's stage ring, so every thread
+    // arrives only after its CTA has consumed its last stage.
+    constexpr bool LATE = NB > 4;
+    if (S > 1 && !LATE) mm_cluster_arrive_relaxed();
 
     if (wib >= ST_CWARPS) {
         // ---- copy warps: warp c takes steps c, c + ST_CPW, ... (the copies
@@ -263,6 +276,7 @@ __global__ void __launch_bounds__(ST_THREADS, 1) k_qgemv_st(StArgs a) {
                 if (j + NS >= st_issued[(j + NS) % ncw]) st_wait_quiet(full0 + 8 * (j % NS), (j / NS) & 1);
         __syncwarp();
         if (S > 1) {   // the cluster barrier counts every thread: the consumers' two phases
+            if (LATE) mm_cluster_arrive_release();
             mm_cluster_wait();
             mm_cluster_arrive_release();
             mm_cluster_wait();
@@ -330,7 +344,11 @@ __global__ void __launch_bounds__(ST_THREADS, 1) k_qgemv_st(StArgs a) {
     st_csync();
 
     float *pt = (float *)(st_sm + L.part);
-    float acc[4] = {0.f, 0.f, 0.f, 0.f};   // rows g + 8 i of tile tw, batch row t
+    float acc[NBLK][4];   // rows g + 8 i of tile tw, batch row 4 nb + t
+#pragma unroll
+    for (int nb = 0; nb < NBLK; nb++)
+#pragma unroll
+        for (int i = 0; i < 4; i++) acc[nb][i] = 0.f;
     bool ok = true;
     int sidx = 0, use = 0, it = 0, gr = 0;   // step j as (stage, use of the stage, item, group)
     for (int j = 0; j < nsteps; j++) {
@@ -409,34 +427,47 @@ __global__ void __launch_bounds__(ST_THREADS, 1) k_qgemv_st(StArgs a) {
                     if constexpr (P::NSC == 2) e4 = *(const float4 *)(scl + (k4 * 2 + 1) * 32 + g * 4);
                     if (!live) d4 = e4 = make_float4(0.f, 0.f, 0.f, 0.f);
                     const float dv[4] = {d4.x, d4.y, d4.z, d4.w}, ev[4] = {e4.x, e4.y, e4.z, e4.w};
-                    uint4 bf = make_uint4(0, 0, 0, 0);
-                    if (live && (NB >= 4 || g < 2 * NB)) bf = img[l * 8 * NB + lane];
-                    const float2 ps = live && t < NB ? xs2[l * NB + t] : make_float2(0.f, 0.f);
+                    // n-block nb holds batch rows 4 nb .. 4 nb + 3 (hi and lo
+                    // columns); this lane's accumulator column is batch row 4 nb + t
+                    uint4 bf[NBLK];
+                    float2 ps[NBLK];
+#pragma unroll
+                    for (int nb = 0; nb < NBLK; nb++) {
+                        bf[nb] = make_uint4(0, 0, 0, 0);
+                        if (live && (NB >= 4 || g < 2 * NB)) bf[nb] = img[l * 8 * NB + nb * 32 + lane];
+                        ps[nb] = live && 4 * nb + t < NB ? xs2[l * NB + 4 * nb + t] : make_float2(0.f, 0.f);
+                    }
                     const float z[4] = {0.f, 0.f, 0.f, 0.f};
 #pragma unroll
                     for (int m = 0; m < 2; m++) {
                         uint32_t A0[4], A1[4];   // rows g + 16 m, g + 8 + 16 m
                         unpack_word<TYPE>(r[2 * m], ex[2 * m][0], ex[2 * m][1], A0);
                         unpack_word<TYPE>(r[2 * m + 1], ex[2 * m + 1][0], ex[2 * m + 1][1], A1);
-                        float e0[4], e1[4];
-                        mma16816(e0, A0[0], A1[0], A0[1], A1[1], bf.x, bf.y, z);
+                        uint32_t B0[4], B1[4];
                         if constexpr (TYPE == HD_TYPE_Q8_0) {
-                            uint32_t B0[4], B1[4];
                             unpack_word<TYPE>(r2[2 * m], 0, 0, B0);
                             unpack_word<TYPE>(r2[2 * m + 1], 0, 0, B1);
-                            mma16816(e0, B0[0], B1[0], B0[1], B1[1], bf.z, bf.w, e0);
-                        } else if constexpr (TYPE == HD_TYPE_Q6_K) {
-                            mma16816(e1, A0[2], A1[2], A0[3], A1[3], bf.z, bf.w, z);
-                        } else {
-                            mma16816(e0, A0[2], A1[2], A0[3], A1[3], bf.z, bf.w, e0);
                         }
 #pragma unroll
-                        for (int h = 0; h < 2; h++) {
-                            const int i = 2 * m + h;
-                            acc[i] = fmaf(dv[i] * ps.x, e0[2 * h] + e0[2 * h + 1], acc[i]);
-                            if constexpr (TYPE == HD_TYPE_Q6_K)
-                                acc[i] = fmaf(ev[i] * ps.x, e1[2 * h] + e1[2 * h + 1], acc[i]);
-                            if constexpr (TYPE == HD_TYPE_Q4_K) acc[i] = fmaf(-ev[i], ps.y, acc[i]);
+                        for (int nb = 0; nb < NBLK; nb++) {
+                            float e0[4], e1[4];
+                            mma16816(e0, A0[0], A1[0], A0[1], A1[1], bf[nb].x, bf[nb].y, z);
+                            if constexpr (TYPE == HD_TYPE_Q8_0) {
+                                mma16816(e0, B0[0], B1[0], B0[1], B1[1], bf[nb].z, bf[nb].w, e0);
+                            } else if constexpr (TYPE == HD_TYPE_Q6_K) {
+                                mma16816(e1, A0[2], A1[2], A0[3], A1[3], bf[nb].z, bf[nb].w, z);
+                            } else {
+                                mma16816(e0, A0[2], A1[2], A0[3], A1[3], bf[nb].z, bf[nb].w, e0);
+                            }
+#pragma unroll
+                            for (int h = 0; h < 2; h++) {
+                                const int i = 2 * m + h;
+                                float &ac = acc[nb][i];
+                                ac = fmaf(dv[i] * ps[nb].x, e0[2 * h] + e0[2 * h + 1], ac);
+                                if constexpr (TYPE == HD_TYPE_Q6_K)
+                                    ac = fmaf(ev[i] * ps[nb].x, e1[2 * h] + e1[2 * h + 1], ac);
+                                if constexpr (TYPE == HD_TYPE_Q4_K) ac = fmaf(-ev[i], ps[nb].y, ac);
+                            }
                         }
                     }
                 }
@@ -448,12 +479,16 @@ __global__ void __launch_bounds__(ST_THREADS, 1) k_qgemv_st(StArgs a) {
             // ---- the block is done: its row sums (unit quarters added in
             // order), across the K parts of the cluster, then stored
             const int r0 = (blk0 + it * bstride) * ST_RB;
-            if (t < NB) {
 #pragma unroll
-                for (int i = 0; i < 4; i++) red[((uh * 4 + tw) * NB + t) * 32 + g + 8 * i] = acc[i];   // uh: quarter
+            for (int nb = 0; nb < NBLK; nb++) {
+                if (4 * nb + t < NB) {
+#pragma unroll
+                    for (int i = 0; i < 4; i++)   // uh: quarter
+                        red[((uh * 4 + tw) * NB + 4 * nb + t) * 32 + g + 8 * i] = acc[nb][i];
+                }
+#pragma unroll
+                for (int i = 0; i < 4; i++) acc[nb][i] = 0.f;
             }
-#pragma unroll
-            for (int i = 0; i < 4; i++) acc[i] = 0.f;
             st_csync();
             const int ntask = ST_RB * a.B;
             if (S == 1) {
@@ -472,7 +507,10 @@ __global__ void __launch_bounds__(ST_THREADS, 1) k_qgemv_st(StArgs a) {
                 }
                 if (it + 1 < nitems) st_csync();   // red is rewritten at the next block's end
             } else {
-                mm_cluster_wait();   // every CTA of the cluster runs: its shared memory may be written
+                // every CTA of the cluster runs (and, at batch > 4, has
+                // consumed its last stage: the first CTA's ring takes the sums)
+                if (LATE) mm_cluster_arrive_release();
+                mm_cluster_wait();
                 for (int task = threadIdx.x; task < ntask; task += ST_CTHREADS) {
                     const int rr = task & (ST_RB - 1), b = task >> 7, ti = rr >> 5, ri = rr & 31;
                     const float o = (red[((0 * 4 + ti) * NB + b) * 32 + ri] + red[((1 * 4 + ti) * NB + b) * 32 + ri]) +
@@ -605,11 +643,11 @@ int launch_st(hd_ctx *ctx, StArgs a, const char *name) {
 // copies of the side bytes and scales), unit * row offsets in 32 bits, and
 // a plan that fits shared memory.
 bool hd_qgemv_stream_fits(const hd_weight *w, int B, int sms) {
-    if (B < 1 || B > 4 || !hd_type_supported(w->type) || w->rows % 8 != 0) return false;
+    if (B < 1 || B > 16 || !hd_type_supported(w->type) || w->rows % 8 != 0) return false;
     if ((int64_t)w->units * w->rows >= ((int64_t)1 << 31) / 32) return false;
     // bulk copies: 16-byte aligned sources
     if (((uintptr_t)w->q | (uintptr_t)w->aux | (uintptr_t)w->meta | (uintptr_t)w->dsb) & 15) return false;
-    const int nb = B <= 1 ? 1 : B <= 2 ? 2 : 4;
+    const int nb = B <= 1 ? 1 : B <= 2 ? 2 : B <= 4 ? 4 : B <= 8 ? 8 : 16;
     bool ok = false;
     HD_TYPE_SWITCH(w->type, TT, ok = st_plan<TT>((int)w->rows, w->units, nb, sms).ok);
     return ok;
@@ -631,11 +669,14 @@ int hd_qgemv_stream(hd_ctx *ctx, const hd_weight *w, const float *x, float *y, i
     a.units = w->units;
     a.S = a.NS = a.upc = a.nblk = 1;
     a.flag = ctx->flag;
-    const int nb = B <= 1 ? 1 : B <= 2 ? 2 : 4;
+    const int nb = B <= 1 ? 1 : B <= 2 ? 2 : B <= 4 ? 4 : B <= 8 ? 8 : 16;
     int rc = HD_E_TYPE;
     HD_TYPE_SWITCH(w->type, TT, {
-        rc = nb == 1 ? launch_st<TT, 1>(ctx, a, name) : nb == 2 ? launch_st<TT, 2>(ctx, a, name)
-                                                                : launch_st<TT, 4>(ctx, a, name);
+        rc = nb == 1    ? launch_st<TT, 1>(ctx, a, name)
+             : nb == 2  ? launch_st<TT, 2>(ctx, a, name)
+             : nb == 4  ? launch_st<TT, 4>(ctx, a, name)
+             : nb == 8  ? launch_st<TT, 8>(ctx, a, name)
+                        : launch_st<TT, 16>(ctx, a, name);
     });
     return rc;
 }

@@ -139,8 +139,8 @@ bool hd_qgemv_sk_fits(const hd_weight *w);
 bool hd_qgemv_small_fits(const hd_weight *w, int B, int sms, bool pair = false);
 int hd_qgemv_small(hd_ctx *ctx, const hd_weight *w, const hd_weight *w_up, const float *x, float *y, int B,
                    const float *bias, const float *residual, const float *norm_w, float eps, const char *name);
-// Streamed Q-GEMV of a large weight at batch 1..4 on the tensor cores:
-// 128-row blocks walking K in lockstep, a cp.async ring (hd_gemv_stream.cu).
+// Streamed Q-GEMV at batch 1..16 on the tensor cores (hd_gemv_stream.cu):
+// 128-row blocks walking K in lockstep through a ring of bulk-copied stages.
 bool hd_qgemv_stream_fits(const hd_weight *w, int B, int sms);
 int hd_qgemv_stream(hd_ctx *ctx, const hd_weight *w, const float *x, float *y, int B, const float *bias,
                     const float *residual, const char *name);

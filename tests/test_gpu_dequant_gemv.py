@@ -197,6 +197,7 @@ def test_gemv_batched_register_blocked(ctx, monkeypatch, t, N, K, B, bias, resid
     register-blocked CUDA-core kernel (the K split over CTAs, the
     one-CTA-per-tile mode of tall matrices with >= 148 tiles of 128 rows)."""
     torch = _torch()
+    monkeypatch.setenv("HACEDLE_GEMV_ST", "0")   # the streamed kernel has its own tests
     if not tensor_cores:
         monkeypatch.setenv("HACEDLE_GEMV_TC", "0")
     y, ref = _gemv_case(ctx, t, N, K, B, 200 + B, bias=bias, residual=residual)
@@ -224,6 +225,7 @@ def test_gemv_tensor_core_k_parts(ctx, monkeypatch, t, N, K, B, parts):
     three-way bf16 split of x, fp32 scales per group) against the oracle, with
     bias and residual epilogues, and bitwise-equal reruns."""
     torch = _torch()
+    monkeypatch.setenv("HACEDLE_GEMV_ST", "0")   # the streamed kernel has its own tests
     if parts:
         monkeypatch.setenv("HACEDLE_GEMV_TC_S", parts)
     y, ref = _gemv_case(ctx, t, N, K, B, 500 + B, bias=True, residual=(B % 2 == 1))

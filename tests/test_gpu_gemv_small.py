@@ -180,14 +180,16 @@ def test_small_gemv_swiglu_pair(ctx, monkeypatch, t, N, K, B, norm, s):
 
 @pytest.mark.parametrize("t", TYPES)
 @pytest.mark.parametrize("N,K,B", [(128, 256, 1), (2048, 1024, 4), (1000, 768, 3), (4096, 2048, 2), (19000, 512, 1),
-                                   (896, 4864, 4), (3584, 9472, 1)])
+                                   (896, 4864, 4), (3584, 9472, 1), (4864, 1024, 16), (896, 4864, 9), (2048, 1024, 8),
+                                   (1000, 768, 13)])
 @pytest.mark.parametrize("s", ["", "1", "3"])
 def test_streamed_tc_gemv_matches_oracle(ctx, monkeypatch, t, N, K, B, s):
-    """The streamed tensor-core GEMV for large weights (k_qgemv_st,
-    hd_gemv_stream.cu: 128-row blocks walking K in lockstep through a
-    cp.async ring, persistent over blocks when they outnumber the SMs, K
-    parts in a cluster otherwise), forced with HACEDLE_GEMV_ST=1 onto small
-    and ragged shapes, with bias and in-place residual; reruns bitwise equal."""
+    """The streamed tensor-core GEMV (k_qgemv_st, hd_gemv_stream.cu:
+    128-row blocks walking K in lockstep through a ring of bulk-copied
+    stages, persistent over blocks when they outnumber the SMs, K parts in a
+    cluster otherwise; batch 5..16 in two or four MMA column blocks), forced
+    with HACEDLE_GEMV_ST=1 onto small and ragged shapes, with bias and
+    in-place residual; reruns bitwise equal."""
     monkeypatch.setenv("HACEDLE_GEMV_ST", "1")
     monkeypatch.setenv("HACEDLE_ST_S", s)
     outs, ref = _run(ctx, t, N, K, B, 900 + N + K + B + t, bias=True, residual=(B % 2 == 1), reps=2)
