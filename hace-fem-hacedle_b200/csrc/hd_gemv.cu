@@ -661,14 +661,20 @@ int big_gemv_kernel(const hd_weight *w, int B, int sms) {
 // 21.7 against 49.3 / 51.4, Q8_0 151936 x 896 41.3 against 126.3 (batch 16
 // 59.0 against 220.8), Q4_K 3584 x 3584 8.7 against 20.0 (batch 16 12.6
 // against 30.4); on the 3 MB decode-sweep weights the tcgen05 kernel stays
-// (batch 16 7.0-8.5 against 7.9-11.7).  HACEDLE_GEMV_ST = 1 forces it, = 0
-// turns it off.
-bool stream_gemv_b16(const hd_weight *w, int B, int sms) {
+// (batch 16 7.0-8.5 against 7.9-11.7).  Where the x fragments of the whole
+// batch do not fit (long K), the batch goes in chunks of 8 or 4 rows, each
+// launch re-reading the weight: batch 16 Q5_0 18944 x 3584 as 2 x 8, Q6_K
+// 3584 x 18944 as 4 x 4 (~2 x 25 and ~4 x 27 us against 83 and 152).
+// Returns the chunk size (0: not this kernel).  HACEDLE_GEMV_ST = 1 forces
+// it, = 0 turns it off.
+int stream_gemv_b16(const hd_weight *w, int B, int sms) {
     const char *v = getenv("HACEDLE_GEMV_ST");
     const int e = v && *v ? atoi(v) : -1;
-    if (e == 0) return false;
-    if (e != 1 && w->gguf_bytes < (size_t)env_int("HACEDLE_GEMV_MID_KB", 4096) * 1024) return false;
-    return hd_qgemv_stream_fits(w, B, sms);
+    if (e == 0) return 0;
+    if (e != 1 && w->gguf_bytes < (size_t)env_int("HACEDLE_GEMV_MID_KB", 4096) * 1024) return 0;
+    if (hd_qgemv_stream_fits(w, B, sms)) return B;
+    if (B > 8 && hd_qgemv_stream_fits(w, 8, sms)) return 8;
+    return hd_qgemv_stream_fits(w, 4, sms) ? 4 : 0;
 }
 
 // pinned: the decoder's GEMVs -- the CTA kernel at batch <= 4 and the
@@ -712,8 +718,16 @@ int run_gemv(hd_ctx *ctx, const hd_weight *w, const hd_weight *w_up, const float
     // small-matrix kernel too, where it takes them
     if ((w_up || nw) && !amax && !pinned && small_gemv(w, B, ctx->sm_count, w_up != nullptr))
         return hd_qgemv_small(ctx, w, w_up, x, y, B, bias, residual, nw, eps, name);
-    if (!w_up && !nw && !amax && !pinned && B > 4 && stream_gemv_b16(w, B, ctx->sm_count))
-        return hd_qgemv_stream(ctx, w, x, y, B, bias, residual, name);
+    if (!w_up && !nw && !amax && !pinned && B > 4) {
+        // in batch chunks of the largest size whose x fragments fit
+        const int cb = stream_gemv_b16(w, B, ctx->sm_count);
+        for (int b0 = 0; cb && b0 < B; b0 += cb) {
+            const int nb = B - b0 < cb ? B - b0 : cb;
+            const int64_t xo = (int64_t)b0 * w->cols, yo = (int64_t)b0 * w->rows;
+            const int rc = hd_qgemv_stream(ctx, w, x + xo, y + yo, nb, bias, residual ? residual + yo : nullptr, name);
+            if (rc || b0 + nb == B) return rc;
+        }
+    }
     if (!w_up && !nw && !amax) {  // batch 5..16 on the tensor cores, where the shape fits
         bool done = false;
         const int rc = hd_qgemv_tc(ctx, w, x, y, B, bias, residual, &done);

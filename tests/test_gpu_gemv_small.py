@@ -196,3 +196,16 @@ def test_streamed_tc_gemv_matches_oracle(ctx, monkeypatch, t, N, K, B, s):
     assert np.isfinite(outs[0]).all()
     assert _rel_err(outs[0], ref) <= REL_TOL
     assert np.array_equal(outs[0].view(np.uint32), outs[1].view(np.uint32))
+
+
+@pytest.mark.parametrize("t,N,K,B", [(S.GGML_Q5_0, 18944, 3584, 16), (S.GGML_Q6_K, 1024, 18944, 11),
+                                     (S.GGML_Q4_K, 3584, 3584, 16)])
+def test_streamed_tc_gemv_batch_chunks(ctx, t, N, K, B):
+    """Default routing at batch 5..16 on weights of 4 MB and more: the
+    streamed kernel, in chunks of 8 or 4 batch rows where the whole batch's
+    x fragments do not fit its shared memory (long K), with bias and
+    in-place residual; reruns bitwise equal."""
+    outs, ref = _run(ctx, t, N, K, B, 950 + B + t, bias=True, residual=True, reps=2)
+    assert np.isfinite(outs[0]).all()
+    assert _rel_err(outs[0], ref) <= REL_TOL
+    assert np.array_equal(outs[0].view(np.uint32), outs[1].view(np.uint32))
