@@ -291,7 +291,9 @@ def run_ours(args, rank, world, local):
     # (exchange over NVLink included, strong scaling) and the 256-sequence
     # decode (replicas, sequences sharded over the ranks).
     l7 = extra.get("layer7b_sharded", {})
-    dq = extra.get("decode_q05b", {}).get("seqs256", {})
+    # (the 256 sequences run as seqs{256 / ranks} per rank)
+    dq = next((v for k, v in extra.get("decode_q05b", {}).items()
+               if k.startswith("seqs") and k != "seqs1" and isinstance(v, dict)), {})
     if "B1" in l7:
         res["layer7b_B1_gbs"] = l7["B1"].get("gbs")
         res["layer7b_B1_exchange_ms"] = l7["B1"].get("exchange_ms")
