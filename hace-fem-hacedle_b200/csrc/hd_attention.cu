@@ -95,7 +95,12 @@ __global__ void __launch_bounds__(ANT) k_attention(const float *__restrict__ q, 
                                                    float *__restrict__ out) {
     extern __shared__ float sm[];
     constexpr int KP = HD + 1;                      // padded K row
-    constexpr int OPT = (MAXREP * HD + ANT - 1) / ANT;
+    // Register blocking (the same arithmetic per output): a thread takes JB
+    // positions of a head's scores (sharing each q load) and 4 consecutive
+    // dimensions of a head's output (one p load and one float4 of V per
+    // step); rep <= 16 and HD <= 128 keep both within one pass of 512 threads.
+    constexpr int JB = 4, JS = CH / JB, DQ = HD / 4;
+    static_assert(MAXREP * DQ <= ANT && MAXREP * JS <= ANT, "one pass");
     // A chunk's K and V rows: CH * HD / 4 float4 each, NLD per thread per
     // batch.  All loads of a batch are issued before any is stored, so the
     // chunk costs one memory latency per batch rather than one per float4.
@@ -185,9 +190,9 @@ __global__ void __launch_bounds__(ANT) k_attention(const float *__restrict__ q, 
         lrun[tid] = 0.f;
     }
     const int npairs = rep * HD;
-    float o[OPT];
-#pragma unroll
-    for (int k = 0; k < OPT; k++) o[k] = 0.f;
+    const bool oth = tid < rep * DQ;   // this thread's outputs: head tid / DQ, dimensions 4 (tid % DQ) ..
+    const int ph_h = oth ? tid / DQ : 0, pd0 = 4 * (tid % DQ);
+    float o[4] = {0.f, 0.f, 0.f, 0.f};
     const int64_t cbase = (int64_t)cseq * max_ctx;
     const int c1 = min(nchunks, (p + 1) * cpc);
     static_assert(NF4 == NLD, "one load batch per chunk");
@@ -241,13 +246,21 @@ __global__ void __launch_bounds__(ANT) k_attention(const float *__restrict__ q, 
             }
             __syncthreads();
         }
-        for (int i = tid; i < rep * nj; i += ANT) {
-            const int h = i / nj, j = i % nj;
-            const float *qh = qs + h * KP, *kj = Ks + j * KP;
-            float sc = 0.f;
-#pragma unroll 16
-            for (int d = 0; d < HD; d++) sc = fmaf(qh[d], kj[d], sc);
-            S[h * CH + j] = __fdiv_rn(sc, scale);
+        if (tid < rep * JS) {   // positions j0, j0 + JS, ... of head h (rows past nj: computed, not stored)
+            const int h = tid / JS, j0 = tid % JS;
+            const float *qh = qs + h * KP, *kj = Ks + j0 * KP;
+            float sc[JB];
+#pragma unroll
+            for (int r = 0; r < JB; r++) sc[r] = 0.f;
+#pragma unroll 8
+            for (int d = 0; d < HD; d++) {
+                const float qd = qh[d];
+#pragma unroll
+                for (int r = 0; r < JB; r++) sc[r] = fmaf(qd, kj[r * JS * KP + d], sc[r]);
+            }
+#pragma unroll
+            for (int r = 0; r < JB; r++)
+                if (j0 + r * JS < nj) S[h * CH + j0 + r * JS] = __fdiv_rn(sc[r], scale);
         }
         __syncthreads();
         for (int h = warp; h < rep; h += ANT / 32) {
@@ -274,37 +287,39 @@ __global__ void __launch_bounds__(ANT) k_attention(const float *__restrict__ q, 
             }
         }
         __syncthreads();
-#pragma unroll
-        for (int k = 0; k < OPT; k++) {
-            const int i = tid + k * ANT;
-            if (i < npairs) {
-                const int h = i / HD, d = i % HD;
-                const float *ph = S + h * CH;
-                float acc = o[k] * alpha[h];
-                for (int j = 0; j < nj; j++) acc = fmaf(ph[j], Vs[j * HD + d], acc);
-                o[k] = acc;
+        if (oth) {
+            const float *ph = S + ph_h * CH, *vd = Vs + pd0;
+            const float al = alpha[ph_h];
+            float a0 = o[0] * al, a1 = o[1] * al, a2 = o[2] * al, a3 = o[3] * al;
+            for (int j = 0; j < nj; j++) {
+                const float pj = ph[j];
+                const float4 v = *(const float4 *)(vd + j * HD);
+                a0 = fmaf(pj, v.x, a0);
+                a1 = fmaf(pj, v.y, a1);
+                a2 = fmaf(pj, v.z, a2);
+                a3 = fmaf(pj, v.w, a3);
             }
+            o[0] = a0;
+            o[1] = a1;
+            o[2] = a2;
+            o[3] = a3;
         }
     }
     __syncthreads();
     if (Pr == 1) {
+        if (oth) {
 #pragma unroll
-        for (int k = 0; k < OPT; k++) {
-            const int i = tid + k * ANT;
-            if (i < npairs) {
-                const int h = i / HD, d = i % HD;
-                out[((int64_t)r * n_heads + h0 + h) * HD + d] = L > 0 ? o[k] / lrun[h] : 0.f;
-            }
+            for (int c = 0; c < 4; c++)
+                out[((int64_t)r * n_heads + h0 + ph_h) * HD + pd0 + c] = L > 0 ? o[c] / lrun[ph_h] : 0.f;
         }
         return;
     }
     // Split row: publish (max, sum, output) and let the last CTA combine.
     const int W = HD + 2;
     float *part = ws + (((int64_t)r * n_kv + kvh) * P) * rep * W;
+    if (oth) {
 #pragma unroll
-    for (int k = 0; k < OPT; k++) {
-        const int i = tid + k * ANT;
-        if (i < npairs) __stcg(part + (int64_t)p * rep * W + (i / HD) * W + i % HD, o[k]);
+        for (int c = 0; c < 4; c++) __stcg(part + (int64_t)p * rep * W + ph_h * W + pd0 + c, o[c]);
     }
     if (tid < rep) {
         __stcg(part + (int64_t)p * rep * W + tid * W + HD, mrun[tid]);
