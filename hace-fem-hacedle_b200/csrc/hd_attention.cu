@@ -96,10 +96,10 @@ __global__ void __launch_bounds__(ANT) k_attention(const float *__restrict__ q, 
     extern __shared__ float sm[];
     constexpr int KP = HD + 1;                      // padded K row
     // Register blocking (the same arithmetic per output): a thread takes JB
-    // positions of a head's scores (sharing each q load) and 4 consecutive
-    // dimensions of a head's output (one p load and one float4 of V per
+    // positions of a head's scores (sharing each q load) and DV consecutive
+    // dimensions of a head's output (one p load and one vector of V per
     // step); rep <= 16 and HD <= 128 keep both within one pass of 512 threads.
-    constexpr int JB = 4, JS = CH / JB, DQ = HD / 4;
+    constexpr int JB = 2, JS = CH / JB, DV = HD >= 128 ? 4 : 2, DQ = HD / DV;
     static_assert(MAXREP * DQ <= ANT && MAXREP * JS <= ANT, "one pass");
     // A chunk's K and V rows: CH * HD / 4 float4 each, NLD per thread per
     // batch.  All loads of a batch are issued before any is stored, so the
@@ -191,8 +191,10 @@ __global__ void __launch_bounds__(ANT) k_attention(const float *__restrict__ q, 
     }
     const int npairs = rep * HD;
     const bool oth = tid < rep * DQ;   // this thread's outputs: head tid / DQ, dimensions 4 (tid % DQ) ..
-    const int ph_h = oth ? tid / DQ : 0, pd0 = 4 * (tid % DQ);
-    float o[4] = {0.f, 0.f, 0.f, 0.f};
+    const int ph_h = oth ? tid / DQ : 0, pd0 = DV * (tid % DQ);
+    float o[DV];
+#pragma unroll
+    for (int c = 0; c < DV; c++) o[c] = 0.f;
     const int64_t cbase = (int64_t)cseq * max_ctx;
     const int c1 = min(nchunks, (p + 1) * cpc);
     static_assert(NF4 == NLD, "one load batch per chunk");
@@ -290,26 +292,32 @@ __global__ void __launch_bounds__(ANT) k_attention(const float *__restrict__ q, 
         if (oth) {
             const float *ph = S + ph_h * CH, *vd = Vs + pd0;
             const float al = alpha[ph_h];
-            float a0 = o[0] * al, a1 = o[1] * al, a2 = o[2] * al, a3 = o[3] * al;
+            float ac[DV];
+#pragma unroll
+            for (int c = 0; c < DV; c++) ac[c] = o[c] * al;
             for (int j = 0; j < nj; j++) {
                 const float pj = ph[j];
-                const float4 v = *(const float4 *)(vd + j * HD);
-                a0 = fmaf(pj, v.x, a0);
-                a1 = fmaf(pj, v.y, a1);
-                a2 = fmaf(pj, v.z, a2);
-                a3 = fmaf(pj, v.w, a3);
+                if constexpr (DV == 4) {
+                    const float4 v = *(const float4 *)(vd + j * HD);
+                    ac[0] = fmaf(pj, v.x, ac[0]);
+                    ac[1] = fmaf(pj, v.y, ac[1]);
+                    ac[2] = fmaf(pj, v.z, ac[2]);
+                    ac[3] = fmaf(pj, v.w, ac[3]);
+                } else {
+                    const float2 v = *(const float2 *)(vd + j * HD);
+                    ac[0] = fmaf(pj, v.x, ac[0]);
+                    ac[1] = fmaf(pj, v.y, ac[1]);
+                }
             }
-            o[0] = a0;
-            o[1] = a1;
-            o[2] = a2;
-            o[3] = a3;
+#pragma unroll
+            for (int c = 0; c < DV; c++) o[c] = ac[c];
         }
     }
     __syncthreads();
     if (Pr == 1) {
         if (oth) {
 #pragma unroll
-            for (int c = 0; c < 4; c++)
+            for (int c = 0; c < DV; c++)
                 out[((int64_t)r * n_heads + h0 + ph_h) * HD + pd0 + c] = L > 0 ? o[c] / lrun[ph_h] : 0.f;
         }
         return;
@@ -319,7 +327,7 @@ __global__ void __launch_bounds__(ANT) k_attention(const float *__restrict__ q, 
     float *part = ws + (((int64_t)r * n_kv + kvh) * P) * rep * W;
     if (oth) {
 #pragma unroll
-        for (int c = 0; c < 4; c++) __stcg(part + (int64_t)p * rep * W + ph_h * W + pd0 + c, o[c]);
+        for (int c = 0; c < DV; c++) __stcg(part + (int64_t)p * rep * W + ph_h * W + pd0 + c, o[c]);
     }
     if (tid < rep) {
         __stcg(part + (int64_t)p * rep * W + tid * W + HD, mrun[tid]);
