@@ -86,7 +86,7 @@ constexpr int MAXREP = 16;
 // earlier), and lens / slots likewise; the new position's row is replaced
 // from shared memory as usual.
 template <int HD, bool EARLY>
-__global__ void __launch_bounds__(ANT) k_attention(const float *__restrict__ q, int64_t qld, const float *__restrict__ kc,
+__global__ void __launch_bounds__(ANT, (EARLY || HD == 128) ? 1 : 2) k_attention(const float *__restrict__ q, int64_t qld, const float *__restrict__ kc,
                                                    const float *__restrict__ vc, const int32_t *__restrict__ lens,
                                                    int pos0, int seqT, int n_heads, int n_kv, int max_ctx,
                                                    float scale, int P, int cpc, float *ws, int *tickets,
