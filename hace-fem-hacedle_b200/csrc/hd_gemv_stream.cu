@@ -18,8 +18,10 @@
 //    release a stage through a second mbarrier, so no CTA-wide barrier paces
 //    the walk (the first NS stages go out before griddepcontrol.wait);
 //  - the products run on the tensor cores (mma.sync m16n8k16, exact fp16
-//    quants against x split into fp16 hi/lo, as hd_gemv_small.cu), about
-//    0.07 instructions per weight;
+//    quants against x split into fp16 hi/lo, as hd_gemv_small.cu; batch
+//    5..16 in two or four MMA column blocks sharing each unpacked
+//    fragment); the unpacking, not the MMAs, sets the consumers' pace
+//    (~185 warp instructions per 32-row unit at batch 1);
 //  - when the row blocks alone leave SMs idle, the K parts of a block form a
 //    thread-block cluster whose partial sums meet in the first CTA through
 //    distributed shared memory.
